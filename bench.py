@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Benchmark of the jax-rs B200 backend's hot path.
+
+Default workload (the headline): f32 GEMM M=N=K=8192 through the C ABI
+(jx_gemm_f32, tcgen05 3xTF32), one GEMM per step.  With --gpus N each rank
+computes its own 8192-row shard of a (8192*N) x 8192 x 8192 product with a
+replica of B (M-row sharding, no collective), so per-GPU work is fixed: weak
+scaling.  Other workloads: --workload chain | rowsum | argmax | fullsum.
+
+Timing: W warm-up steps, then exactly K steps between barrier +
+torch.cuda.synchronize(), CUDA events on the launching stream, max over
+ranks.  Operands are 256 MiB each (larger than the 126 MB L2).
+
+`--impl reference` times the reference's CPU implementation of the same
+workload (the oracle's C restatement of jax-rs's CPU loop, all host threads,
+a bounded row sample per step) and prints the same JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "f32 GEMM TFLOP/s + MLP train samples/s at 1/2/4/8 B200; fused-elt HBM GB/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="sgemm", choices=["sgemm", "chain", "rowsum", "argmax", "fullsum"])
+    p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-rows", type=int, default=48, help="GEMM rows timed by the CPU baseline")
+    return p.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+class Dist:
+    def __init__(self, n):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v):
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU reference (oracle) timing -- the only place bench.py runs oracle code
+# ---------------------------------------------------------------------------
+def cpu_sgemm(size, rows, threads, reps=1):
+    import oracle as O
+    O.build()
+    rng = np.random.default_rng(1)
+    a = rng.uniform(-1, 1, (rows, size)).astype(np.float32)
+    b = rng.uniform(-1, 1, (size, size)).astype(np.float32)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.matmul(a, b, nthreads=threads)
+    dt = (time.perf_counter() - t0) / reps
+    return 2.0 * rows * size * size / dt / 1e12, dt
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_sgemm(args, dist, jx, torch):
+    M = N = K = args.size
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(1 + dist.rank)
+    A = torch.empty((M, K), device=dev).uniform_(-1, 1, generator=g)   # this rank's row shard
+    g.manual_seed(1)
+    B = torch.empty((K, N), device=dev).uniform_(-1, 1, generator=g)   # replicated
+    Cm = torch.empty((M, N), device=dev)
+    Kp = jx.gemm_kpad(K)
+    Ah, Al = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
+    Bh, Bl = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
+
+    def step():
+        jx.gemm(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, stream=s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = clk.stop()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms_max = dist.max(ms)
+    flops_rank = 2.0 * M * N * K
+    value = flops_rank * dist.world / (ms_max * 1e-3) / 1e12
+
+    # dominant kernel alone: the tcgen05 main loop on pre-split operands
+    jx.gemm_split(A.data_ptr(), Ah.data_ptr(), Al.data_ptr(), M, K, stream=s)
+    jx.gemm_split(B.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), N, K, ld=N, trans=True, stream=s)
+    for _ in range(3):
+        jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp, stream=s)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp, stream=s)
+    e1.record(st)
+    torch.cuda.synchronize()
+    kern_ms = e0.elapsed_time(e1) / args.steps
+    del Ah, Al, Bh, Bl
+
+    # e2e: host buffers through the C ABI, h2d of A and B, GEMM, d2h of C per step
+    hA = torch.empty((M, K), dtype=torch.float32).pin_memory()
+    hB = torch.empty((K, N), dtype=torch.float32).pin_memory()
+    hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    hA.copy_(A.cpu())
+    hB.copy_(B.cpu())
+    nbA, nbB, nbC = hA.numel() * 4, hB.numel() * 4, hC.numel() * 4
+
+    def e2e_step():
+        jx.call("jx_memcpy_h2d", A.data_ptr(), hA.data_ptr(), nbA, s)
+        jx.call("jx_memcpy_h2d", B.data_ptr(), hB.data_ptr(), nbB, s)
+        step()
+        jx.call("jx_memcpy_d2h", hC.data_ptr(), Cm.data_ptr(), nbC, s)
+
+    e2e_step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(e0.elapsed_time(e1) / args.e2e_steps)
+    e2e_val = flops_rank * dist.world / (e2e_ms * 1e-3) / 1e12
+
+    hbm, bf16, basis = load_peaks()
+    peak = bf16 / 2.0 / 3.0  # tf32 issues at half the bf16 rate; 3xTF32 needs 3 MMAs per f32 product
+    achieved = flops_rank / (kern_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic U(-1,1) operands (torch generator, seed 1)",
+        "config": {"workload": f"sgemm {M}x{N}x{K} f32 per rank (M-row shard of a {M * dist.world}x{N}x{K} "
+                               f"product, B replicated), JX_PREC_3XTF32",
+                   "global_batch": None, "seq_len": None, "parallelism": f"M-row shards x{dist.world}, no collective",
+                   "l2": "operands 256 MiB each > 126 MB L2; no flush needed"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
+                     "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
+                     "traffic": None, "kernel_ms": round(kern_ms, 4)},
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
+                "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+    return line
+
+
+def run_chain(args, dist, jx, torch):
+    n = 1 << 28
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(2 + dist.rank)
+    X = torch.randn(n, device=dev, generator=g)
+    Y = torch.empty_like(X)
+    U, B = jx.OP_UNARY, jx.OP_BINARY
+    code = [(jx.OP_CONST, 1, 0, 0), (jx.OP_CONST, 2, 1, 0), (jx.OP_CONST, 3, 2, 0),
+            (B + jx.BIN["mul"], 4, 0, 1), (B + jx.BIN["add"], 4, 4, 2), (U + jx.UN["gelu"], 4, 4, 0),
+            (U + jx.UN["sigmoid"], 5, 0, 0), (B + jx.BIN["mul"], 4, 4, 5), (U + jx.UN["tanh"], 5, 0, 0),
+            (B + jx.BIN["div"], 5, 5, 3), (B + jx.BIN["sub"], 4, 4, 5), (jx.OP_STORE, 0, 4, 0)]
+    tape = jx.Tape(code, [1.1, 0.9, 2.0], 1, 1)
+
+    def step():
+        tape.run([X.data_ptr()], [Y.data_ptr()], n, s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    bytes_step = 8.0 * n
+    gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
+    hbm, _, basis = load_peaks()
+    return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+            "config": {"workload": "jit tape y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2 over 2^28 f32 per rank",
+                       "l2": "1 GiB in + 1 GiB out > L2"},
+            "roofline": {"bound": "hbm", "kernel": "tape_kernel", "achieved": round(gbs / dist.world, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
+                         "peak_basis": basis, "traffic": None},
+            "gpu_launches": args.steps, "clocks": clocks}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    dist = Dist(args.gpus)
+    torch.cuda.set_device(dist.local)
+    jx = importlib.import_module("jax-rs_b200")
+    jx.init(dist.local)
+    if args.workload == "sgemm":
+        line = run_sgemm(args, dist, jx, torch)
+    elif args.workload == "chain":
+        line = run_chain(args, dist, jx, torch)
+    else:
+        raise SystemExit(f"workload {args.workload} not wired into bench.py yet")
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":
+        tflops, dt = cpu_sgemm(args.size, args.cpu_rows, 1)
+        line["cpu_baseline"] = {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                "sample": f"{args.cpu_rows} rows of the {args.size}^3 product "
+                                          f"({dt:.1f} s, jax-rs CPU loop order, 1 thread like the reference)"}
+    dist.close()
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def reference_arm(args):
+    """The reference's CPU implementation of the same workload (oracle restatement)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rows = max(8, args.cpu_rows)
+    if args.workload != "sgemm":
+        print(json.dumps({"impl": "reference", "unavailable": f"reference arm wired for sgemm only"}))
+        return
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_sgemm(args.size, min(rows, 8), threads)
+    steps = max(1, min(args.steps, 3))
+    vals, dts = [], []
+    for _ in range(steps):
+        v, dt = cpu_sgemm(args.size, rows, threads)
+        vals.append(v)
+        dts.append(dt)
+    value = statistics.median(vals)
+    sample = (f"{rows} rows of the {args.size}^3 product per step (jax-rs CPU loop order, "
+              f"row-parallel over {threads} host threads)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(dts) * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic U(-1,1)",
+        "config": {"workload": f"sgemm {args.size}x{args.size}x{args.size} f32 (row sample)"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

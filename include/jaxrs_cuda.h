@@ -1,0 +1,235 @@
+/*
+ * jaxrs_cuda.h -- C ABI of the jax-rs B200 (sm_100a) compute backend.
+ *
+ * This is the FFI surface a `Device::Cuda(n)` arm of jax-rs binds.  Each entry
+ * point names the reference interface it replaces (paths relative to the
+ * jax-rs 0.5.1 source tree).  Conventions, mirroring the reference's
+ * `gpu_*` launchers (src/backend/ops.rs):
+ *   - outputs are pre-allocated by the caller, as `gpu_*` takes `&Buffer` outputs;
+ *   - pointers are device pointers unless a parameter says "host";
+ *   - all work is enqueued on `stream` (NULL = the legacy default stream) and
+ *     nothing blocks except jx_memcpy_d2h / jx_stream_sync, the equivalent of
+ *     the reference's blocking readback (src/buffer.rs:711-749);
+ *   - every function returns JX_OK (0) or a JX_E* status; jx_last_error()
+ *     returns the message of the calling thread's last failure.  The reference
+ *     panics on the same conditions (e.g. src/backend/ops.rs:30-36); a Rust
+ *     shim turns a non-zero status into that panic.
+ */
+#ifndef JAXRS_CUDA_H
+#define JAXRS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define JX_OK 0
+#define JX_EINVAL 1      /* bad argument (the reference's assert!/panic!) */
+#define JX_ENOMEM 2      /* device allocation failed */
+#define JX_ECUDA 3       /* CUDA runtime/driver error */
+#define JX_ENCCL 4       /* NCCL error */
+#define JX_ETIMEOUT 5    /* a bounded wait (device or host watchdog) expired */
+#define JX_EUNSUPPORTED 6
+#define JX_EDEVICE 7     /* a kernel flagged bad input (see jx_device_status) */
+
+typedef void *jx_stream_t; /* a cudaStream_t */
+
+#if defined(__GNUC__)
+#define JX_API __attribute__((visibility("default")))
+#else
+#define JX_API
+#endif
+
+/* ---- context / device (src/backend/webgpu.rs:31-75, src/device.rs:10-80) -- */
+JX_API const char *jx_last_error(void);
+JX_API int jx_version(void);
+/* WebGpuContext::init (src/backend/webgpu.rs:31-64): select and initialise a device. */
+JX_API int jx_init(int device);
+JX_API int jx_device_count(int *count);
+JX_API int jx_set_device(int device);
+JX_API int jx_get_device(int *device);
+/* Device-side error word (bit 0: NaN met by an arg-reduction, bit 1: a bounded
+ * wait timed out).  Reads and clears it; synchronises the device. */
+JX_API int jx_device_status(unsigned int *flags);
+
+/* ---- storage (src/buffer.rs:40-122,581-590,700-749) ------------------------ */
+/* Buffer::zeros (src/buffer.rs:40-74) when zero != 0; stream-ordered allocation. */
+JX_API int jx_malloc(void **ptr, size_t nbytes, int zero, jx_stream_t stream);
+/* Last drop of a Buffer (Arc<BufferInner>); stream-ordered free. */
+JX_API int jx_free(void *ptr, jx_stream_t stream);
+/* Buffer::from_f32 upload (src/buffer.rs:81-122).  `src` is host memory. */
+JX_API int jx_memcpy_h2d(void *dst, const void *src, size_t nbytes, jx_stream_t stream);
+/* Buffer::to_f32_vec readback (src/buffer.rs:581-590,711-749): blocks until the
+ * copy lands in host memory `dst`. */
+JX_API int jx_memcpy_d2h(void *dst, const void *src, size_t nbytes, jx_stream_t stream);
+JX_API int jx_memcpy_d2d(void *dst, const void *src, size_t nbytes, jx_stream_t stream);
+JX_API int jx_stream_create(jx_stream_t *stream);
+JX_API int jx_stream_destroy(jx_stream_t stream);
+JX_API int jx_stream_sync(jx_stream_t stream);
+
+/* ---- GEMM (gpu_matmul src/backend/ops.rs:460-467; Array::matmul
+ *      src/ops/linalg.rs:154-237; einsum "bij,bjk->bik" src/ops/einsum.rs:488-523) */
+#define JX_PREC_3XTF32 0 /* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32 */
+#define JX_PREC_EXACT 1  /* sequential-k f32, no FMA: the reference's CPU loop order, bit-exact */
+/* C[b] = op(A[b]) . op(B[b]) for b < batch, row-major.  op(X) = X or X^T per
+ * trans flags: A is [M,K] (or [K,M] when transA), B is [K,N] (or [N,K]).
+ * lda/ldb/ldc: row strides in elements; stride*: batch strides in elements. */
+JX_API int jx_gemm_f32(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, int transA,
+                int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t strideA,
+                int64_t strideB, int64_t strideC, int precision, jx_stream_t stream);
+/* Scratch bytes jx_gemm_f32 uses (library-owned) for JX_PREC_3XTF32. */
+JX_API int jx_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t batch, size_t *bytes);
+/* The two stages of JX_PREC_3XTF32, for operands reused across calls (a weight
+ * matrix split once per step).  jx_gemm_kpad: K rounded up to the k-block.
+ * jx_gemm_split_f32 writes hi = tf32(x), lo = tf32(x - hi) K-major:
+ * hi/lo are [batch][rows][Kp]; element (r,k) is src[b*stride + r*ld + k], or
+ * src[b*stride + k*ld + r] when trans != 0.  jx_gemm_presplit_f32 computes
+ * C[b] = Ah.Bh^T + Ah.Bl^T + Al.Bh^T from such buffers (A rows = M, B rows = N). */
+JX_API int jx_gemm_kpad(int64_t K, int64_t *Kp);
+JX_API int jx_gemm_split_f32(const float *src, float *hi, float *lo, int64_t rows, int64_t K, int64_t ld,
+                             int trans, int64_t batch, int64_t stride, jx_stream_t stream);
+JX_API int jx_gemm_presplit_f32(const float *Ah, const float *Al, const float *Bh, const float *Bl, float *C,
+                                int64_t M, int64_t N, int64_t Kp, int64_t ldc, int64_t batch, int64_t strideC,
+                                jx_stream_t stream);
+
+/* ---- elementwise (gpu_binary_op src/backend/ops.rs:21-26; binary_op with
+ *      broadcasting src/ops/binary.rs:7-74,134-168; unary_op src/ops/unary.rs:30-49;
+ *      nn::relu/gelu/sigmoid src/nn.rs:22-26,111-140) ----------------------- */
+#define JX_BIN_ADD 0
+#define JX_BIN_SUB 1
+#define JX_BIN_MUL 2
+#define JX_BIN_DIV 3
+#define JX_BIN_POW 4
+#define JX_BIN_MIN 5
+#define JX_BIN_MAX 6
+/* out = a op b with NumPy broadcasting of a_shape/b_shape (ndim <= 8). */
+JX_API int jx_binary_f32(int op, const float *a, const int64_t *a_shape, int a_ndim, const float *b,
+                  const int64_t *b_shape, int b_ndim, float *out, jx_stream_t stream);
+#define JX_UN_NEG 0
+#define JX_UN_ABS 1
+#define JX_UN_SIN 2
+#define JX_UN_COS 3
+#define JX_UN_TANH 4
+#define JX_UN_EXP 5
+#define JX_UN_LOG 6
+#define JX_UN_SQRT 7
+#define JX_UN_RECIP 8
+#define JX_UN_SQUARE 9
+#define JX_UN_RELU 10
+#define JX_UN_GELU 11
+#define JX_UN_SIGMOID 12
+#define JX_UN_GELU_GRAD 13 /* d/dx nn::gelu (restated adjoint, used by grad tapes) */
+JX_API int jx_unary_f32(int op, const float *x, float *y, int64_t n, jx_stream_t stream);
+
+/* ---- jit op-tape (FusedGroup src/trace/ir.rs:8-17; gpu_fused_execute
+ *      src/backend/ops.rs:283-437; generate_fused_shader src/trace/fusion.rs:296-346)
+ * A tape is a straight-line register program over per-element values.  Each
+ * instruction is 4 int32 words {opcode, dst, src0, src1}; registers 0..nin-1
+ * hold the inputs on entry; JX_OP_CONST loads consts[src0]; JX_OP_STORE writes
+ * register src0 to output dst; registers 0..15 are usable.  The tape is
+ * validated on creation (operands defined before use, every output stored) and copied
+ * into the kernel's constant-bank parameter space on launch. */
+#define JX_OP_CONST 1
+#define JX_OP_STORE 2
+#define JX_OP_UNARY 16  /* opcode = 16 + JX_UN_* */
+#define JX_OP_BINARY 48 /* opcode = 48 + JX_BIN_* */
+#define JX_OP_SELECT_GT 64 /* dst = (src0 > 0) ? src1 : 0 (relu-style masks) */
+#define JX_TAPE_MAX_INSTR 128
+#define JX_TAPE_MAX_REGS 16
+#define JX_TAPE_MAX_CONSTS 64
+#define JX_TAPE_MAX_IO 8
+typedef struct jx_tape jx_tape;
+JX_API int jx_tape_create(const int32_t *code, int n_instr, const float *consts, int n_consts, int n_inputs,
+                   int n_outputs, jx_tape **out);
+JX_API int jx_tape_destroy(jx_tape *tape);
+/* ins/outs: host arrays of device pointers, each of n elements. */
+JX_API int jx_tape_run(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
+                jx_stream_t stream);
+
+/* ---- reductions (gpu_reduce_all src/backend/ops.rs:639-643; reduce_axis
+ *      src/ops/reduce.rs:53-135; argmax/argmin src/ops/reduce.rs:281-309) ---- */
+#define JX_RED_SUM 0
+#define JX_RED_MAX 1
+#define JX_RED_MIN 2
+#define JX_RED_PROD 3
+/* out[0] = fold(op) over n elements (device scalar). */
+JX_API int jx_reduce_all_f32(const float *x, float *out, int64_t n, int op, jx_stream_t stream);
+/* x viewed as [outer, len, inner]; out[outer, inner] = fold over len. */
+JX_API int jx_reduce_axis_f32(const float *x, float *out, int64_t outer, int64_t len, int64_t inner, int op,
+                       jx_stream_t stream);
+/* Per-row arg reduction of x[rows, cols]: argmax keeps the LAST index among
+ * equal maxima, argmin the FIRST among equal minima (Iterator::max_by/min_by).
+ * A NaN sets JX_DEVERR_NAN in the device error word (the reference panics).
+ * out_val may be NULL. */
+JX_API int jx_argreduce_rows_f32(const float *x, int32_t *out_idx, float *out_val, int64_t rows, int64_t cols,
+                          int is_max, jx_stream_t stream);
+/* VJPs (transpose_sum_axis src/trace/transpose_rules.rs:409-418; transpose_max_all
+ * :444-469 applied per row): dx[r,c] = ct[r]; dx[r,c] = ct[r]*(x==max)/(count>1?count:1). */
+JX_API int jx_sum_rows_vjp_f32(const float *ct, float *dx, int64_t rows, int64_t cols, jx_stream_t stream);
+JX_API int jx_max_rows_vjp_f32(const float *x, const float *ct, float *dx, int64_t rows, int64_t cols,
+                        jx_stream_t stream);
+
+/* ---- FFT (gpu_fft_complex src/backend/ops.rs:1736-1741; fft_recursive
+ *      src/ops/fft.rs:40-70; ifft :146-191; fft2/ifft2 :261-396) ----------- */
+/* Batched complex-to-complex FFT, interleaved [re,im] f32, n a power of two.
+ * inverse != 0 applies the 1/n scale as ifft does.  in may equal out. */
+JX_API int jx_fft_c2c_f32(const float *in, float *out, int64_t n, int64_t batch, int inverse, jx_stream_t stream);
+/* Batched 2-D transform of [batch, h, w] complex images: rows, then columns. */
+JX_API int jx_fft2_c2c_f32(const float *in, float *out, int64_t h, int64_t w, int64_t batch, int inverse,
+                    jx_stream_t stream);
+
+/* ---- conv2d (gpu_conv2d src/backend/ops.rs:815-828; nn::conv2d_batched
+ *      src/nn.rs:2048-2144), NCHW input, OIHW weight --------------------- */
+JX_API int jx_conv2d_fwd_f32(const float *x, const float *w, float *y, int64_t B, int64_t C, int64_t H, int64_t W,
+                      int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad, jx_stream_t stream);
+JX_API int jx_conv2d_bwd_data_f32(const float *dy, const float *w, float *dx, int64_t B, int64_t C, int64_t H,
+                           int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad,
+                           jx_stream_t stream);
+JX_API int jx_conv2d_bwd_filter_f32(const float *x, const float *dy, float *dw, int64_t B, int64_t C, int64_t H,
+                             int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad,
+                             jx_stream_t stream);
+
+/* ---- nn / optim (src/nn.rs:155-221,300-318; src/optim.rs:138-189) -------- */
+/* y[r,:] = softmax(x[r,:]) (src/nn.rs:155-168 applied per row). */
+JX_API int jx_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols, jx_stream_t stream);
+/* Fused softmax + cross_entropy_loss (src/nn.rs:300-318: mean over rows*cols
+ * elements, eps 1e-7) forward and backward.  labels are class indices (f32 as
+ * randint returns them, one_hot src/nn.rs:205-221 semantics).  Writes probs
+ * (may be NULL), dlogits = dL/dlogits, loss_out[0] (device scalar). */
+JX_API int jx_softmax_xent_f32(const float *logits, const float *labels, float *probs, float *dlogits,
+                        float *loss_out, int64_t rows, int64_t cols, jx_stream_t stream);
+/* y[r,c] = act(y[r,c] + bias[c]); act: 0 none, 1 relu, 2 gelu (broadcast_to +
+ * add src/ops/manipulation.rs:919-946, then src/nn.rs:22-26 / :111-122).
+ * pre (may be NULL) receives the pre-activation. */
+JX_API int jx_bias_act_f32(float *y, const float *bias, float *pre, int64_t rows, int64_t cols, int act,
+                    jx_stream_t stream);
+/* dz = dy * act'(pre) (act 1 relu, 2 gelu); db[c] = sum_r dz[r,c] (db may be NULL). */
+JX_API int jx_act_bwd_f32(const float *dy, const float *pre, float *dz, float *db, int64_t rows, int64_t cols,
+                   int act, jx_stream_t stream);
+/* Column sums db[c] = sum_r dy[r,c] (bias gradient). */
+JX_API int jx_col_sum_f32(const float *dy, float *db, int64_t rows, int64_t cols, jx_stream_t stream);
+/* optim::adam_update (src/optim.rs:138-189) over `count` tensors in one launch,
+ * in the reference's op order (bit-exact): step is the new step number (>=1);
+ * step == 1 treats m and v as absent (state.m == None). */
+JX_API int jx_adam_step_f32(float *const *params, const float *const *grads, float *const *m, float *const *v,
+                     const int64_t *sizes, int count, float lr, float beta1, float beta2, float eps,
+                     int64_t step, jx_stream_t stream);
+
+/* ---- data-parallel collectives (no reference counterpart: the reference has
+ *      a single global device, src/backend/webgpu.rs:6) -------------------- */
+JX_API int jx_nccl_unique_id_size(void);
+JX_API int jx_nccl_get_unique_id(void *id_out /* jx_nccl_unique_id_size() bytes */);
+/* Non-blocking communicator init with a host watchdog of timeout_ms. */
+JX_API int jx_nccl_init(const void *id, int nranks, int rank, int timeout_ms, void **comm_out);
+/* In-place sum all-reduce of count floats; polls for async errors up to timeout_ms. */
+JX_API int jx_nccl_allreduce_sum_f32(void *comm, float *buf, int64_t count, jx_stream_t stream);
+JX_API int jx_nccl_wait(void *comm, jx_stream_t stream, int timeout_ms);
+JX_API int jx_nccl_destroy(void *comm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JAXRS_CUDA_H */

@@ -1,0 +1,524 @@
+// gemm.cu -- f32 GEMM for Array::matmul (src/ops/linalg.rs:154-237), the
+// batched einsum "bij,bjk->bik" (src/ops/einsum.rs:488-523) and the matmul
+// transposes used by transpose_matmul (src/trace/transpose_rules.rs:537-567).
+//
+// JX_PREC_3XTF32: f32 accuracy on the 5th-generation tensor cores.
+//   1. split pass: every operand element x becomes hi = tf32_rn(x) and
+//      lo = tf32_rn(x - hi), written K-major (rows of K contiguous floats,
+//      K padded to the k-block) into library scratch; transposed operands are
+//      transposed here, so the main kernel only ever sees K-major tiles.
+//   2. main kernel (persistent, one CTA per SM, warp-specialised):
+//        warp 0      TMA producer: Ahi, Alo, Bhi, Blo tiles -> smem ring
+//        warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
+//                    D += Ah.Bh + Ah.Bl + Al.Bh  (kind::tf32, f32 accumulate in TMEM)
+//        warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> global C
+//      Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i
+//      overlap the main loop of tile i+1.
+// JX_PREC_EXACT: one thread per output, sequential k, no FMA contraction: the
+//   reference CPU loop's exact rounding sequence (bit-identical results).
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <mutex>
+
+#include "jx_common.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 32;  // 32 f32 = 128 B rows -> 128-byte swizzle
+constexpr int STAGES = 2;
+constexpr int A_TILE = BM * BK * 4;  // 16 KB
+constexpr int B_TILE = BN * BK * 4;  // 32 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+constexpr int GEMM_THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+constexpr int GROUP_M = 16;
+constexpr size_t GEMM_SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+struct TileInfo {
+  int m_blk, n_blk, b;
+};
+
+__device__ __forceinline__ TileInfo tile_coords(int t, int tiles_m, int tiles_n) {
+  int per_batch = tiles_m * tiles_n;
+  int b = t / per_batch;
+  int r = t - b * per_batch;
+  int in_group = GROUP_M * tiles_n;
+  int g = r / in_group;
+  int first_m = g * GROUP_M;
+  int gsize = min(tiles_m - first_m, GROUP_M);
+  int local = r - g * in_group;
+  TileInfo ti;
+  ti.m_blk = first_m + local % gsize;
+  ti.n_blk = local / gsize;
+  ti.b = b;
+  return ti;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait on an mbarrier phase with a wall-clock limit (about 4 s); on expiry the
+// device error word gets JX_DEVERR_TIMEOUT and the caller unwinds.
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* err) {
+  if (jxd::mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_ns();
+  while (true) {
+    for (int i = 0; i < 256; ++i)
+      if (jxd::mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > 4000000000ull) {
+      atomicOr(err, JX_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                       const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                       float* __restrict__ C, int M, int N, int Kp, long long ldc, long long strideC,
+                       int tiles_m, int tiles_n, int num_tiles, unsigned int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = jxd::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                 // [STAGES]
+  uint64_t* empty = bars + STAGES;       // [STAGES]
+  uint64_t* tfull = bars + 2 * STAGES;   // [2]
+  uint64_t* tempty = bars + 2 * STAGES + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = Kp / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      jxd::mbar_init(&full[s], 1);
+      jxd::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      jxd::mbar_init(&tfull[a], 1);
+      jxd::mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    jxd::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    jxd::tma_prefetch_desc(&tmAh);
+    jxd::tma_prefetch_desc(&tmAl);
+    jxd::tma_prefetch_desc(&tmBh);
+    jxd::tma_prefetch_desc(&tmBl);
+  }
+  if (warp == 1) {
+    jxd::tmem_alloc(tmem_slot, TMEM_COLS);
+    jxd::tmem_relinquish();
+  }
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (jxd::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+        const int ya = ti.m_blk * BM, yb = ti.n_blk * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          jxd::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          const int x = kb * BK;
+          jxd::tma_load_3d(st, &tmAh, &full[stage], x, ya, ti.b);
+          jxd::tma_load_3d(st + A_TILE, &tmAl, &full[stage], x, ya, ti.b);
+          jxd::tma_load_3d(st + 2 * A_TILE, &tmBh, &full[stage], x, yb, ti.b);
+          jxd::tma_load_3d(st + 2 * A_TILE + B_TILE, &tmBl, &full[stage], x, yb, ti.b);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: wait (bounded) until every load issued above has landed.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!wait_bounded(&empty[stage], phase ^ 1u, err)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (jxd::elect_one()) {
+      constexpr uint32_t idesc = jxd::idesc_tf32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      const uint32_t smem_base = jxd::smem_u32(smem);
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        if (!wait_bounded(&tempty[acc], acc_phase ^ 1u, err)) { *abort_flag = 1; break; }
+        jxd::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
+          jxd::tc_fence_after();
+          const uint32_t sa_h = smem_base + stage * STAGE_BYTES;
+          const uint32_t sa_l = sa_h + A_TILE;
+          const uint32_t sb_h = sa_h + 2 * A_TILE;
+          const uint32_t sb_l = sb_h + B_TILE;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
+            const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + off);
+            const uint64_t al = jxd::smem_desc_k_sw128(sa_l + off);
+            const uint64_t bh = jxd::smem_desc_k_sw128(sb_h + off);
+            const uint64_t bl = jxd::smem_desc_k_sw128(sb_l + off);
+            jxd::mma_tf32(d_tmem, al, bh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            jxd::mma_tf32(d_tmem, ah, bl, idesc, 1u);
+            jxd::mma_tf32(d_tmem, ah, bh, idesc, 1u);
+          }
+          jxd::mma_commit(&empty[stage]);  // frees the slot once these MMAs retire
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        jxd::mma_commit(&tfull[acc]);  // accumulator complete
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = ((ldc & 3) == 0) && ((strideC & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      if (*abort_flag) break;
+      if (!wait_bounded(&tfull[acc], acc_phase, err)) { *abort_flag = 1; break; }
+      jxd::tc_fence_after();
+      TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+      const int row = ti.m_blk * BM + q * 32 + lane;
+      float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
+      const int col0 = ti.n_blk * BN;
+      const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        jxd::tmem_ld16(t_addr + c, r);
+        jxd::tmem_ld_wait();
+        if (row < M) {
+          const int col = col0 + c;
+          if (vec_ok && col + 16 <= N) {
+            float4* dst = reinterpret_cast<float4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < N) crow[col + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+      jxd::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) jxd::mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    jxd::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Operand split: dst_hi/dst_lo [batch][rows][Kp] K-major, zero-padded K..Kp.
+//   direct:     element (r, k) at src[b*sb + r*ld + k]
+//   transposed: element (r, k) at src[b*sb + k*ld + r]
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  hi = __uint_as_float(h);
+  float rem = __fsub_rn(x, hi);
+  uint32_t l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(rem));
+  lo = __uint_as_float(l);
+}
+
+__global__ void split_direct_kernel(const float* __restrict__ src, float* __restrict__ hi,
+                                    float* __restrict__ lo, int rows, int K, int Kp, long long ld,
+                                    long long sb) {
+  const int b = blockIdx.z;
+  const long long total = (long long)rows * Kp;
+  const float* s = src + (long long)b * sb;
+  float* h = hi + (long long)b * total;
+  float* l = lo + (long long)b * total;
+  const bool vec = ((ld & 3) == 0) && ((sb & 3) == 0) && ((K & 3) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* sr = s + (long long)r * ld;
+    float* hr = h + (long long)r * Kp;
+    float* lr = l + (long long)r * Kp;
+    if (vec) {
+      for (int k = threadIdx.x * 4; k < Kp; k += blockDim.x * 4) {
+        float4 x = k < K ? *reinterpret_cast<const float4*>(sr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 xh, xl;
+        split_tf32(x.x, xh.x, xl.x);
+        split_tf32(x.y, xh.y, xl.y);
+        split_tf32(x.z, xh.z, xl.z);
+        split_tf32(x.w, xh.w, xl.w);
+        *reinterpret_cast<float4*>(hr + k) = xh;
+        *reinterpret_cast<float4*>(lr + k) = xl;
+      }
+    } else {
+      for (int k = threadIdx.x; k < Kp; k += blockDim.x) {
+        float x = k < K ? sr[k] : 0.0f;
+        float xh, xl;
+        split_tf32(x, xh, xl);
+        hr[k] = xh;
+        lr[k] = xl;
+      }
+    }
+  }
+}
+
+__global__ void split_transpose_kernel(const float* __restrict__ src, float* __restrict__ hi,
+                                       float* __restrict__ lo, int rows, int K, int Kp, long long ld,
+                                       long long sb) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const float* s = src + (long long)b * sb;
+  const long long total = (long long)rows * Kp;
+  float* h = hi + (long long)b * total;
+  float* l = lo + (long long)b * total;
+  const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  // read: element (r, k) lives at s[k*ld + r]; coalesced along r
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int k = k0 + j, r = r0 + threadIdx.x;
+    tile[j][threadIdx.x] = (k < K && r < rows) ? s[(long long)k * ld + r] : 0.0f;
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int r = r0 + j, k = k0 + threadIdx.x;
+    if (r < rows && k < Kp) {
+      float xh, xl;
+      split_tf32(tile[threadIdx.x][j], xh, xl);
+      h[(long long)r * Kp + k] = xh;
+      l[(long long)r * Kp + k] = xl;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Exact path: the reference loop's rounding sequence (src/ops/linalg.rs:220-228):
+// sum = 0; for p in 0..k { sum = sum + a*b } with each product and sum rounded.
+// ---------------------------------------------------------------------------
+__global__ void gemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                  float* __restrict__ C, int M, int N, int K, int transA, int transB,
+                                  long long lda, long long ldb, long long ldc, long long sA, long long sB,
+                                  long long sC) {
+  __shared__ float As[16][17];
+  __shared__ float Bs[16][17];
+  const int b = blockIdx.z;
+  const float* a = A + (long long)b * sA;
+  const float* bb = B + (long long)b * sB;
+  const int row = blockIdx.y * 16 + threadIdx.y;
+  const int col = blockIdx.x * 16 + threadIdx.x;
+  float sum = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    {
+      const int r = blockIdx.y * 16 + threadIdx.y, k = k0 + threadIdx.x;
+      float v = 0.0f;
+      if (r < M && k < K) v = transA ? a[(long long)k * lda + r] : a[(long long)r * lda + k];
+      As[threadIdx.y][threadIdx.x] = v;
+    }
+    {
+      const int k = k0 + threadIdx.y, c = blockIdx.x * 16 + threadIdx.x;
+      float v = 0.0f;
+      if (k < K && c < N) v = transB ? bb[(long long)c * ldb + k] : bb[(long long)k * ldb + c];
+      Bs[threadIdx.y][threadIdx.x] = v;
+    }
+    __syncthreads();
+    const int kmax = min(16, K - k0);
+    for (int kk = 0; kk < kmax; ++kk) sum = __fadd_rn(sum, __fmul_rn(As[threadIdx.y][kk], Bs[kk][threadIdx.x]));
+    __syncthreads();
+  }
+  if (row < M && col < N) C[(long long)b * sC + (long long)row * ldc + col] = sum;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return jx::fail(JX_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  return JX_OK;
+}
+
+int make_kmajor_map(CUtensorMap* map, const float* base, int Kp, int rows, int batch, int box_rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)Kp * 4, (cuuint64_t)Kp * 4 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return jx::fail(JX_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return JX_OK;
+}
+
+inline long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
+
+int launch_split(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
+                 int batch, bool transposed, cudaStream_t st) {
+  if (!transposed) {
+    int blocks = (int)std::min<long long>(rows, (long long)jx::num_sms() * 16);
+    split_direct_kernel<<<dim3(blocks, 1, batch), 256, 0, st>>>(src, hi, lo, rows, K, Kp, ld, sb);
+  } else {
+    dim3 grid((rows + 31) / 32, (Kp + 31) / 32, batch);
+    split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(src, hi, lo, rows, K, Kp, ld, sb);
+  }
+  JX_LAUNCH_CHECK("gemm split kernel");
+  return JX_OK;
+}
+
+}  // namespace
+
+namespace jx {
+// Shared by conv2d (implicit GEMM) and the dense layers: 3xTF32 GEMM on
+// pre-split K-major operands.  Ah/Al: [batch][M][Kp]; Bh/Bl: [batch][N][Kp].
+int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
+                  int Kp, long long ldc, long long strideC, int batch, cudaStream_t st) {
+  int rc = get_encode();
+  if (rc) return rc;
+  CUtensorMap mAh, mAl, mBh, mBl;
+  if ((rc = make_kmajor_map(&mAh, Ah, Kp, M, batch, BM))) return rc;
+  if ((rc = make_kmajor_map(&mAl, Al, Kp, M, batch, BM))) return rc;
+  if ((rc = make_kmajor_map(&mBh, Bh, Kp, N, batch, BN))) return rc;
+  if ((rc = make_kmajor_map(&mBl, Bl, Kp, N, batch, BN))) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+    attr_set[dev & 63] = true;
+  }
+  const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  const long long nt = (long long)tiles_m * tiles_n * batch;
+  if (nt > 0x7fffffffLL) return fail(JX_EINVAL, "gemm: too many tiles");
+  const int grid = (int)std::min<long long>(nt, num_sms());
+  unsigned int* err = device_error_word();
+  gemm_3xtf32_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(mAh, mAl, mBh, mBl, C, M, N, Kp, ldc, strideC, tiles_m,
+                                                          tiles_n, (int)nt, err);
+  JX_LAUNCH_CHECK("gemm_3xtf32_kernel");
+  return JX_OK;
+}
+
+int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
+                       int batch, bool transposed, cudaStream_t st) {
+  return launch_split(src, hi, lo, rows, K, Kp, ld, sb, batch, transposed, st);
+}
+
+long long gemm_kpad(long long K) { return round_up(K, BK); }
+}  // namespace jx
+
+extern "C" {
+
+int jx_gemm_kpad(int64_t K, int64_t* Kp) {
+  JX_REQUIRE(Kp && K >= 0, "jx_gemm_kpad: bad argument");
+  *Kp = round_up(K, BK);
+  return JX_OK;
+}
+
+int jx_gemm_split_f32(const float* src, float* hi, float* lo, int64_t rows, int64_t K, int64_t ld, int trans,
+                      int64_t batch, int64_t stride, jx_stream_t stream) {
+  JX_REQUIRE(rows >= 0 && K >= 0 && batch >= 0, "gemm split: negative dimension");
+  if (rows == 0 || batch == 0) return JX_OK;
+  JX_REQUIRE(src && hi && lo, "gemm split: NULL pointer");
+  JX_REQUIRE(rows < (1LL << 31) && K < (1LL << 31) && batch < 65536, "gemm split: dimension too large");
+  JX_REQUIRE(ld >= (trans ? rows : K), "gemm split: leading dimension too small");
+  const long long Kp = round_up(K, BK);
+  return launch_split(src, hi, lo, (int)rows, (int)K, (int)Kp, ld, stride, (int)batch, trans != 0,
+                      jx::as_stream(stream));
+}
+
+int jx_gemm_presplit_f32(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int64_t M,
+                         int64_t N, int64_t Kp, int64_t ldc, int64_t batch, int64_t strideC, jx_stream_t stream) {
+  JX_REQUIRE(M >= 0 && N >= 0 && Kp >= 0 && batch >= 0, "gemm presplit: negative dimension");
+  if (M == 0 || N == 0 || batch == 0) return JX_OK;
+  JX_REQUIRE(Ah && Al && Bh && Bl && C, "gemm presplit: NULL pointer");
+  JX_REQUIRE(Kp > 0 && Kp % BK == 0, "gemm presplit: Kp must be a positive multiple of %d", BK);
+  JX_REQUIRE(ldc >= N, "gemm presplit: ldc too small");
+  JX_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && Kp < (1LL << 31) && batch < 65536, "gemm presplit: too large");
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  JX_REQUIRE(a16(Ah) && a16(Al) && a16(Bh) && a16(Bl), "gemm presplit: operands must be 16-byte aligned");
+  return jx::gemm_presplit(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch,
+                           jx::as_stream(stream));
+}
+
+int jx_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t batch, size_t* bytes) {
+  JX_REQUIRE(bytes, "jx_gemm_workspace_size: NULL");
+  long long Kp = round_up(K, BK);
+  *bytes = (size_t)2 * (size_t)batch * (size_t)(M + N) * (size_t)Kp * sizeof(float);
+  return JX_OK;
+}
+
+int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int transA, int transB,
+                int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t strideA, int64_t strideB,
+                int64_t strideC, int precision, jx_stream_t stream) {
+  JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
+  if (M == 0 || N == 0 || batch == 0) return JX_OK;
+  JX_REQUIRE(A && B && C, "matmul: NULL operand");
+  JX_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && batch < 65536, "matmul: dimension too large");
+  JX_REQUIRE(lda >= (transA ? M : K) && ldb >= (transB ? K : N) && ldc >= N, "matmul: leading dimension too small");
+  cudaStream_t st = jx::as_stream(stream);
+  if (K == 0) {
+    for (int64_t b = 0; b < batch; ++b)
+      JX_CUDA(cudaMemset2DAsync(C + b * strideC, ldc * 4, 0, N * 4, M, st));
+    return JX_OK;
+  }
+  if (precision == JX_PREC_EXACT) {
+    dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + 15) / 16), (unsigned)batch);
+    JX_REQUIRE(grid.y < 65536, "matmul(exact): M too large");
+    gemm_exact_kernel<<<grid, dim3(16, 16), 0, st>>>(A, B, C, (int)M, (int)N, (int)K, transA, transB, lda, ldb, ldc,
+                                                     strideA, strideB, strideC);
+    JX_LAUNCH_CHECK("gemm_exact_kernel");
+    return JX_OK;
+  }
+  JX_REQUIRE(precision == JX_PREC_3XTF32, "matmul: unknown precision %d", precision);
+  const long long Kp = round_up(K, BK);
+  size_t ws = 0;
+  jx_gemm_workspace_size(M, N, K, batch, &ws);
+  void* scratch = nullptr;
+  int rc = jx::scratch_get(ws, &scratch, st);
+  if (rc) return rc;
+  float* Ah = reinterpret_cast<float*>(scratch);
+  float* Al = Ah + (size_t)batch * M * Kp;
+  float* Bh = Al + (size_t)batch * M * Kp;
+  float* Bl = Bh + (size_t)batch * N * Kp;
+  rc = launch_split(A, Ah, Al, (int)M, (int)K, (int)Kp, lda, strideA, (int)batch, transA != 0, st);
+  if (!rc) rc = launch_split(B, Bh, Bl, (int)N, (int)K, (int)Kp, ldb, strideB, (int)batch, transB == 0, st);
+  if (!rc) rc = jx::gemm_presplit(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st);
+  int rc2 = jx::scratch_release(scratch, st);
+  return rc ? rc : rc2;
+}
+
+}  // extern "C"

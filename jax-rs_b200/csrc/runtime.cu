@@ -1,0 +1,219 @@
+// runtime.cu -- context, error reporting, storage and streams of the C ABI.
+//
+// Replaces the reference's WebGPU context (src/backend/webgpu.rs:6-75: a global
+// OnceLock device + queue) with one CUDA context per device, and its Buffer
+// storage (src/buffer.rs:12-122, 581-749) with stream-ordered allocations.
+#include <stdarg.h>
+#include <mutex>
+#include <vector>
+
+#include "jx_common.cuh"
+
+namespace jx {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return JX_OK;
+  set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  return e == cudaErrorMemoryAllocation ? JX_ENOMEM : JX_ECUDA;
+}
+
+cudaStream_t as_stream(jx_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static const int kMaxDev = 64;
+static std::mutex g_mu;
+static int g_sms[kMaxDev];
+static unsigned int* g_err_word[kMaxDev];
+
+static int cur_dev() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int num_sms() {
+  int d = cur_dev();
+  if (d < 0 || d >= kMaxDev) return 148;
+  if (g_sms[d] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    g_sms[d] = n > 0 ? n : 148;
+  }
+  return g_sms[d];
+}
+
+int scratch_get(size_t bytes, void** out, cudaStream_t st) {
+  *out = nullptr;
+  cudaError_t e = cudaMallocAsync(out, bytes ? bytes : 16, st);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return check_cuda(e, "scratch cudaMallocAsync");
+  }
+  return JX_OK;
+}
+
+int scratch_release(void* p, cudaStream_t st) {
+  if (!p) return JX_OK;
+  cudaError_t e = cudaFreeAsync(p, st);
+  return e == cudaSuccess ? JX_OK : check_cuda(e, "scratch cudaFreeAsync");
+}
+
+unsigned int* device_error_word() {
+  int d = cur_dev();
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_word[d]) {
+    if (cudaMalloc(&g_err_word[d], sizeof(unsigned int)) != cudaSuccess) return nullptr;
+    cudaMemset(g_err_word[d], 0, sizeof(unsigned int));
+    cudaDeviceSynchronize();
+  }
+  return g_err_word[d];
+}
+
+}  // namespace jx
+
+using namespace jx;
+
+extern "C" {
+
+const char* jx_last_error(void) { return g_last_error.c_str(); }
+
+int jx_version(void) { return 1; }
+
+int jx_device_count(int* count) {
+  JX_REQUIRE(count, "jx_device_count: count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return check_cuda(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return JX_OK;
+}
+
+int jx_init(int device) {
+  int n = 0;
+  JX_CUDA(cudaGetDeviceCount(&n));
+  JX_REQUIRE(device >= 0 && device < n, "jx_init: device %d out of range (%d devices)", device, n);
+  JX_CUDA(cudaSetDevice(device));
+  cudaDeviceProp p;
+  JX_CUDA(cudaGetDeviceProperties(&p, device));
+  if (p.major != 10)
+    return fail(JX_EUNSUPPORTED, "jx_init: device %d is sm_%d%d; this library is built for sm_100a only",
+                device, p.major, p.minor);
+  JX_CUDA(cudaFree(0));  // create the primary context
+  {
+    // Keep stream-ordered scratch cached in the pool between calls.
+    cudaMemPool_t pool;
+    JX_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+    uint64_t thr = UINT64_MAX;
+    JX_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
+  }
+  (void)num_sms();
+  if (!device_error_word()) return fail(JX_ENOMEM, "jx_init: cannot allocate the device error word");
+  return JX_OK;
+}
+
+int jx_set_device(int device) {
+  JX_CUDA(cudaSetDevice(device));
+  return JX_OK;
+}
+
+int jx_get_device(int* device) {
+  JX_REQUIRE(device, "jx_get_device: NULL");
+  JX_CUDA(cudaGetDevice(device));
+  return JX_OK;
+}
+
+int jx_device_status(unsigned int* flags) {
+  JX_REQUIRE(flags, "jx_device_status: NULL");
+  unsigned int* w = device_error_word();
+  if (!w) return fail(JX_ENOMEM, "device error word unavailable");
+  JX_CUDA(cudaDeviceSynchronize());
+  unsigned int v = 0;
+  JX_CUDA(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost));
+  JX_CUDA(cudaMemset(w, 0, sizeof(v)));
+  *flags = v;
+  return JX_OK;
+}
+
+int jx_malloc(void** ptr, size_t nbytes, int zero, jx_stream_t stream) {
+  JX_REQUIRE(ptr, "jx_malloc: ptr is NULL");
+  *ptr = nullptr;
+  if (nbytes == 0) nbytes = 16;
+  cudaError_t e = cudaMallocAsync(ptr, nbytes, as_stream(stream));
+  if (e != cudaSuccess) {
+    *ptr = nullptr;
+    return check_cuda(e, "jx_malloc: cudaMallocAsync");
+  }
+  if (zero) JX_CUDA(cudaMemsetAsync(*ptr, 0, nbytes, as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_free(void* ptr, jx_stream_t stream) {
+  if (!ptr) return JX_OK;
+  JX_CUDA(cudaFreeAsync(ptr, as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_memcpy_h2d(void* dst, const void* src, size_t nbytes, jx_stream_t stream) {
+  if (nbytes == 0) return JX_OK;
+  JX_REQUIRE(dst && src, "jx_memcpy_h2d: NULL pointer");
+  JX_CUDA(cudaMemcpyAsync(dst, src, nbytes, cudaMemcpyHostToDevice, as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_memcpy_d2h(void* dst, const void* src, size_t nbytes, jx_stream_t stream) {
+  if (nbytes == 0) return JX_OK;
+  JX_REQUIRE(dst && src, "jx_memcpy_d2h: NULL pointer");
+  JX_CUDA(cudaMemcpyAsync(dst, src, nbytes, cudaMemcpyDeviceToHost, as_stream(stream)));
+  JX_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_memcpy_d2d(void* dst, const void* src, size_t nbytes, jx_stream_t stream) {
+  if (nbytes == 0) return JX_OK;
+  JX_REQUIRE(dst && src, "jx_memcpy_d2d: NULL pointer");
+  JX_CUDA(cudaMemcpyAsync(dst, src, nbytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_stream_create(jx_stream_t* stream) {
+  JX_REQUIRE(stream, "jx_stream_create: NULL");
+  cudaStream_t s;
+  JX_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = reinterpret_cast<jx_stream_t>(s);
+  return JX_OK;
+}
+
+int jx_stream_destroy(jx_stream_t stream) {
+  if (stream) JX_CUDA(cudaStreamDestroy(as_stream(stream)));
+  return JX_OK;
+}
+
+int jx_stream_sync(jx_stream_t stream) {
+  JX_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  return JX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/jaxrs_cuda.h declares, and rejects bad arguments with JX_EINVAL before
+touching the device (the reference panics on the same conditions)."""
+import ctypes as C
+
+import pytest
+
+
+def test_library_exports_every_declared_symbol(jx):
+    L = jx.lib()
+    declared = jx.header_symbols()
+    assert len(declared) >= 40
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, missing
+
+
+def test_binding_covers_header(jx):
+    assert set(jx.header_symbols()) <= set(jx._SIGS)
+
+
+def test_gemm_rejects_bad_shapes(jx):
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.gemm(0, 0, 0, -1, 2, 2)
+    assert e.value.status == jx.JX_EINVAL
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.gemm(1, 1, 1, 4, 4, 4, lda=2)
+    assert "leading dimension" in e.value.message
+    with pytest.raises(jx.JaxRsError):
+        jx.gemm(1, 1, 1, 4, 4, 4, precision=7)
+
+
+def test_gemm_empty_is_a_noop(jx):
+    jx.gemm(0, 0, 0, 0, 5, 3)
+    jx.gemm(0, 0, 0, 5, 0, 3)
+
+
+def test_tape_validation(jx):
+    U, B = jx.OP_UNARY, jx.OP_BINARY
+    good = [(B + jx.BIN["mul"], 1, 0, 0), (jx.OP_STORE, 0, 1, 0)]
+    t = jx.Tape(good, [], 1, 1)
+    assert t.handle
+    bad_cases = [
+        ([(U + jx.UN["exp"], 1, 5, 0), (jx.OP_STORE, 0, 1, 0)], "undefined source"),
+        ([(B + jx.BIN["add"], 1, 0, 0)], "output never stored"),
+        ([(99, 1, 0, 0), (jx.OP_STORE, 0, 1, 0)], "unknown opcode"),
+        ([(jx.OP_CONST, 1, 3, 0), (jx.OP_STORE, 0, 1, 0)], "constant index"),
+        ([(U + jx.UN["exp"], 40, 0, 0), (jx.OP_STORE, 0, 40, 0)], "register range"),
+    ]
+    for code, why in bad_cases:
+        with pytest.raises(jx.JaxRsError) as e:
+            jx.Tape(code, [1.0], 1, 1)
+        assert e.value.status == jx.JX_EINVAL, why
+    with pytest.raises(jx.JaxRsError):
+        jx.Tape(good * 100, [], 1, 1)  # longer than JX_TAPE_MAX_INSTR
+
+
+def test_binary_broadcast_rejects_incompatible(jx):
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.binary("add", 1, (2, 3), 1, (4,), 1)
+    assert "broadcast" in e.value.message
+
+
+def test_reduce_and_arg_argument_checks(jx):
+    with pytest.raises(jx.JaxRsError):
+        jx.call("jx_reduce_all_f32", 1, 1, 10, 9, None)
+    with pytest.raises(jx.JaxRsError):
+        jx.argreduce_rows(1, 1, None, 4, 0)
+
+
+def test_last_error_is_thread_local(jx):
+    import threading
+    with pytest.raises(jx.JaxRsError):
+        jx.gemm(0, 0, 0, -1, 1, 1)
+    msg = jx.last_error()
+    seen = []
+
+    def other():
+        seen.append(jx.last_error())
+
+    th = threading.Thread(target=other)
+    th.start()
+    th.join()
+    assert msg and seen == [""]
