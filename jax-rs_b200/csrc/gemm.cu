@@ -11,9 +11,13 @@
 //        warp 0      TMA producer: Ahi, Alo, Bhi, Blo tiles -> smem ring
 //        warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
 //                    D += Ah.Bh + Ah.Bl + Al.Bh  (kind::tf32, f32 accumulate in TMEM)
-//        warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> global C
-//      Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i
-//      overlap the main loop of tile i+1.
+//        warps 2..9  epilogue: the tile's f32 accumulator lives in registers
+//      K is consumed in spans of 128: the MMA warp sums one span into one of
+//      two TMEM partial buffers (2 x 256 columns, ping-pong) while the
+//      epilogue adds the previous span into registers with round-to-nearest.
+//      The tensor core's internal accumulation truncates; short TMEM sums
+//      keep that bias from growing with K, so the result holds f32 accuracy
+//      at any K.  The epilogue stores C once per tile.
 // JX_PREC_EXACT: one thread per output, sequential k, no FMA contraction: the
 //   reference CPU loop's exact rounding sequence (bit-identical results).
 #include <cudaTypedefs.h>
@@ -31,8 +35,11 @@ constexpr int STAGES = 2;
 constexpr int A_TILE = BM * BK * 4;  // 16 KB
 constexpr int B_TILE = BN * BK * 4;  // 32 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
-constexpr int GEMM_THREADS = 192;
-constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+constexpr int EPI_WARPS = 8;                     // epilogue warps (two per TMEM lane quarter)
+constexpr int EPI_COLS = BN / 2;                 // columns of the tile each epilogue thread owns
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;  // producer warp + MMA warp + epilogue
+constexpr int TMEM_COLS = 2 * BN;                // two span partial buffers
+constexpr int SPAN_KB = 4;                       // k-blocks per TMEM partial sum (128 K elements)
 constexpr int GROUP_M = 16;
 constexpr size_t GEMM_SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
@@ -86,10 +93,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t raw_addr = jxd::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;                 // [STAGES]
-  uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* tfull = bars + 2 * STAGES;   // [2]
-  uint64_t* tempty = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* full = bars;                     // [STAGES] TMA -> MMA
+  uint64_t* empty = bars + STAGES;           // [STAGES] MMA -> TMA
+  uint64_t* sfull = bars + 2 * STAGES;       // [2] span partial ready (MMA -> epilogue)
+  uint64_t* sempty = bars + 2 * STAGES + 2;  // [2] span partial drained (epilogue -> MMA)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -103,8 +110,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       jxd::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
-      jxd::mbar_init(&tfull[a], 1);
-      jxd::mbar_init(&tempty[a], 4);
+      jxd::mbar_init(&sfull[a], 1);
+      jxd::mbar_init(&sempty[a], EPI_WARPS);
     }
     *abort_flag = 0;
     jxd::fence_mbar_init();
@@ -144,7 +151,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: wait (bounded) until every load issued above has landed.
+      // Drain: wait (bounded) until every load issued above has been consumed.
       for (int s = 0; s < STAGES; ++s) {
         if (!wait_bounded(&empty[stage], phase ^ 1u, err)) break;
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -152,81 +159,98 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // K is consumed in spans of SPAN_KB k-blocks.  Each span accumulates from
+    // zero into one of two TMEM partial buffers (ping-pong); the epilogue adds
+    // the span into f32 registers with round-to-nearest.  The tensor core's
+    // own accumulation truncates, so keeping each TMEM sum short bounds that
+    // bias; over a full K it would grow linearly with K.
     if (jxd::elect_one()) {
       constexpr uint32_t idesc = jxd::idesc_tf32(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      uint32_t span_ctr = 0;
       const uint32_t smem_base = jxd::smem_u32(smem);
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-        if (!wait_bounded(&tempty[acc], acc_phase ^ 1u, err)) { *abort_flag = 1; break; }
-        jxd::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
+        for (int kb0 = 0; kb0 < num_kb && !*abort_flag; kb0 += SPAN_KB) {
+          const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+          if (!wait_bounded(&sempty[p], ph ^ 1u, err)) { *abort_flag = 1; break; }
           jxd::tc_fence_after();
-          const uint32_t sa_h = smem_base + stage * STAGE_BYTES;
-          const uint32_t sa_l = sa_h + A_TILE;
-          const uint32_t sb_h = sa_h + 2 * A_TILE;
-          const uint32_t sb_l = sb_h + B_TILE;
+          const uint32_t d_tmem = tmem_base + p * (uint32_t)BN;
+          const int kb_end = min(kb0 + SPAN_KB, num_kb);
+          for (int kb = kb0; kb < kb_end; ++kb) {
+            if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
+            jxd::tc_fence_after();
+            const uint32_t sa_h = smem_base + stage * STAGE_BYTES;
+            const uint32_t sa_l = sa_h + A_TILE;
+            const uint32_t sb_h = sa_h + 2 * A_TILE;
+            const uint32_t sb_l = sb_h + B_TILE;
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k) {
-            const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
-            const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + off);
-            const uint64_t al = jxd::smem_desc_k_sw128(sa_l + off);
-            const uint64_t bh = jxd::smem_desc_k_sw128(sb_h + off);
-            const uint64_t bl = jxd::smem_desc_k_sw128(sb_l + off);
-            jxd::mma_tf32(d_tmem, al, bh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            jxd::mma_tf32(d_tmem, ah, bl, idesc, 1u);
-            jxd::mma_tf32(d_tmem, ah, bh, idesc, 1u);
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
+              const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + off);
+              const uint64_t al = jxd::smem_desc_k_sw128(sa_l + off);
+              const uint64_t bh = jxd::smem_desc_k_sw128(sb_h + off);
+              const uint64_t bl = jxd::smem_desc_k_sw128(sb_l + off);
+              jxd::mma_tf32(d_tmem, al, bh, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+              jxd::mma_tf32(d_tmem, ah, bl, idesc, 1u);
+              jxd::mma_tf32(d_tmem, ah, bh, idesc, 1u);
+            }
+            jxd::mma_commit(&empty[stage]);  // frees the smem slot once these MMAs retire
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
           }
-          jxd::mma_commit(&empty[stage]);  // frees the slot once these MMAs retire
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          jxd::mma_commit(&sfull[p]);  // span partial complete
+          ++span_ctr;
         }
-        jxd::mma_commit(&tfull[acc]);  // accumulator complete
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Warp w may access TMEM lanes 32*(w%4)..+31 (one output row per thread);
+    // the two warps sharing a lane quarter split the 256 columns in halves.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const bool vec_ok = ((ldc & 3) == 0) && ((strideC & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    uint32_t span_ctr = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      if (*abort_flag) break;
-      if (!wait_bounded(&tfull[acc], acc_phase, err)) { *abort_flag = 1; break; }
-      jxd::tc_fence_after();
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+      bool ok = true;
+      for (int kb0 = 0; kb0 < num_kb; kb0 += SPAN_KB) {
+        const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+        if (*abort_flag || !wait_bounded(&sfull[p], ph, err)) { *abort_flag = 1; ok = false; break; }
+        jxd::tc_fence_after();
+        const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + p * (uint32_t)BN + (uint32_t)(half * EPI_COLS);
+#pragma unroll
+        for (int c = 0; c < EPI_COLS; c += 32) {
+          uint32_t r[32];
+          jxd::tmem_ld32(t_addr + c, r);
+          jxd::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c + j] = __fadd_rn(acc[c + j], __uint_as_float(r[j]));
+        }
+        jxd::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) jxd::mbar_arrive(&sempty[p]);
+        ++span_ctr;
+      }
+      if (!ok) break;
       TileInfo ti = tile_coords(t, tiles_m, tiles_n);
       const int row = ti.m_blk * BM + q * 32 + lane;
-      float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
-      const int col0 = ti.n_blk * BN;
-      const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        jxd::tmem_ld16(t_addr + c, r);
-        jxd::tmem_ld_wait();
-        if (row < M) {
-          const int col = col0 + c;
-          if (vec_ok && col + 16 <= N) {
-            float4* dst = reinterpret_cast<float4*>(crow + col);
+      if (row < M) {
+        float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
+        const int col0 = ti.n_blk * BN + half * EPI_COLS;
+        if (vec_ok && col0 + EPI_COLS <= N) {
+          float4* dst = reinterpret_cast<float4*>(crow + col0);
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-          } else {
+          for (int v = 0; v < EPI_COLS / 4; ++v)
+            dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+        } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (col + j < N) crow[col + j] = __uint_as_float(r[j]);
-          }
+          for (int j = 0; j < EPI_COLS; ++j)
+            if (col0 + j < N) crow[col0 + j] = acc[j];
         }
       }
-      jxd::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) jxd::mbar_arrive(&tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
   }
 

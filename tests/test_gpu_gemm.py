@@ -43,7 +43,7 @@ def test_identity(jx, dev, prec):
 
 
 SHAPES = [(1, 1, 1), (2, 3, 4), (17, 33, 65), (128, 256, 32), (129, 257, 33), (300, 520, 1000),
-          (1024, 1024, 1024), (640, 384, 2048), (255, 1000, 784)]
+          (1024, 1024, 1024), (640, 384, 2048), (255, 1000, 784), (256, 256, 32768), (128, 512, 100003)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
