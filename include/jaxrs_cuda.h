@@ -94,6 +94,20 @@ JX_API int jx_gemm_split_f32(const float *src, float *hi, float *lo, int64_t row
 JX_API int jx_gemm_presplit_f32(const float *Ah, const float *Al, const float *Bh, const float *Bl, float *C,
                                 int64_t M, int64_t N, int64_t Kp, int64_t ldc, int64_t batch, int64_t strideC,
                                 jx_stream_t stream);
+/* No counterpart in the reference.  jx_gemm_f32 (JX_PREC_3XTF32) for callers
+ * that cannot let a library allocate device memory: a process whose own arena
+ * or caching allocator already owns the device's memory, a latency-critical
+ * loop that cannot afford an allocator call, or a plugin host that forbids
+ * allocation behind its back.  It allocates nothing; its operand-split
+ * workspace is a fixed 64 MiB device array inside the library, held by every
+ * GPU that loads the library until the process exits.  Limit:
+ * 2*batch*(M+N)*round_up(K,32) <= 16777216 floats, else JX_EINVAL.  The first
+ * call on each device looks up the array's address (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
+JX_API int jx_gemm_f32_noalloc(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
+                               int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
+                               int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream);
 
 /* ---- elementwise (gpu_binary_op src/backend/ops.rs:21-26; binary_op with
  *      broadcasting src/ops/binary.rs:7-74,134-168; unary_op src/ops/unary.rs:30-49;

@@ -62,6 +62,7 @@ _SIGS = {
     "jx_gemm_f32": [vp, vp, vp, i64, i64, i64, ci, ci, i64, i64, i64, i64, i64, i64, i64, ci, vp],
     "jx_gemm_workspace_size": [i64, i64, i64, i64, C.POINTER(C.c_size_t)],
     "jx_gemm_kpad": [i64, C.POINTER(i64)],
+    "jx_gemm_f32_noalloc": [vp, vp, vp, i64, i64, i64, ci, ci, i64, i64, i64, i64, i64, i64, i64, vp],
     "jx_gemm_split_f32": [vp, vp, vp, i64, i64, i64, ci, i64, i64, vp],
     "jx_gemm_presplit_f32": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp],
     "jx_binary_f32": [ci, vp, C.POINTER(i64), ci, vp, C.POINTER(i64), ci, vp, vp],

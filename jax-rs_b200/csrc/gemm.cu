@@ -429,8 +429,9 @@ int launch_split(const float* src, float* hi, float* lo, int rows, int K, int Kp
 namespace jx {
 // Shared by conv2d (implicit GEMM) and the dense layers: 3xTF32 GEMM on
 // pre-split K-major operands.  Ah/Al: [batch][M][Kp]; Bh/Bl: [batch][N][Kp].
-int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
-                  int Kp, long long ldc, long long strideC, int batch, cudaStream_t st) {
+// Launches the main kernel; `err` is the device word it flags a timed-out wait in.
+int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
+                      int Kp, long long ldc, long long strideC, int batch, cudaStream_t st, unsigned int* err) {
   int rc = get_encode();
   if (rc) return rc;
   CUtensorMap mAh, mAl, mBh, mBl;
@@ -449,11 +450,15 @@ int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float
   const long long nt = (long long)tiles_m * tiles_n * batch;
   if (nt > 0x7fffffffLL) return fail(JX_EINVAL, "gemm: too many tiles");
   const int grid = (int)std::min<long long>(nt, num_sms());
-  unsigned int* err = device_error_word();
   gemm_3xtf32_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(mAh, mAl, mBh, mBl, C, M, N, Kp, ldc, strideC, tiles_m,
                                                           tiles_n, (int)nt, err);
   JX_LAUNCH_CHECK("gemm_3xtf32_kernel");
   return JX_OK;
+}
+
+int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
+                  int Kp, long long ldc, long long strideC, int batch, cudaStream_t st) {
+  return gemm_presplit_err(Ah, Al, Bh, Bl, C, M, N, Kp, ldc, strideC, batch, st, device_error_word());
 }
 
 int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
@@ -546,3 +551,93 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// jx_gemm_f32_noalloc: the 3xTF32 GEMM for callers that must not allocate.
+//
+// Some callers cannot let a library allocate device memory. A host process
+// may have handed all of HBM to its own arena or caching allocator up front,
+// so a library allocation either fails or fragments memory it does not own. A
+// latency-critical loop may not afford an allocator call. A plugin host may
+// forbid libraries from allocating behind its back. jx_gemm_f32 takes its
+// operand-split workspace from the device memory pool on every call; this
+// variant instead uses the fixed array below, so it performs no allocation of
+// any kind. The caller still provides A, B and C.
+//
+// Limits and behaviour:
+//   * The workspace holds NOALLOC_SCRATCH_FLOATS floats (64 MiB). A call needs
+//     2 * batch * (M + N) * round_up(K, 32) floats; larger problems are
+//     rejected with JX_EINVAL before anything is launched.
+//   * Every GPU that loads this library keeps the 64 MiB array until the
+//     process exits.
+//   * The array's device address is looked up with cudaGetSymbolAddress on the
+//     first call made on each device (with that device current). That first
+//     call should therefore come before any stream capture.
+//   * All calls share the one array and it keeps the last call's contents:
+//     the split pass rewrites every element a call reads (K padding included),
+//     so nothing needs clearing. Calls that overlap on the GPU (for example
+//     on two streams of one device) race on the array; the caller must
+//     serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t NOALLOC_SCRATCH_FLOATS = (size_t)16 << 20;  // 64 MiB of f32
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+static __device__ unsigned int g_noalloc_err;  // timed-out-wait flag of this entry point's launches
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64];
+unsigned int* g_noalloc_err_ptr[64];
+
+// Host code may not pass g_noalloc_scratch itself to a kernel: in host code
+// that name is a host-side stand-in, not the device address.
+int noalloc_setup(float** scratch, unsigned int** err) {
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return jx::fail(JX_EUNSUPPORTED, "gemm noalloc: device index %d >= 64", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    void* q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return jx::check_cuda(e, "gemm noalloc: cudaGetSymbolAddress(scratch)");
+    e = cudaGetSymbolAddress(&q, g_noalloc_err);
+    if (e != cudaSuccess) return jx::check_cuda(e, "gemm noalloc: cudaGetSymbolAddress(error word)");
+    g_noalloc_err_ptr[dev] = reinterpret_cast<unsigned int*>(q);
+    g_noalloc_ptr[dev] = reinterpret_cast<float*>(p);
+  }
+  *scratch = g_noalloc_ptr[dev];
+  *err = g_noalloc_err_ptr[dev];
+  return JX_OK;
+}
+}  // namespace
+
+extern "C" int jx_gemm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                                   int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
+                                   int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream) {
+  JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
+  if (M == 0 || N == 0 || batch == 0) return JX_OK;
+  JX_REQUIRE(A && B && C, "matmul: NULL operand");
+  JX_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && batch < 65536, "matmul: dimension too large");
+  JX_REQUIRE(lda >= (transA ? M : K) && ldb >= (transB ? K : N) && ldc >= N, "matmul: leading dimension too small");
+  JX_REQUIRE(K > 0, "gemm noalloc: K must be positive");
+  const long long Kp = round_up(K, BK);
+  const double need = 2.0 * (double)batch * (double)(M + N) * (double)Kp;
+  if (need > (double)NOALLOC_SCRATCH_FLOATS)
+    return jx::fail(JX_EINVAL,
+                    "gemm noalloc: needs %.0f workspace floats (2*batch*(M+N)*Kp), above the fixed maximum of %zu "
+                    "(64 MiB); use jx_gemm_f32 for this size",
+                    need, NOALLOC_SCRATCH_FLOATS);
+  float* ws = nullptr;
+  unsigned int* err = nullptr;
+  int rc = noalloc_setup(&ws, &err);
+  if (rc) return rc;
+  cudaStream_t st = jx::as_stream(stream);
+  float* Ah = ws;
+  float* Al = Ah + (size_t)batch * M * Kp;
+  float* Bh = Al + (size_t)batch * M * Kp;
+  float* Bl = Bh + (size_t)batch * N * Kp;
+  rc = launch_split(A, Ah, Al, (int)M, (int)K, (int)Kp, lda, strideA, (int)batch, transA != 0, st);
+  if (!rc) rc = launch_split(B, Bh, Bl, (int)N, (int)K, (int)Kp, ldb, strideB, (int)batch, transB == 0, st);
+  if (!rc) rc = jx::gemm_presplit_err(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st, err);
+  return rc;
+}
