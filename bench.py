@@ -46,7 +46,7 @@ def parse():
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-rows", type=int, default=48, help="GEMM rows timed by the CPU baseline")
+    p.add_argument("--cpu-rows", type=int, default=24, help="GEMM rows timed by the CPU baseline")
     return p.parse_args()
 
 
@@ -320,6 +320,55 @@ def run_chain(args, dist, jx, torch):
             "gpu_launches": args.steps, "clocks": clocks}
 
 
+def run_reduce(args, dist, jx, torch):
+    """Last-axis sum / argmax over [65536, 4096], or the full sum of 2^28."""
+    rows, cols = 65536, 4096
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(2 + dist.rank)
+    X = torch.randn((rows, cols), device=dev, generator=g)
+    out = torch.empty(rows, device=dev)
+    idx = torch.empty(rows, dtype=torch.int32, device=dev)
+    if args.workload == "rowsum":
+        def step():
+            jx.reduce_axis(X.data_ptr(), out.data_ptr(), rows, cols, 1, "sum", s)
+        kern, bytes_step = "reduce_rows_kernel", 4.0 * rows * cols + 4.0 * rows
+    elif args.workload == "argmax":
+        def step():
+            jx.argreduce_rows(X.data_ptr(), idx.data_ptr(), None, rows, cols, True, s)
+        kern, bytes_step = "argreduce_rows_kernel", 4.0 * rows * cols + 4.0 * rows
+    else:
+        def step():
+            jx.reduce_all(X.data_ptr(), out.data_ptr(), rows * cols, "sum", s)
+        kern, bytes_step = "reduce_all_pass1", 4.0 * rows * cols
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
+    hbm, _, basis = load_peaks()
+    return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+            "config": {"workload": f"{args.workload} over [{rows}, {cols}] f32 per rank", "l2": "1 GiB input > L2"},
+            "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
+                         "traffic": None},
+            "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -334,7 +383,7 @@ def main():
     elif args.workload == "chain":
         line = run_chain(args, dist, jx, torch)
     else:
-        raise SystemExit(f"workload {args.workload} not wired into bench.py yet")
+        line = run_reduce(args, dist, jx, torch)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":
         tflops, dt = cpu_sgemm(args.size, args.cpu_rows, 1)
         line["cpu_baseline"] = {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",

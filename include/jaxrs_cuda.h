@@ -144,8 +144,10 @@ JX_API int jx_unary_f32(int op, const float *x, float *y, int64_t n, jx_stream_t
  * instruction is 4 int32 words {opcode, dst, src0, src1}; registers 0..nin-1
  * hold the inputs on entry; JX_OP_CONST loads consts[src0]; JX_OP_STORE writes
  * register src0 to output dst; registers 0..15 are usable.  The tape is
- * validated on creation (operands defined before use, every output stored) and copied
- * into the kernel's constant-bank parameter space on launch. */
+ * validated on creation (operands defined before use, every output stored).
+ * Each distinct op structure is turned into one straight-line kernel (NVRTC,
+ * sm_100a, cached per process and device); constants are passed in the
+ * launch's parameter block, i.e. the constant bank, on every run. */
 #define JX_OP_CONST 1
 #define JX_OP_STORE 2
 #define JX_OP_UNARY 16  /* opcode = 16 + JX_UN_* */
@@ -154,11 +156,21 @@ JX_API int jx_unary_f32(int op, const float *x, float *y, int64_t n, jx_stream_t
 #define JX_TAPE_MAX_INSTR 128
 #define JX_TAPE_MAX_REGS 16
 #define JX_TAPE_MAX_CONSTS 64
-#define JX_TAPE_MAX_IO 8
+#define JX_TAPE_MAX_IO 4
 typedef struct jx_tape jx_tape;
 JX_API int jx_tape_create(const int32_t *code, int n_instr, const float *consts, int n_consts, int n_inputs,
                    int n_outputs, jx_tape **out);
 JX_API int jx_tape_destroy(jx_tape *tape);
+/* Generates and compiles (NVRTC, sm_100a) the kernel for this tape's op
+ * structure on the current device, if the process has not already; the
+ * first jx_tape_run does the same implicitly.  Tapes that differ only in their
+ * constants share one compiled kernel. */
+JX_API int jx_tape_compile(const jx_tape *tape);
+/* The generated CUDA source of the tape's kernel (without the shared op
+ * definitions), NUL-terminated into buf[cap]; *len = bytes needed. */
+JX_API int jx_tape_source(const jx_tape *tape, char *buf, size_t cap, size_t *len);
+/* Generates and NVRTC-compiles the tape's kernel without loading it (needs no GPU). */
+JX_API int jx_tape_check(const jx_tape *tape);
 /* ins/outs: host arrays of device pointers, each of n elements. */
 JX_API int jx_tape_run(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
                 jx_stream_t stream);

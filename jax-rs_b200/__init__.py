@@ -69,6 +69,9 @@ _SIGS = {
     "jx_unary_f32": [ci, vp, vp, i64, vp],
     "jx_tape_create": [C.POINTER(C.c_int32), ci, C.POINTER(cf), ci, ci, ci, C.POINTER(vp)],
     "jx_tape_destroy": [vp],
+    "jx_tape_compile": [vp],
+    "jx_tape_source": [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
+    "jx_tape_check": [vp],
     "jx_tape_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
     "jx_reduce_all_f32": [vp, vp, i64, ci, vp],
     "jx_reduce_axis_f32": [vp, vp, i64, i64, i64, ci, vp],
@@ -202,6 +205,17 @@ class Tape:
         call("jx_tape_create", carr, len(code), karr, len(consts), n_inputs, n_outputs, C.byref(h))
         self.handle = h
         self.n_inputs, self.n_outputs = n_inputs, n_outputs
+
+    def source(self) -> str:
+        need = C.c_size_t(0)
+        call("jx_tape_source", self.handle, None, 0, C.byref(need))
+        buf = C.create_string_buffer(need.value)
+        call("jx_tape_source", self.handle, buf, need.value, C.byref(need))
+        return buf.value.decode()
+
+    def check(self):
+        """NVRTC-compiles the tape's kernel without a GPU (raises on failure)."""
+        call("jx_tape_check", self.handle)
 
     def run(self, ins, outs, n, stream=None):
         ia = (vp * max(len(ins), 1))(*ins)

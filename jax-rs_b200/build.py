@@ -53,10 +53,31 @@ def _stale(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def _write_tape_prelude():
+    """_build/tape_prelude.inc: the source every NVRTC-compiled op-tape kernel
+    starts with -- the JX_UN_*/JX_BIN_* codes of the C ABI header followed by
+    csrc/jx_math.cuh -- as a C++ string literal."""
+    import re
+    with open(os.path.join(HERE, "..", "include", "jaxrs_cuda.h")) as f:
+        hdr = f.read()
+    defines = re.findall(r"^#define (JX_(?:UN|BIN)_\w+) (\d+)", hdr, flags=re.M)
+    with open(os.path.join(CSRC, "jx_math.cuh")) as f:
+        math_src = f.read()
+    body = "".join(f"#define {k} {v}\n" for k, v in defines) + math_src + "\n"
+    out = os.path.join(BUILD, "tape_prelude.inc")
+    text = 'R"JXPRELUDE(' + body + ')JXPRELUDE"\n'
+    if not os.path.exists(out) or open(out).read() != text:
+        with open(out, "w") as f:
+            f.write(text)
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     inc, libdir = _nccl_flags()
-    hdrs = _headers()
+    inc = inc + ["-I" + BUILD]
+    _write_tape_prelude()
+    hdrs = _headers() + [os.path.join(BUILD, "tape_prelude.inc")]
     objs = []
     jobs = []
     for src in sources():
@@ -81,7 +102,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 if verbose and (r.stdout or r.stderr):
                     sys.stderr.write(r.stdout + r.stderr)
     if force or jobs or _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + libdir + ["-lnccl"] + LINK_LIBS
+        cuda_lib = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "lib64")
+        cmd = ([NVCC] + ARCH + ["-shared", "-o", LIB] + objs + libdir + ["-lnccl"] +
+               ["-L" + cuda_lib, "-lnvrtc", "-Xlinker", "-rpath," + cuda_lib] + LINK_LIBS)
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -81,3 +81,38 @@ def test_last_error_is_thread_local(jx):
     th.start()
     th.join()
     assert msg and seen == [""]
+
+
+def _chain_code(jx):
+    U, B = jx.OP_UNARY, jx.OP_BINARY
+    return [(jx.OP_CONST, 1, 0, 0), (jx.OP_CONST, 2, 1, 0), (jx.OP_CONST, 3, 2, 0),
+            (B + jx.BIN["mul"], 4, 0, 1), (B + jx.BIN["add"], 4, 4, 2), (U + jx.UN["gelu"], 4, 4, 0),
+            (U + jx.UN["sigmoid"], 5, 0, 0), (B + jx.BIN["mul"], 4, 4, 5), (U + jx.UN["tanh"], 5, 0, 0),
+            (B + jx.BIN["div"], 5, 5, 3), (B + jx.BIN["sub"], 4, 4, 5), (jx.OP_STORE, 0, 4, 0)]
+
+
+def test_tape_kernel_compiles_without_gpu(jx):
+    """The chain's generated kernel NVRTC-compiles for sm_100a (no GPU needed),
+    and division by the constant 2 became a multiplication by 0.5."""
+    t = jx.Tape(_chain_code(jx), [1.1, 0.9, 2.0], 1, 1)
+    src = t.source()
+    assert "jx_tape_kernel" in src and "jxm::unary_t<11>" in src
+    assert "binary_t<3>" not in src  # no division left
+    t.check()
+
+
+def test_every_op_compiles(jx):
+    """One tape touching every unary and binary op, in both operand orders."""
+    code = [(jx.OP_CONST, 2, 0, 0)]
+    r = 3
+    for name, u in jx.UN.items():
+        code.append((jx.OP_UNARY + u, r, 0, 0))
+        r = 3 if r == 12 else r + 1
+    for name, b in jx.BIN.items():
+        code.append((jx.OP_BINARY + b, r, 0, 1))
+        code.append((jx.OP_BINARY + b, r, 2, 0))
+    code.append((jx.OP_SELECT_GT, 13, 0, 1))
+    code.append((jx.OP_STORE, 0, 13, 0))
+    code.append((jx.OP_STORE, 1, r, 0))
+    t = jx.Tape(code, [0.5], 2, 2)
+    t.check()

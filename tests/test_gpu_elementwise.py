@@ -117,3 +117,121 @@ def test_binary_broadcast_bit_exact(jx, dev, oracle, op, sa, sb):
     jx.binary(op, A.data_ptr(), sa, B.data_ptr(), sb, O.data_ptr(), dev.stream)
     got = dev.get(O)
     assert np.array_equal(got, oracle.binary(op, a, b))
+
+
+SAFE_UN = ["neg", "abs", "tanh", "sigmoid", "relu", "square", "gelu"]
+SAFE_BIN = ["add", "sub", "mul", "min", "max"]
+
+
+def _emulate(oracle, code, consts, inputs, n_out):
+    """Runs a register-form tape with the oracle's per-op functions (f32)."""
+    regs = {i: x for i, x in enumerate(inputs)}
+    outs = [None] * n_out
+    for op, dst, s0, s1 in code:
+        if op == 1:
+            regs[dst] = np.full_like(inputs[0], consts[s0])
+        elif op == 2:
+            outs[dst] = regs[s0].copy()
+        elif op == 64:
+            regs[dst] = np.where(regs[s0] > 0, regs[s1], np.float32(0)).astype(np.float32)
+        elif op >= 48:
+            name = [k for k, v in oracle.BINOPS.items() if v == op - 48][0]
+            regs[dst] = oracle.binary(name, regs[s0], regs[s1])
+        else:
+            name = [k for k, v in oracle.UNOPS.items() if v == op - 16][0]
+            regs[dst] = oracle.unary(name, regs[s0])
+    return outs
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_tapes_vs_oracle(jx, dev, oracle, seed):
+    """Random straight-line tapes: value reuse, x op x, both operand orders,
+    constants, several inputs/outputs -- exercises the accumulator lowering."""
+    rng = np.random.default_rng(seed)
+    n_in = int(rng.integers(1, 5))
+    n_out = int(rng.integers(1, 4))
+    consts = [float(c) for c in rng.uniform(-2, 2, 4).astype(np.float32)]
+    defined = list(range(n_in))
+    code = []
+    for _ in range(int(rng.integers(4, 24))):
+        kind = rng.random()
+        dst = int(rng.integers(0, 12))
+        if kind < 0.1:
+            code.append((jx.OP_CONST, dst, int(rng.integers(0, 4)), 0))
+        elif kind < 0.45:
+            code.append((jx.OP_UNARY + jx.UN[SAFE_UN[rng.integers(len(SAFE_UN))]], dst,
+                         int(rng.choice(defined)), 0))
+        elif kind < 0.55:
+            code.append((jx.OP_SELECT_GT, dst, int(rng.choice(defined)), int(rng.choice(defined))))
+        else:
+            a = int(rng.choice(defined))
+            b = a if rng.random() < 0.2 else int(rng.choice(defined))
+            code.append((jx.OP_BINARY + jx.BIN[SAFE_BIN[rng.integers(len(SAFE_BIN))]], dst, a, b))
+        if dst not in defined:
+            defined.append(dst)
+    for j in range(n_out):
+        code.append((jx.OP_STORE, j, int(rng.choice(defined)), 0))
+    n = 4099
+    xs = [rng.standard_normal(n).astype(np.float32) for _ in range(n_in)]
+    try:
+        tape = jx.Tape(code, consts, n_in, n_out)
+    except jx.JaxRsError as e:
+        assert "live at once" in e.message  # legitimately too many live values
+        return
+    X = [dev.put(x) for x in xs]
+    Y = [dev.full((n,), np.nan) for _ in range(n_out)]
+    tape.run([t.data_ptr() for t in X], [t.data_ptr() for t in Y], n, dev.stream)
+    want = _emulate(oracle, code, consts, xs, n_out)
+    for j in range(n_out):
+        got = dev.get(Y[j])
+        assert _close(got, want[j]), (seed, j, code)
+
+
+def _ulp_grid():
+    xs = np.concatenate([np.linspace(-30, 30, 1 << 20, dtype=np.float32),
+                         np.logspace(-30, 1.4, 4096).astype(np.float32),
+                         -np.logspace(-30, 1.4, 4096).astype(np.float32),
+                         np.array([0.0, -0.0, 0.25, -0.25, 0.2499999, 88.0, -87.0, 1e-38], np.float32)])
+    return xs
+
+
+@pytest.mark.parametrize("op,rel,absol", [("exp", 1.5e-6, 0.0), ("tanh", 5e-6, 3e-7), ("sigmoid", 1.5e-6, 1e-30),
+                                          ("gelu", 5e-6, 3e-7)])
+def test_transcendental_error_bounds(jx, dev, oracle, op, rel, absol):
+    """exp/tanh/sigmoid/gelu on the multi-function unit against glibc (the
+    reference's libm): per element |d - o| <= rel*|o| + absol."""
+    x = _ulp_grid()
+    if op == "exp":
+        x = x[(x > -87.0) & (x < 88.0)]  # normal-range results (below 2^-126 flushes to zero)
+    X, Y = dev.put(x), dev.full(x.shape, np.nan)
+    jx.unary(op, X.data_ptr(), Y.data_ptr(), x.size, dev.stream)
+    y = dev.get(Y).astype(np.float64)
+    o = oracle.unary(op, x).astype(np.float64)
+    err = np.abs(y - o)
+    bound = rel * np.abs(o) + absol
+    worst = int(np.argmax(err - bound))
+    assert np.all(err <= bound), (op, float(x[worst]), y[worst], o[worst])
+
+
+def test_tanh_small_arguments_keep_relative_accuracy(jx, dev):
+    """Below |x| = 0.05 tanh uses its odd series: relative accuracy holds down
+    to the smallest inputs; above it the absolute error stays below 3e-7."""
+    x = np.array([1e-30, -1e-20, 1e-10, 3e-5, -0.01, 0.049, 0.1, -0.3, 2.0], np.float32)
+    X, Y = dev.put(x), dev.full(x.shape, np.nan)
+    jx.unary("tanh", X.data_ptr(), Y.data_ptr(), x.size, dev.stream)
+    y = dev.get(Y).astype(np.float64)
+    ref = np.tanh(x.astype(np.float64))
+    small = np.abs(x) < 0.05
+    np.testing.assert_allclose(y[small], ref[small], rtol=2e-7)
+    assert np.all(np.abs(y[~small] - ref[~small]) <= 3e-7)
+
+
+def test_div_by_power_of_two_constant_is_exact(jx, dev, oracle):
+    """x / 2 lowered to x * 0.5 must give the bits of the IEEE division."""
+    code = [(jx.OP_CONST, 1, 0, 0), (jx.OP_BINARY + jx.BIN["div"], 2, 0, 1), (jx.OP_STORE, 0, 2, 0)]
+    for c in (2.0, 0.25, -8.0, 3.0):
+        tape = jx.Tape(code, [c], 1, 1)
+        x = np.random.default_rng(1).standard_normal(1001).astype(np.float32) * 1e3
+        X, Y = dev.put(x), dev.full(x.shape, np.nan)
+        tape.run([X.data_ptr()], [Y.data_ptr()], x.size, dev.stream)
+        assert np.array_equal(dev.get(Y), (x / np.float32(c)).astype(np.float32))
