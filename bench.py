@@ -42,7 +42,11 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="sgemm", choices=["sgemm", "chain", "rowsum", "argmax", "fullsum"])
+    p.add_argument("--workload", default="sgemm",
+                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp"])
+    p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "exact"],
+                   help="GEMM precision of the MLP trainer")
+    p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -369,6 +373,132 @@ def run_reduce(args, dist, jx, torch):
             "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
 
 
+def run_mlp(args, dist, jx, torch):
+    """MLP training through the native trainer (jx_mlp_train_step).
+
+    mlp:      784-256-128-10 ReLU, batch 128, Adam; one GPU (replicas for N > 1).
+    wide_mlp: 8192 -> 4 x (8192 GELU) -> 1000, global batch split over the
+              ranks, gradients all-reduced per layer with NCCL (data parallel).
+    """
+    wide = args.workload == "wide_mlp"
+    if wide:
+        widths, acts = [8192, 8192, 8192, 8192, 8192, 1000], ["gelu"] * 4
+        gb = args.global_batch
+        assert gb % dist.world == 0, "global batch must divide by the rank count"
+        batch = gb // dist.world
+    else:
+        widths, acts, batch = [784, 256, 128, 10], ["relu", "relu"], 128
+        gb = batch * dist.world
+    prec = jx.PREC_EXACT if args.precision == "exact" else jx.PREC_3XTF32
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    net = jx.MLP(widths, acts, batch, prec)
+    rng = np.random.default_rng(1)  # identical initial parameters on every rank
+    Ws, bs = [], []
+    for l in range(len(widths) - 1):
+        fi, fo = widths[l], widths[l + 1]
+        if wide:  # He-normal
+            Ws.append((rng.standard_normal((fi, fo), dtype=np.float32) * np.float32(np.sqrt(2.0 / fi))))
+        else:  # Xavier-uniform
+            a = np.sqrt(6.0 / (fi + fo))
+            Ws.append(rng.uniform(-a, a, (fi, fo)).astype(np.float32))
+        bs.append(np.zeros(fo, np.float32))
+    net.set_params(net.pack(Ws, bs))
+    net.set_adam(1e-3, 0.9, 0.999, 1e-8)
+    comm = None
+    if dist.world > 1 and wide:
+        import ctypes as C
+        nid = jx.lib().jx_nccl_unique_id_size()
+        idb = (C.c_char * nid)()
+        if dist.rank == 0:
+            jx.call("jx_nccl_get_unique_id", idb)
+        obj = [bytes(idb)]
+        dist.pg.broadcast_object_list(obj, src=0)
+        idb = (C.c_char * nid).from_buffer_copy(obj[0])
+        comm = C.c_void_p()
+        jx.call("jx_nccl_init", idb, dist.world, dist.rank, 120000, C.byref(comm))
+        net.attach_comm(comm, dist.world, gb)
+    # a few pre-generated batches on the device, cycled through (inputs are
+    # per-step synthetic data; generating them is outside the timed region)
+    g = torch.Generator(device=dev)
+    g.manual_seed(100 + dist.rank)
+    nb = 4
+    X = [torch.randn((batch, widths[0]), device=dev, generator=g) for _ in range(nb)]
+    Y = [torch.randint(0, widths[-1], (batch,), device=dev, generator=g).float() for _ in range(nb)]
+    loss = torch.empty(1, device=dev)
+
+    def step(i):
+        net.step(X[i % nb].data_ptr(), Y[i % nb].data_ptr(), loss.data_ptr(), s)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    final_loss = float(loss.item())
+    samples = gb if wide else batch * dist.world
+    value = samples / (ms * 1e-3)
+    # e2e: per step, the batch comes from pinned host memory and the loss goes back
+    hx = torch.empty((batch, widths[0]), dtype=torch.float32).pin_memory()
+    hy = torch.empty((batch,), dtype=torch.float32).pin_memory()
+    hl = torch.empty((1,), dtype=torch.float32).pin_memory()
+    hx.copy_(X[0].cpu())
+    hy.copy_(Y[0].cpu())
+    e2e_steps = max(1, min(args.steps, 20 if not wide else 3))
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(e2e_steps):
+        jx.call("jx_memcpy_h2d", X[0].data_ptr(), hx.data_ptr(), hx.numel() * 4, s)
+        jx.call("jx_memcpy_h2d", Y[0].data_ptr(), hy.data_ptr(), hy.numel() * 4, s)
+        step(0)
+        jx.call("jx_memcpy_d2h", hl.data_ptr(), loss.data_ptr(), 4, s)
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(e0.elapsed_time(e1) / e2e_steps)
+    flops = 0.0
+    for l in range(len(widths) - 1):
+        flops += 3 * 2.0 * batch * widths[l] * widths[l + 1]  # fwd + dX + dW GEMMs
+    _, bf16, basis = load_peaks()
+    peak = bf16 / 2.0 / 3.0
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong" if wide else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic N(0,1) inputs, uniform integer labels (torch generator)",
+        "config": {"workload": ("wide MLP 8192-4x8192(GELU)-1000, softmax-CE, Adam, data parallel"
+                                if wide else "MLP 784-256(ReLU)-128(ReLU)-10, softmax-CE, Adam"),
+                   "global_batch": samples, "per_rank_batch": batch, "precision": args.precision,
+                   "parallelism": f"dp{dist.world}" + (" (NCCL per-layer gradient all-reduce)" if wide and
+                                                      dist.world > 1 else "")},
+        "final_loss": final_loss,
+        "roofline": {"bound": "tensor" if wide else "launch", "kernel": "whole training step",
+                     "achieved": round(flops / (ms * 1e-3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
+                     "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)", "traffic": None},
+        "e2e": {"value": round(samples / (e2e_ms * 1e-3), 1), "unit": "samples/s",
+                "h2d_bytes_per_step": (hx.numel() + hy.numel()) * 4, "d2h_bytes_per_step": 4,
+                "ms_per_step": round(e2e_ms, 4)},
+        "clocks": clocks,
+    }
+    if comm is not None:
+        torch.cuda.synchronize()
+        del net
+        jx.call("jx_nccl_destroy", comm)
+    return line
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -382,6 +512,8 @@ def main():
         line = run_sgemm(args, dist, jx, torch)
     elif args.workload == "chain":
         line = run_chain(args, dist, jx, torch)
+    elif args.workload in ("mlp", "wide_mlp"):
+        line = run_mlp(args, dist, jx, torch)
     else:
         line = run_reduce(args, dist, jx, torch)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":

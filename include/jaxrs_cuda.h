@@ -221,12 +221,15 @@ JX_API int jx_conv2d_bwd_filter_f32(const float *x, const float *dy, float *dw, 
 /* ---- nn / optim (src/nn.rs:155-221,300-318; src/optim.rs:138-189) -------- */
 /* y[r,:] = softmax(x[r,:]) (src/nn.rs:155-168 applied per row). */
 JX_API int jx_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols, jx_stream_t stream);
-/* Fused softmax + cross_entropy_loss (src/nn.rs:300-318: mean over rows*cols
- * elements, eps 1e-7) forward and backward.  labels are class indices (f32 as
- * randint returns them, one_hot src/nn.rs:205-221 semantics).  Writes probs
- * (may be NULL), dlogits = dL/dlogits, loss_out[0] (device scalar). */
+/* Fused softmax + cross_entropy_loss (src/nn.rs:300-318, eps 1e-7) forward and
+ * backward.  labels are class indices stored as f32, as randint returns them,
+ * with one_hot's semantics (src/nn.rs:205-221).  The loss is
+ * -sum(t*ln(p+eps)) / count, where the reference's count is rows*cols; a
+ * data-parallel caller passes the global element count so that summing the
+ * ranks' gradients gives the gradient of the global loss.  Writes probs (may be
+ * NULL), dlogits = dL/dlogits (may be NULL) and loss_out[0] (device scalar). */
 JX_API int jx_softmax_xent_f32(const float *logits, const float *labels, float *probs, float *dlogits,
-                        float *loss_out, int64_t rows, int64_t cols, jx_stream_t stream);
+                               float *loss_out, int64_t rows, int64_t cols, int64_t count, jx_stream_t stream);
 /* y[r,c] = act(y[r,c] + bias[c]); act: 0 none, 1 relu, 2 gelu (broadcast_to +
  * add src/ops/manipulation.rs:919-946, then src/nn.rs:22-26 / :111-122).
  * pre (may be NULL) receives the pre-activation. */
@@ -243,6 +246,31 @@ JX_API int jx_col_sum_f32(const float *dy, float *db, int64_t rows, int64_t cols
 JX_API int jx_adam_step_f32(float *const *params, const float *const *grads, float *const *m, float *const *v,
                      const int64_t *sizes, int count, float lr, float beta1, float beta2, float eps,
                      int64_t step, jx_stream_t stream);
+
+/* ---- Dense-stack trainer (examples/mlp_training.rs:94-145 trains with finite
+ *      differences + SGD; here: analytic backward, optim::adam_update
+ *      src/optim.rs:138-189, Array::matmul + broadcast bias + nn activations) --
+ * widths[0..n_layers]; acts[l] (0 none, 1 relu, 2 gelu) for hidden layers
+ * l < n_layers-1; the last layer feeds fused softmax cross-entropy.  Params
+ * are one flat f32 vector [W1, b1, W2, b2, ...], W row-major [in, out], each
+ * block starting at the offsets jx_mlp_param_offsets reports. */
+typedef struct jx_mlp jx_mlp;
+JX_API int jx_mlp_create(const int64_t *widths, int n_layers, const int *acts, int64_t batch, int precision,
+                         jx_mlp **out);
+JX_API int jx_mlp_param_count(const jx_mlp *mlp, int64_t *count);
+JX_API int jx_mlp_param_offsets(const jx_mlp *mlp, int64_t *w_off, int64_t *b_off);
+JX_API int jx_mlp_set_params(jx_mlp *mlp, const float *host_params, int64_t count);
+JX_API int jx_mlp_get_params(const jx_mlp *mlp, float *host_params, int64_t count);
+/* Resets the optimiser state (adam_init) and sets its hyper-parameters. */
+JX_API int jx_mlp_set_adam(jx_mlp *mlp, float lr, float beta1, float beta2, float eps);
+/* Data parallel: gradients are summed over the communicator's ranks; the loss
+ * is normalised by the global batch (global_batch = batch * world). */
+JX_API int jx_mlp_attach_comm(jx_mlp *mlp, void *comm, int world, int64_t global_batch);
+/* One step: forward, backward, (all-reduce), Adam.  x [batch, widths[0]] and
+ * labels [batch] are device pointers; loss_out (device scalar) may be NULL. */
+JX_API int jx_mlp_train_step(jx_mlp *mlp, const float *x, const float *labels, float *loss_out,
+                             jx_stream_t stream);
+JX_API int jx_mlp_destroy(jx_mlp *mlp);
 
 /* ---- data-parallel collectives (no reference counterpart: the reference has
  *      a single global device, src/backend/webgpu.rs:6) -------------------- */

@@ -84,12 +84,21 @@ _SIGS = {
     "jx_conv2d_bwd_data_f32": [vp, vp, vp] + [i64] * 9 + [vp],
     "jx_conv2d_bwd_filter_f32": [vp, vp, vp] + [i64] * 9 + [vp],
     "jx_softmax_rows_f32": [vp, vp, i64, i64, vp],
-    "jx_softmax_xent_f32": [vp, vp, vp, vp, vp, i64, i64, vp],
+    "jx_softmax_xent_f32": [vp, vp, vp, vp, vp, i64, i64, i64, vp],
     "jx_bias_act_f32": [vp, vp, vp, i64, i64, ci, vp],
     "jx_act_bwd_f32": [vp, vp, vp, vp, i64, i64, ci, vp],
     "jx_col_sum_f32": [vp, vp, i64, i64, vp],
     "jx_adam_step_f32": [C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(i64), ci,
                          cf, cf, cf, cf, i64, vp],
+    "jx_mlp_create": [C.POINTER(i64), ci, C.POINTER(ci), i64, ci, C.POINTER(vp)],
+    "jx_mlp_param_count": [vp, C.POINTER(i64)],
+    "jx_mlp_param_offsets": [vp, C.POINTER(i64), C.POINTER(i64)],
+    "jx_mlp_set_params": [vp, vp, i64],
+    "jx_mlp_get_params": [vp, vp, i64],
+    "jx_mlp_set_adam": [vp, cf, cf, cf, cf],
+    "jx_mlp_attach_comm": [vp, vp, ci, i64],
+    "jx_mlp_train_step": [vp, vp, vp, vp, vp],
+    "jx_mlp_destroy": [vp],
     "jx_nccl_unique_id_size": [],
     "jx_nccl_get_unique_id": [vp],
     "jx_nccl_init": [vp, ci, ci, ci, C.POINTER(vp)],
@@ -256,3 +265,70 @@ def fft_c2c(x, y, n, batch, inverse=False, stream=None):
 
 def fft2_c2c(x, y, h, w, batch, inverse=False, stream=None):
     call("jx_fft2_c2c_f32", x, y, h, w, batch, int(inverse), stream)
+
+
+class MLP:
+    """Native Dense-stack trainer (jx_mlp_*): widths [d0, d1, ..., dL], hidden
+    activations ('relu' | 'gelu' | 'none'), softmax cross-entropy, Adam."""
+
+    ACTS = {"none": 0, "relu": 1, "gelu": 2}
+
+    def __init__(self, widths, acts, batch, precision=PREC_3XTF32):
+        w = (i64 * len(widths))(*widths)
+        a = (ci * max(len(acts), 1))(*[self.ACTS[x] for x in acts] or [0])
+        h = vp()
+        call("jx_mlp_create", w, len(widths) - 1, a, batch, precision, C.byref(h))
+        self.handle = h
+        self.widths = list(widths)
+        self.batch = batch
+        n = i64(0)
+        call("jx_mlp_param_count", h, C.byref(n))
+        self.nparams = n.value
+        L = len(widths) - 1
+        wo, bo = (i64 * L)(), (i64 * L)()
+        call("jx_mlp_param_offsets", h, wo, bo)
+        self.w_off, self.b_off = list(wo), list(bo)
+
+    def pack(self, weights, biases):
+        """Flat parameter vector from per-layer W [in, out] and b [out] (numpy)."""
+        import numpy as np
+        flat = np.zeros(self.nparams, np.float32)
+        for l, (W, b) in enumerate(zip(weights, biases)):
+            flat[self.w_off[l]:self.w_off[l] + W.size] = np.asarray(W, np.float32).ravel()
+            flat[self.b_off[l]:self.b_off[l] + b.size] = np.asarray(b, np.float32).ravel()
+        return flat
+
+    def unpack(self, flat):
+        Ws, bs = [], []
+        for l in range(len(self.widths) - 1):
+            i, o = self.widths[l], self.widths[l + 1]
+            Ws.append(flat[self.w_off[l]:self.w_off[l] + i * o].reshape(i, o))
+            bs.append(flat[self.b_off[l]:self.b_off[l] + o])
+        return Ws, bs
+
+    def set_params(self, flat):
+        import numpy as np
+        flat = np.ascontiguousarray(flat, np.float32)
+        call("jx_mlp_set_params", self.handle, flat.ctypes.data, flat.size)
+
+    def get_params(self):
+        import numpy as np
+        out = np.empty(self.nparams, np.float32)
+        call("jx_mlp_get_params", self.handle, out.ctypes.data, out.size)
+        return out
+
+    def set_adam(self, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8):
+        call("jx_mlp_set_adam", self.handle, lr, b1, b2, eps)
+
+    def attach_comm(self, comm, world, global_batch):
+        call("jx_mlp_attach_comm", self.handle, comm, world, global_batch)
+
+    def step(self, x, labels, loss_out=None, stream=None):
+        call("jx_mlp_train_step", self.handle, x, labels, loss_out, stream)
+
+    def __del__(self):
+        try:
+            if self.handle and _lib is not None:
+                _lib.jx_mlp_destroy(self.handle)
+        except Exception:
+            pass

@@ -1,0 +1,140 @@
+// dp.cu -- NCCL plumbing for data-parallel training (no reference counterpart:
+// jax-rs has one global device, src/backend/webgpu.rs:6).
+//
+// Communicators are created non-blocking and every wait is bounded: init and
+// collectives poll ncclCommGetAsyncError, and when the host watchdog's limit
+// passes the communicator is aborted and the call returns JX_ETIMEOUT, so a
+// rank that never joins ends the others' calls with an error, not a hang.
+#include <nccl.h>
+
+#include <chrono>
+#include <thread>
+
+#include "jx_common.cuh"
+
+namespace {
+
+int nccl_fail(ncclResult_t r, const char* what) {
+  return jx::fail(JX_ENCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+
+struct Comm {
+  ncclComm_t comm;
+  int timeout_ms;
+};
+
+// Polls the communicator until its pending operation leaves ncclInProgress.
+int wait_comm(Comm* c, int timeout_ms, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    ncclResult_t st;
+    ncclResult_t r = ncclCommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) return nccl_fail(r, what);
+    if (st == ncclSuccess) return JX_OK;
+    if (st != ncclInProgress) return nccl_fail(st, what);
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > timeout_ms) {
+      ncclCommAbort(c->comm);
+      c->comm = nullptr;
+      return jx::fail(JX_ETIMEOUT, "%s: no progress within %d ms; communicator aborted", what, timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+}  // namespace
+
+namespace jx {
+// Used by the trainer: enqueue an in-place sum all-reduce on `st`.
+int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  JX_REQUIRE(c && c->comm, "allreduce: communicator is NULL or was aborted");
+  ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, c->comm, st);
+  if (r == ncclInProgress) return wait_comm(c, c->timeout_ms, "ncclAllReduce");
+  if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+  return JX_OK;
+}
+}  // namespace jx
+
+extern "C" {
+
+int jx_nccl_unique_id_size(void) { return (int)sizeof(ncclUniqueId); }
+
+int jx_nccl_get_unique_id(void* id_out) {
+  JX_REQUIRE(id_out, "jx_nccl_get_unique_id: NULL");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  memcpy(id_out, &id, sizeof(id));
+  return JX_OK;
+}
+
+int jx_nccl_init(const void* id, int nranks, int rank, int timeout_ms, void** comm_out) {
+  JX_REQUIRE(id && comm_out, "jx_nccl_init: NULL argument");
+  JX_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, "jx_nccl_init: rank %d of %d", rank, nranks);
+  JX_REQUIRE(timeout_ms > 0, "jx_nccl_init: timeout must be positive");
+  *comm_out = nullptr;
+  Comm* c = new Comm();
+  c->timeout_ms = timeout_ms;
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = ncclCommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    delete c;
+    return nccl_fail(r, "ncclCommInitRankConfig");
+  }
+  int rc = wait_comm(c, timeout_ms, "ncclCommInitRankConfig");
+  if (rc) {
+    if (c->comm) ncclCommAbort(c->comm);
+    delete c;
+    return rc;
+  }
+  *comm_out = c;
+  return JX_OK;
+}
+
+int jx_nccl_allreduce_sum_f32(void* comm, float* buf, int64_t count, jx_stream_t stream) {
+  JX_REQUIRE(count >= 0, "allreduce: negative count");
+  if (count == 0) return JX_OK;
+  JX_REQUIRE(buf, "allreduce: NULL buffer");
+  return jx::nccl_allreduce(comm, buf, count, jx::as_stream(stream));
+}
+
+int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  JX_REQUIRE(c && c->comm, "jx_nccl_wait: communicator is NULL or was aborted");
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaStreamQuery(jx::as_stream(stream));
+    if (q == cudaSuccess) return JX_OK;
+    if (q != cudaErrorNotReady) return jx::check_cuda(q, "jx_nccl_wait: cudaStreamQuery");
+    ncclResult_t st;
+    ncclCommGetAsyncError(c->comm, &st);
+    if (st != ncclSuccess && st != ncclInProgress) return nccl_fail(st, "jx_nccl_wait");
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() > timeout_ms) {
+      ncclCommAbort(c->comm);
+      c->comm = nullptr;
+      return jx::fail(JX_ETIMEOUT, "jx_nccl_wait: stream not done within %d ms; communicator aborted", timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+int jx_nccl_destroy(void* comm) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  if (!c) return JX_OK;
+  int rc = JX_OK;
+  if (c->comm) {
+    ncclResult_t r = ncclCommFinalize(c->comm);
+    if (r == ncclInProgress) rc = wait_comm(c, c->timeout_ms, "ncclCommFinalize");
+    else if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommFinalize");
+    if (c->comm) ncclCommDestroy(c->comm);
+  }
+  delete c;
+  return rc;
+}
+
+}  // extern "C"

@@ -461,6 +461,13 @@ int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float
   return gemm_presplit_err(Ah, Al, Bh, Bl, C, M, N, Kp, ldc, strideC, batch, st, device_error_word());
 }
 
+// Sets the main kernel's shared-memory limit on the current device once, up
+// front (jx_init), so no later call -- e.g. one inside a stream capture -- has to.
+int gemm_prepare() {
+  JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+  return JX_OK;
+}
+
 int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
                        int batch, bool transposed, cudaStream_t st) {
   return launch_split(src, hi, lo, rows, K, Kp, ld, sb, batch, transposed, st);

@@ -11,6 +11,7 @@
 
 namespace jx {
 
+int gemm_prepare();
 static thread_local std::string g_last_error;
 
 void set_error(const char* fmt, ...) {
@@ -131,6 +132,7 @@ int jx_init(int device) {
   }
   (void)num_sms();
   if (!device_error_word()) return fail(JX_ENOMEM, "jx_init: cannot allocate the device error word");
+  if (int rc = gemm_prepare()) return rc;
   return JX_OK;
 }
 
