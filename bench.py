@@ -43,7 +43,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp"])
+                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d"])
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer")
     p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
@@ -373,6 +373,60 @@ def run_reduce(args, dist, jx, torch):
             "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
 
 
+def run_fft(args, dist, jx, torch):
+    """Batched complex FFTs: 1-D n=4096 x 65536, or 2-D 1024x1024 x 256 per rank."""
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(3 + dist.rank)
+    if args.workload == "fft1d":
+        n, batch = 4096, 65536
+        X = torch.randn((batch, n, 2), device=dev, generator=g)
+        Y = torch.empty_like(X)
+
+        def step():
+            jx.fft_c2c(X.data_ptr(), Y.data_ptr(), n, batch, False, s)
+        wl, kern, launches = f"1-D complex FFT n={n} x batch {batch} per rank (2 GiB in, 2 GiB out)", "fft_kernel", 1
+    else:
+        h = w = 1024
+        batch = 256
+        X = torch.randn((batch, h, w, 2), device=dev, generator=g)
+        Y = torch.empty_like(X)
+
+        def step():
+            jx.fft2_c2c(X.data_ptr(), Y.data_ptr(), h, w, batch, False, s)
+        wl, kern, launches = f"2-D complex FFT {h}x{w} x batch {batch} per rank (rows, then columns)", "fft_kernel", 2
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    nbytes = 2.0 * X.numel() * 4  # algorithmic: one read and one write of the batch
+    gbs = nbytes * dist.world / (ms * 1e-3) / 1e9
+    hbm, _, basis = load_peaks()
+    return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (complex64)", "data": "synthetic N(0,1) real and imaginary parts",
+            "config": {"workload": wl, "l2": "2 GiB per pass > L2",
+                       "parallelism": f"batch shards x{dist.world}, no collective"},
+            "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
+                         "traffic": None,
+                         "note": "2-D counts one read + one write; the row and column passes move it twice"
+                         if launches == 2 else ""},
+            "gpu_launches": args.steps * launches, "clocks": clocks}
+
+
 def run_mlp(args, dist, jx, torch):
     """MLP training through the native trainer (jx_mlp_train_step).
 
@@ -514,6 +568,8 @@ def main():
         line = run_chain(args, dist, jx, torch)
     elif args.workload in ("mlp", "wide_mlp"):
         line = run_mlp(args, dist, jx, torch)
+    elif args.workload in ("fft1d", "fft2d"):
+        line = run_fft(args, dist, jx, torch)
     else:
         line = run_reduce(args, dist, jx, torch)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":

@@ -103,7 +103,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                     sys.stderr.write(r.stdout + r.stderr)
     if force or jobs or _stale(LIB, objs):
         cuda_lib = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "lib64")
-        cmd = ([NVCC] + ARCH + ["-shared", "-o", LIB] + objs + libdir + ["-lnccl"] +
+        cmd = ([NVCC] + ARCH + ["-shared", "-o", LIB] + objs +
                ["-L" + cuda_lib, "-lnvrtc", "-Xlinker", "-rpath," + cuda_lib] + LINK_LIBS)
         if verbose:
             print(" ".join(cmd), flush=True)

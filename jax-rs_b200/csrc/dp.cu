@@ -5,17 +5,67 @@
 // collectives poll ncclCommGetAsyncError, and when the host watchdog's limit
 // passes the communicator is aborted and the call returns JX_ETIMEOUT, so a
 // rank that never joins ends the others' calls with an error, not a hang.
+//
+// NCCL is resolved at first use with dlopen/dlsym, preferring a libnccl.so.2
+// the process has already loaded (e.g. the one torch ships), so loading this
+// library never pins a different NCCL than the rest of the process uses.
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <chrono>
+#include <mutex>
 #include <thread>
 
 #include "jx_common.cuh"
 
 namespace {
 
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*);
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
+  ncclResult_t (*CommAbort)(ncclComm_t);
+  ncclResult_t (*CommFinalize)(ncclComm_t);
+  ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  const char* (*GetErrorString)(ncclResult_t);
+  bool ok;
+};
+NcclApi g_nccl;
+std::once_flag g_nccl_once;
+
+const NcclApi* nccl() {
+  std::call_once(g_nccl_once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    bool ok = true;
+    auto sym = [&](const char* name) {
+      void* f = dlsym(h, name);
+      ok = ok && f != nullptr;
+      return f;
+    };
+    g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(sym("ncclGetUniqueId"));
+    g_nccl.CommInitRankConfig = reinterpret_cast<decltype(g_nccl.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
+    g_nccl.CommGetAsyncError = reinterpret_cast<decltype(g_nccl.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+    g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(sym("ncclCommAbort"));
+    g_nccl.CommFinalize = reinterpret_cast<decltype(g_nccl.CommFinalize)>(sym("ncclCommFinalize"));
+    g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
+    g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(sym("ncclAllReduce"));
+    g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
+    g_nccl.ok = ok;
+  });
+  return g_nccl.ok ? &g_nccl : nullptr;
+}
+
+#define JX_NCCL_API(api)                                                              \
+  const NcclApi* api = nccl();                                                        \
+  if (!api) return jx::fail(JX_ENCCL, "NCCL (libnccl.so.2) could not be loaded");
+
 int nccl_fail(ncclResult_t r, const char* what) {
-  return jx::fail(JX_ENCCL, "%s: %s", what, ncclGetErrorString(r));
+  const NcclApi* api = nccl();
+  return jx::fail(JX_ENCCL, "%s: %s", what, api ? api->GetErrorString(r) : "NCCL unavailable");
 }
 
 struct Comm {
@@ -25,16 +75,17 @@ struct Comm {
 
 // Polls the communicator until its pending operation leaves ncclInProgress.
 int wait_comm(Comm* c, int timeout_ms, const char* what) {
+  JX_NCCL_API(api);
   const auto t0 = std::chrono::steady_clock::now();
   while (true) {
     ncclResult_t st;
-    ncclResult_t r = ncclCommGetAsyncError(c->comm, &st);
+    ncclResult_t r = api->CommGetAsyncError(c->comm, &st);
     if (r != ncclSuccess) return nccl_fail(r, what);
     if (st == ncclSuccess) return JX_OK;
     if (st != ncclInProgress) return nccl_fail(st, what);
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
     if (ms.count() > timeout_ms) {
-      ncclCommAbort(c->comm);
+      api->CommAbort(c->comm);
       c->comm = nullptr;
       return jx::fail(JX_ETIMEOUT, "%s: no progress within %d ms; communicator aborted", what, timeout_ms);
     }
@@ -47,9 +98,10 @@ int wait_comm(Comm* c, int timeout_ms, const char* what) {
 namespace jx {
 // Used by the trainer: enqueue an in-place sum all-reduce on `st`.
 int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st) {
+  JX_NCCL_API(api);
   Comm* c = reinterpret_cast<Comm*>(comm);
   JX_REQUIRE(c && c->comm, "allreduce: communicator is NULL or was aborted");
-  ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, c->comm, st);
+  ncclResult_t r = api->AllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, c->comm, st);
   if (r == ncclInProgress) return wait_comm(c, c->timeout_ms, "ncclAllReduce");
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
   return JX_OK;
@@ -62,8 +114,9 @@ int jx_nccl_unique_id_size(void) { return (int)sizeof(ncclUniqueId); }
 
 int jx_nccl_get_unique_id(void* id_out) {
   JX_REQUIRE(id_out, "jx_nccl_get_unique_id: NULL");
+  JX_NCCL_API(api);
   ncclUniqueId id;
-  ncclResult_t r = ncclGetUniqueId(&id);
+  ncclResult_t r = api->GetUniqueId(&id);
   if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
   memcpy(id_out, &id, sizeof(id));
   return JX_OK;
@@ -74,20 +127,21 @@ int jx_nccl_init(const void* id, int nranks, int rank, int timeout_ms, void** co
   JX_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, "jx_nccl_init: rank %d of %d", rank, nranks);
   JX_REQUIRE(timeout_ms > 0, "jx_nccl_init: timeout must be positive");
   *comm_out = nullptr;
+  JX_NCCL_API(api);
   Comm* c = new Comm();
   c->timeout_ms = timeout_ms;
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
   ncclUniqueId uid;
   memcpy(&uid, id, sizeof(uid));
-  ncclResult_t r = ncclCommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  ncclResult_t r = api->CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
     delete c;
     return nccl_fail(r, "ncclCommInitRankConfig");
   }
   int rc = wait_comm(c, timeout_ms, "ncclCommInitRankConfig");
   if (rc) {
-    if (c->comm) ncclCommAbort(c->comm);
+    if (c->comm) api->CommAbort(c->comm);
     delete c;
     return rc;
   }
@@ -103,6 +157,7 @@ int jx_nccl_allreduce_sum_f32(void* comm, float* buf, int64_t count, jx_stream_t
 }
 
 int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
+  JX_NCCL_API(api);
   Comm* c = reinterpret_cast<Comm*>(comm);
   JX_REQUIRE(c && c->comm, "jx_nccl_wait: communicator is NULL or was aborted");
   const auto t0 = std::chrono::steady_clock::now();
@@ -111,11 +166,11 @@ int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
     if (q == cudaSuccess) return JX_OK;
     if (q != cudaErrorNotReady) return jx::check_cuda(q, "jx_nccl_wait: cudaStreamQuery");
     ncclResult_t st;
-    ncclCommGetAsyncError(c->comm, &st);
+    api->CommGetAsyncError(c->comm, &st);
     if (st != ncclSuccess && st != ncclInProgress) return nccl_fail(st, "jx_nccl_wait");
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
     if (ms.count() > timeout_ms) {
-      ncclCommAbort(c->comm);
+      api->CommAbort(c->comm);
       c->comm = nullptr;
       return jx::fail(JX_ETIMEOUT, "jx_nccl_wait: stream not done within %d ms; communicator aborted", timeout_ms);
     }
@@ -126,12 +181,13 @@ int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
 int jx_nccl_destroy(void* comm) {
   Comm* c = reinterpret_cast<Comm*>(comm);
   if (!c) return JX_OK;
+  JX_NCCL_API(api);
   int rc = JX_OK;
   if (c->comm) {
-    ncclResult_t r = ncclCommFinalize(c->comm);
+    ncclResult_t r = api->CommFinalize(c->comm);
     if (r == ncclInProgress) rc = wait_comm(c, c->timeout_ms, "ncclCommFinalize");
     else if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommFinalize");
-    if (c->comm) ncclCommDestroy(c->comm);
+    if (c->comm) api->CommDestroy(c->comm);
   }
   delete c;
   return rc;

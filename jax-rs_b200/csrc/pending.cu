@@ -6,8 +6,6 @@
 #define JX_PENDING(name) return jx::fail(JX_EUNSUPPORTED, name ": not available in this build")
 
 extern "C" {
-int jx_fft_c2c_f32(const float*, float*, int64_t, int64_t, int, jx_stream_t) { JX_PENDING("jx_fft_c2c_f32"); }
-int jx_fft2_c2c_f32(const float*, float*, int64_t, int64_t, int64_t, int, jx_stream_t) { JX_PENDING("jx_fft2_c2c_f32"); }
 int jx_conv2d_fwd_f32(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                       int64_t, int64_t, int64_t, jx_stream_t) { JX_PENDING("jx_conv2d_fwd_f32"); }
 int jx_conv2d_bwd_data_f32(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t,
