@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                        float* __restrict__ C, int M, int N, int Kp, long long ldc, long long strideC,
-                       int tiles_m, int tiles_n, int num_tiles, unsigned int* err) {
+                       int tiles_m, int tiles_n, int num_tiles, int a_bcast, int b_bcast, unsigned int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = jxd::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -144,10 +144,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* st = smem + stage * STAGE_BYTES;
           jxd::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           const int x = kb * BK;
-          jxd::tma_load_3d(st, &tmAh, &full[stage], x, ya, ti.b);
-          jxd::tma_load_3d(st + A_TILE, &tmAl, &full[stage], x, ya, ti.b);
-          jxd::tma_load_3d(st + 2 * A_TILE, &tmBh, &full[stage], x, yb, ti.b);
-          jxd::tma_load_3d(st + 2 * A_TILE + B_TILE, &tmBl, &full[stage], x, yb, ti.b);
+          const int za = a_bcast ? 0 : ti.b, zb = b_bcast ? 0 : ti.b;  // a broadcast operand has one batch entry
+          jxd::tma_load_3d(st, &tmAh, &full[stage], x, ya, za);
+          jxd::tma_load_3d(st + A_TILE, &tmAl, &full[stage], x, ya, za);
+          jxd::tma_load_3d(st + 2 * A_TILE, &tmBh, &full[stage], x, yb, zb);
+          jxd::tma_load_3d(st + 2 * A_TILE + B_TILE, &tmBl, &full[stage], x, yb, zb);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -268,15 +269,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //   direct:     element (r, k) at src[b*sb + r*ld + k]
 //   transposed: element (r, k) at src[b*sb + k*ld + r]
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-  uint32_t h;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-  hi = __uint_as_float(h);
-  float rem = __fsub_rn(x, hi);
-  uint32_t l;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(rem));
-  lo = __uint_as_float(l);
-}
+using jxd::split_tf32;
 
 __global__ void split_direct_kernel(const float* __restrict__ src, float* __restrict__ hi,
                                     float* __restrict__ lo, int rows, int K, int Kp, long long ld,
@@ -430,15 +423,18 @@ namespace jx {
 // Shared by conv2d (implicit GEMM) and the dense layers: 3xTF32 GEMM on
 // pre-split K-major operands.  Ah/Al: [batch][M][Kp]; Bh/Bl: [batch][N][Kp].
 // Launches the main kernel; `err` is the device word it flags a timed-out wait in.
+// a_bcast / b_bcast: that operand has a single batch entry shared by every
+// batch entry of the other (conv2d's weights).
 int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
-                      int Kp, long long ldc, long long strideC, int batch, cudaStream_t st, unsigned int* err) {
+                      int Kp, long long ldc, long long strideC, int batch, cudaStream_t st, unsigned int* err,
+                      bool a_bcast, bool b_bcast) {
   int rc = get_encode();
   if (rc) return rc;
   CUtensorMap mAh, mAl, mBh, mBl;
-  if ((rc = make_kmajor_map(&mAh, Ah, Kp, M, batch, BM))) return rc;
-  if ((rc = make_kmajor_map(&mAl, Al, Kp, M, batch, BM))) return rc;
-  if ((rc = make_kmajor_map(&mBh, Bh, Kp, N, batch, BN))) return rc;
-  if ((rc = make_kmajor_map(&mBl, Bl, Kp, N, batch, BN))) return rc;
+  if ((rc = make_kmajor_map(&mAh, Ah, Kp, M, a_bcast ? 1 : batch, BM))) return rc;
+  if ((rc = make_kmajor_map(&mAl, Al, Kp, M, a_bcast ? 1 : batch, BM))) return rc;
+  if ((rc = make_kmajor_map(&mBh, Bh, Kp, N, b_bcast ? 1 : batch, BN))) return rc;
+  if ((rc = make_kmajor_map(&mBl, Bl, Kp, N, b_bcast ? 1 : batch, BN))) return rc;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -451,14 +447,14 @@ int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const f
   if (nt > 0x7fffffffLL) return fail(JX_EINVAL, "gemm: too many tiles");
   const int grid = (int)std::min<long long>(nt, num_sms());
   gemm_3xtf32_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(mAh, mAl, mBh, mBl, C, M, N, Kp, ldc, strideC, tiles_m,
-                                                          tiles_n, (int)nt, err);
+                                                          tiles_n, (int)nt, a_bcast ? 1 : 0, b_bcast ? 1 : 0, err);
   JX_LAUNCH_CHECK("gemm_3xtf32_kernel");
   return JX_OK;
 }
 
 int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
                   int Kp, long long ldc, long long strideC, int batch, cudaStream_t st) {
-  return gemm_presplit_err(Ah, Al, Bh, Bl, C, M, N, Kp, ldc, strideC, batch, st, device_error_word());
+  return gemm_presplit_err(Ah, Al, Bh, Bl, C, M, N, Kp, ldc, strideC, batch, st, device_error_word(), false, false);
 }
 
 // Sets the main kernel's shared-memory limit on the current device once, up
@@ -645,6 +641,8 @@ extern "C" int jx_gemm_f32_noalloc(const float* A, const float* B, float* C, int
   float* Bl = Bh + (size_t)batch * N * Kp;
   rc = launch_split(A, Ah, Al, (int)M, (int)K, (int)Kp, lda, strideA, (int)batch, transA != 0, st);
   if (!rc) rc = launch_split(B, Bh, Bl, (int)N, (int)K, (int)Kp, ldb, strideB, (int)batch, transB == 0, st);
-  if (!rc) rc = jx::gemm_presplit_err(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st, err);
+  if (!rc)
+    rc = jx::gemm_presplit_err(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st, err, false,
+                               false);
   return rc;
 }
