@@ -43,10 +43,12 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d"])
+                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
+                            "conv", "bgemm"])
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer")
     p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
+    p.add_argument("--fft-batch", type=int, default=0, help="override the FFT batch (smaller cases for profiling)")
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -373,6 +375,67 @@ def run_reduce(args, dist, jx, torch):
             "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
 
 
+def run_conv_bgemm(args, dist, jx, torch):
+    """conv: [64,256,56,56] x [256,256,3,3] stride 1 pad 1, forward + dX + dW per step.
+    bgemm: batched [64,2048,2048] x [64,2048,2048] (einsum bij,bjk->bik)."""
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(3 + dist.rank)
+    if args.workload == "conv":
+        B, C, H, W, O, K = 64, 256, 56, 56, 256, 3
+        geo = (B, C, H, W, O, K, K, 1, 1)
+        X = torch.randn((B, C, H, W), device=dev, generator=g)
+        Wt = torch.randn((O, C, K, K), device=dev, generator=g) * float(np.sqrt(2.0 / (C * K * K)))
+        G = torch.randn((B, O, H, W), device=dev, generator=g)
+        Y, DX, DW = torch.empty_like(G), torch.empty_like(X), torch.empty_like(Wt)
+
+        def step():
+            jx.call("jx_conv2d_fwd_f32", X.data_ptr(), Wt.data_ptr(), Y.data_ptr(), *geo, s)
+            jx.call("jx_conv2d_bwd_data_f32", G.data_ptr(), Wt.data_ptr(), DX.data_ptr(), *geo, s)
+            jx.call("jx_conv2d_bwd_filter_f32", X.data_ptr(), G.data_ptr(), DW.data_ptr(), *geo, s)
+        flops = 3 * 2.0 * B * O * C * K * K * H * W
+        wl = "conv2d [64,256,56,56] x [256,256,3,3] s1 p1: forward + input grad + weight grad per step"
+    else:
+        nb, n = 64, 2048
+        A = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)
+        Bm = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)
+        Cm = torch.empty((nb, n, n), device=dev)
+
+        def step():
+            jx.gemm(A.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), n, n, n, batch=nb, strideA=n * n, strideB=n * n,
+                    strideC=n * n, stream=s)
+        flops = 2.0 * nb * n ** 3
+        wl = "batched sgemm [64,2048,2048] x [64,2048,2048] per rank (einsum bij,bjk->bik), JX_PREC_3XTF32"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    tf = flops * dist.world / (ms * 1e-3) / 1e12
+    _, bf16, basis = load_peaks()
+    peak = bf16 / 2.0 / 3.0
+    return {"metric": METRIC, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": wl,
+                                                                                 "parallelism": f"batch shards x{dist.world}"},
+            "roofline": {"bound": "tensor", "kernel": "whole step (operand producers + gemm_3xtf32_kernel)",
+                         "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                         "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
+                         "traffic": None},
+            "clocks": clocks}
+
+
 def run_fft(args, dist, jx, torch):
     """Batched complex FFTs: 1-D n=4096 x 65536, or 2-D 1024x1024 x 256 per rank."""
     dev = torch.device("cuda", dist.local)
@@ -381,7 +444,7 @@ def run_fft(args, dist, jx, torch):
     g = torch.Generator(device=dev)
     g.manual_seed(3 + dist.rank)
     if args.workload == "fft1d":
-        n, batch = 4096, 65536
+        n, batch = 4096, args.fft_batch or 65536
         X = torch.randn((batch, n, 2), device=dev, generator=g)
         Y = torch.empty_like(X)
 
@@ -390,7 +453,7 @@ def run_fft(args, dist, jx, torch):
         wl, kern, launches = f"1-D complex FFT n={n} x batch {batch} per rank (2 GiB in, 2 GiB out)", "fft_kernel", 1
     else:
         h = w = 1024
-        batch = 256
+        batch = args.fft_batch or 256
         X = torch.randn((batch, h, w, 2), device=dev, generator=g)
         Y = torch.empty_like(X)
 
@@ -570,6 +633,8 @@ def main():
         line = run_mlp(args, dist, jx, torch)
     elif args.workload in ("fft1d", "fft2d"):
         line = run_fft(args, dist, jx, torch)
+    elif args.workload in ("conv", "bgemm"):
+        line = run_conv_bgemm(args, dist, jx, torch)
     else:
         line = run_reduce(args, dist, jx, torch)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":
