@@ -13,8 +13,8 @@
 // memory and the last writes it, both coalesced, so an n = 4096 transform
 // touches shared memory only twice.  Twiddles exp(-2 pi i t/n) come from a
 // per-size table computed in double precision.  Columns of a 2-D transform
-// run the same kernel with 16 adjacent columns per CTA, so every global
-// access is a 128-byte row segment.
+// run the same kernel with 8 adjacent columns per CTA, so every global
+// access is a 64-byte row segment.
 #include <math.h>
 
 #include <mutex>
@@ -294,7 +294,7 @@ int launch_fft(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, b
 }
 
 // Transforms per CTA: row transforms fill 256 threads; column transforms take
-// 16 adjacent columns (128-byte segments) when the width allows.
+// 8 adjacent columns when the width allows.
 template <int LOGN>
 int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, long long w, long long hw, bool inv,
                   float scale, cudaStream_t st) {
@@ -307,8 +307,10 @@ int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, lo
   }
   Addr<true> ad{N, w, hw};
   if constexpr (N <= 1024) {
-    constexpr int TPC = T * 16 <= 1024 ? 16 : 1;
-    if (w % 16 == 0) return launch_fft<LOGN, TPC, true>(in, out, ntrans, ad, inv, scale, st);
+    // 8 adjacent columns (64-byte row segments) per CTA: small enough that
+    // several CTAs share an SM, so one CTA's loads overlap another's math.
+    constexpr int TPC = T * 8 <= 512 ? 8 : 1;
+    if (w % 8 == 0) return launch_fft<LOGN, TPC, true>(in, out, ntrans, ad, inv, scale, st);
   }
   return launch_fft<LOGN, 1, true>(in, out, ntrans, ad, inv, scale, st);
 }
@@ -380,21 +382,12 @@ int jx_fft2_c2c_f32(const float* in, float* out, int64_t h, int64_t w, int64_t b
   JX_REQUIRE(in && out, "fft2: NULL pointer");
   cudaStream_t st = jx::as_stream(stream);
   // Rows of length w, then columns of length h (src/ops/fft.rs:261-313); the
-  // column pass works in place on the output.  Images go through in chunks
-  // of at most ~48 MiB, so a chunk's column pass reads what its row pass just
-  // wrote from L2 instead of HBM.
-  const long long img = h * w;
-  long long chunk = (48LL << 20) / (8 * img);
-  if (chunk < 1) chunk = 1;
-  for (long long b0 = 0; b0 < batch; b0 += chunk) {
-    const long long nb = batch - b0 < chunk ? batch - b0 : chunk;
-    const float2* src = reinterpret_cast<const float2*>(in) + b0 * img;
-    float2* dst = reinterpret_cast<float2*>(out) + b0 * img;
-    int rc = fft_batched(src, dst, lw, h * nb, false, 0, 0, inverse != 0, st);
-    if (!rc) rc = fft_batched(dst, dst, lh, w * nb, true, w, img, inverse != 0, st);
-    if (rc) return rc;
-  }
-  return JX_OK;
+  // column pass works in place on the output.
+  int rc = fft_batched(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), lw, h * batch, false, 0, 0,
+                       inverse != 0, st);
+  if (rc) return rc;
+  return fft_batched(reinterpret_cast<const float2*>(out), reinterpret_cast<float2*>(out), lh, w * batch, true, w,
+                     h * w, inverse != 0, st);
 }
 
 }  // extern "C"
