@@ -115,8 +115,22 @@ __device__ __forceinline__ void dft_r(cf2* v) {
   else dft16<INV>(v);
 }
 
-// padded shared-memory index: one spare slot per 16 complex values
-__device__ __forceinline__ int pad(int i) { return i + (i >> 4); }
+// Shared-memory slot of point i of one transform.  Row transforms (a warp
+// inside one transform) pad one slot per 16 points.  Column groups of 8 (a
+// warp spans 8 columns x 4 consecutive points) give each column a region of
+// N + 4 slots and XOR the low two bits of i with bits 2..3 and 4..5; with
+// that, the stride-R0 writes of the leading pass and the stride-1, -2 and -16
+// accesses of the radix-16 passes each touch all 16 eight-byte bank pairs
+// exactly twice per warp (the two-wavefront minimum) for every N <= 1024.
+template <bool SWZ>
+__device__ __forceinline__ int sidx(int i) {
+  if constexpr (SWZ) return (i & ~3) | ((i ^ (i >> 2) ^ (i >> 4)) & 3);
+  else return i + (i >> 4);
+}
+template <int N, bool SWZ>
+constexpr int region() {
+  return SWZ ? N + 4 : N + N / 16;
+}
 
 template <bool COLS>
 struct Addr {
@@ -136,7 +150,8 @@ __global__ void __launch_bounds__(TPC * ((1 << LOGN) / 16)) fft_kernel(const flo
   constexpr int N = 1 << LOGN;
   constexpr int T = N / 16;
   constexpr int R0 = 1 << (LOGN % 4);  // leading radix (1: none)
-  constexpr int NPAD = N + N / 16;
+  constexpr bool SWZ = COLS && TPC == 8;
+  constexpr int NPAD = region<N, SWZ>();
   extern __shared__ float2 sm_raw[];
   cf2* sm = reinterpret_cast<cf2*>(sm_raw);
   const int tid = threadIdx.x;
@@ -163,7 +178,7 @@ __global__ void __launch_bounds__(TPC * ((1 << LOGN) / 16)) fft_kernel(const flo
       }
       dft_r<R0, INV>(u);
 #pragma unroll
-      for (int i = 0; i < R0; ++i) S[pad(b * R0 + i)] = u[i];
+      for (int i = 0; i < R0; ++i) S[sidx<SWZ>(b * R0 + i)] = u[i];
     }
     Ns = R0;
     __syncthreads();
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(TPC * ((1 << LOGN) / 16)) fft_kernel(const flo
         const float2 x = active ? __ldcs(in + gbase + (long long)(j + r * T) * es) : make_float2(0.f, 0.f);
         v[r] = {x.x, x.y};
       } else {
-        v[r] = S[pad(j + r * T)];
+        v[r] = S[sidx<SWZ>(j + r * T)];
       }
     }
     const int k = j % Ns;
@@ -218,7 +233,7 @@ __global__ void __launch_bounds__(TPC * ((1 << LOGN) / 16)) fft_kernel(const flo
       }
     } else {
 #pragma unroll
-      for (int r = 0; r < 16; ++r) S[pad(idxD + r * Ns)] = v[r];
+      for (int r = 0; r < 16; ++r) S[sidx<SWZ>(idxD + r * Ns)] = v[r];
       __syncthreads();
     }
     Ns *= 16;
@@ -274,7 +289,7 @@ int launch_fft(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, b
                cudaStream_t st) {
   constexpr int N = 1 << LOGN;
   constexpr int THREADS = TPC * (N / 16);
-  const size_t smem = sizeof(float2) * (size_t)TPC * (N + N / 16);
+  const size_t smem = sizeof(float2) * (size_t)TPC * region<N, COLS && TPC == 8>();
   const float2* tw = nullptr;
   int rc = twiddles(LOGN, &tw);
   if (rc) return rc;
