@@ -7,17 +7,27 @@
 // reuse, forward only).  The reference has no conv backward; dX and dW here
 // are the exact adjoints of its forward loop.
 //
-// With K = C*KH*KW and P = OH*OW (output pixels):
-//   forward   Y_b[O, P]  = W[O, K] . Xcol_b[K, P]          (batch = images, W shared)
-//   input     dXcol_b[K, P] = W^T[K, O] . dY_b[O, P], then col2im (gather)
-//   weight    dW[O, K] = sum_b dY_b[O, P] . Xcol_b^T[P, K] (contraction over
-//             B*P, split in S slices, partial results added in slice order)
-// The GEMM takes K-major hi/lo operand pairs (see gemm.cu).  The producers
-// below write those pairs directly from the NCHW tensors -- im2col and the
-// tf32 split fused into one pass -- so no plain im2col matrix is ever stored.
+// Implicit GEMM (conv_gemm_kernel).  With K = C*KH*KW and P = OH*OW:
+//   forward   Y[O, (b,p)]      = W[O, (c,kh,kw)]  . X gathered at (b,p),(c,kh,kw)
+//   input     dX[C, (b,ih,iw)] = W'[C, (o,kh,kw)] . dY gathered at (b,ih,iw),(o,kh,kw)
+//   weight    dW[O, (c,kh,kw)] = sum over slices of dY[O, (b,p)] . X gathered
+// The A operand (filter, or dY for the weight gradient) is split into tf32
+// hi/lo once and streamed by TMA.  The B operand is never stored: the eight
+// epilogue warps of the GEMM gather it straight from the NCHW tensor every
+// k-block (bounds and stride tests from a per-index offset table in shared
+// memory), split it, and write the hi/lo tiles into the stage in the layout
+// TMA would have produced, then publish them to the tensor core with
+// fence.proxy.async before arriving on the stage's barrier.  The same warps
+// drain the TMEM span partials and store the tile (NCHW for the forward and
+// the input gradient).  The weight-gradient contraction over B*P is split in
+// slices whose partial products are added in slice order.
+//
+// Shapes outside the implicit kernel's limits (table of more than 4096
+// indices, kernel extent above 127, stride above 255) take the explicit path:
+// fused im2col+split producers into scratch, the plain GEMM, col2im.
 #include <algorithm>
 
-#include "jx_common.cuh"
+#include "tc_gemm.cuh"
 
 namespace jx {
 int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
@@ -160,6 +170,366 @@ __global__ void slice_sum(const float* __restrict__ part, float* __restrict__ ou
   }
 }
 
+// ---------------------------------------------------------------------------
+// Implicit GEMM
+// ---------------------------------------------------------------------------
+using jxg::A_TILE;
+using jxg::B_TILE;
+using jxg::BK;
+using jxg::BM;
+using jxg::BN;
+using jxg::EPI_COLS;
+using jxg::EPI_WARPS;
+using jxg::SPAN_KB;
+using jxg::STAGE_BYTES;
+using jxg::STAGES;
+using jxg::TMEM_COLS;
+
+// Warps: warpgroup 0 = TMA (warp 0), MMA issuer and TMEM owner (warp 1), two
+// idle warps; warpgroups 1 and 2 (warps 4..11) gather, drain and store.  The
+// block launches with 168 registers per thread (384 x 168 = 64,512); warpgroup
+// 0 gives all but 40 back (setmaxnreg.dec) and the gathering warpgroups take
+// 232 each (setmaxnreg.inc): 128 x 40 + 256 x 232 = 64,512, the launch total.
+constexpr int CONV_THREADS = 384;
+constexpr int CONV_FIRST_EPI = 4;
+constexpr int CONV_LAUNCH_REGS = 168;
+constexpr int CONV_LOW_REGS = 40;
+constexpr int CONV_HIGH_REGS = 232;
+static_assert(128 * CONV_LOW_REGS + 256 * CONV_HIGH_REGS <= CONV_THREADS * CONV_LAUNCH_REGS,
+              "register split exceeds the launch allocation");
+constexpr int TABLE_MAX = 4096;  // gather indices held in shared memory
+constexpr int BAR_BYTES = 256;
+constexpr size_t IMPLICIT_SMEM = (size_t)STAGES * STAGE_BYTES + BAR_BYTES + TABLE_MAX * 8 + 1024 /*align*/;
+
+// Gather table entry for one index of the gathered dimension:
+//   x = element offset of the index in the source image (channel plane + tap)
+//   y = int8 dh | int8 dw << 8 | uint8 mh << 16 | uint8 mw << 24
+// The element for a thread's position (qh, qw, rh, rw) is
+//   src[boff + x]  if mh == rh && mw == rw && 0 <= qh+dh < LH && 0 <= qw+dw < LW, else 0.
+// A padding entry has mh = 255, which matches no position.
+__host__ __device__ inline uint32_t pack_tap(int dh, int dw, int mh, int mw) {
+  return (uint32_t)(dh & 0xff) | ((uint32_t)(dw & 0xff) << 8) | ((uint32_t)(mh & 0xff) << 16) |
+         ((uint32_t)(mw & 0xff) << 24);
+}
+
+struct ImplicitArgs {
+  int M, N, num_kb;                  // GEMM rows, columns, contraction k-blocks
+  int tiles_m, tiles_n, num_tiles;   // num_tiles = tiles_m * tiles_n * slices
+  int a_bcast;                       // A has one batch entry (the filter)
+  int table_n;
+  int LH, LW;                        // spatial extent of the gathered tensor
+  int S, P;                          // stride, padding
+  long long img_stride;              // elements per image of the gathered tensor
+  // rows mode (forward, input gradient): B rows are pixels of a PH x PW grid
+  int PW, NPpix, dx_mode;
+  long long out_img_stride;          // M * NPpix: NCHW output
+  // cols mode (weight gradient): B columns are output pixels q of all images
+  long long Q, Ks;                   // contraction length, per-slice length
+  int OW, NPo;
+  long long ldc, strideC;            // row-major partial outputs per slice
+};
+
+// Table of the gathered index: TAB_FWD (c,kh,kw) over x; TAB_DX (o,kh,kw)
+// over dY; entries [count, n) are padding.
+enum { TAB_FWD = 0, TAB_DX = 1 };
+__global__ void build_gather_table(uint2* __restrict__ tab, int n, int count, int mode, const Geo g) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int kk = g.KH * g.KW;
+  if (i >= count) {
+    tab[i] = make_uint2(0u, pack_tap(0, 0, 255, 255));
+    return;
+  }
+  const int ch = i / kk, r = i - (i / kk) * kk;
+  const int kh = r / g.KW, kw = r - (r / g.KW) * g.KW;
+  if (mode == TAB_FWD) {
+    tab[i] = make_uint2((uint32_t)(ch * g.H * g.W + kh * g.W + kw), pack_tap(kh, kw, 0, 0));
+  } else {
+    // input position ih + P = S*qh + rh meets tap kh iff rh == kh % S, at output row qh - kh / S
+    const int dh = -(kh / g.S), dw = -(kw / g.S);
+    tab[i] = make_uint2((uint32_t)(ch * g.OH * g.OW + dh * g.OW + dw), pack_tap(dh, dw, kh % g.S, kw % g.S));
+  }
+}
+
+__device__ __forceinline__ float gather_one(const float* __restrict__ src, long long boff, uint2 e, int qh, int qw,
+                                            int rh, int rw, int LH, int LW) {
+  const int dh = (int)(signed char)(e.y & 0xffu), dw = (int)(signed char)((e.y >> 8) & 0xffu);
+  const int mh = (int)((e.y >> 16) & 0xffu), mw = (int)(e.y >> 24);
+  const bool ok = (mh == rh) & (mw == rw) & ((unsigned)(qh + dh) < (unsigned)LH) & ((unsigned)(qw + dw) < (unsigned)LW);
+  return ok ? __ldg(src + boff + (int)e.x) : 0.0f;
+}
+
+// COLS = false: forward / input gradient (B rows = pixels, k = gathered index)
+// COLS = true:  weight gradient (B rows = gathered index, k = output pixels)
+template <bool COLS>
+__global__ void __launch_bounds__(CONV_THREADS, 1)
+    conv_gemm_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                     const float* __restrict__ src, const uint2* __restrict__ table, const ImplicitArgs a,
+                     float* __restrict__ out, unsigned int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = jxd::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                     // [STAGES] A landed + B written
+  uint64_t* empty = bars + STAGES;           // [STAGES] MMA done with the stage
+  uint64_t* sfull = bars + 2 * STAGES;       // [2] span partial ready
+  uint64_t* sempty = bars + 2 * STAGES + 2;  // [2] span partial drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint2* tab = reinterpret_cast<uint2*>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = a.num_kb;
+
+  for (int i = threadIdx.x; i < a.table_n; i += blockDim.x) tab[i] = table[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      jxd::mbar_init(&full[s], 1 + EPI_WARPS);  // TMA's expect_tx arrive + one per gathering warp
+      jxd::mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      jxd::mbar_init(&sfull[s], 1);
+      jxd::mbar_init(&sempty[s], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    jxd::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    jxd::tma_prefetch_desc(&tmAh);
+    jxd::tma_prefetch_desc(&tmAl);
+  }
+  if (warp == 1) {
+    jxd::tmem_alloc(tmem_slot, TMEM_COLS);
+    jxd::tmem_relinquish();
+  }
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < CONV_FIRST_EPI) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CONV_LOW_REGS));
+    // ---------------- TMA: A operand (hi, lo) ----------------
+    if (warp == 0 && jxd::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
+        const jxg::TileInfo ti = jxg::tile_coords(t, a.tiles_m, a.tiles_n);
+        const int ya = ti.m_blk * BM, za = a.a_bcast ? 0 : ti.b;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          jxd::mbar_arrive_expect_tx(&full[stage], 2 * A_TILE);
+          jxd::tma_load_3d(st, &tmAh, &full[stage], kb * BK, ya, za);
+          jxd::tma_load_3d(st + A_TILE, &tmAl, &full[stage], kb * BK, ya, za);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        if (!jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // ---------------- MMA issuer ----------------
+    if (warp == 1 && jxd::elect_one())
+      jxg::mma_issuer(smem, full, empty, sfull, sempty, tmem_base, a.num_tiles, num_kb, abort_flag, err);
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CONV_HIGH_REGS));
+    // ---------------- gather B, drain spans, store ----------------
+    const int gw = warp - CONV_FIRST_EPI;  // 0..7
+    const int q4 = warp & 3, half = gw >> 2;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t span_ctr = 0;
+    for (int t = blockIdx.x; t < a.num_tiles; t += gridDim.x) {
+      const jxg::TileInfo ti = jxg::tile_coords(t, a.tiles_m, a.tiles_n);
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+      // rows mode: this thread's B row is one pixel for the whole tile
+      int qh = 0, qw = 0, rh = -1, rw = 0;
+      long long boff = 0;
+      if constexpr (!COLS) {
+        const long long n = (long long)ti.n_blk * BN + gw * 32 + lane;
+        if (n < a.N) {
+          const long long b = n / a.NPpix;
+          const int p = (int)(n - b * a.NPpix);
+          const int ph = p / a.PW, pw = p - (p / a.PW) * a.PW;
+          if (a.dx_mode) {
+            const int th = ph + a.P, tw = pw + a.P;
+            qh = th / a.S;
+            rh = th - qh * a.S;
+            qw = tw / a.S;
+            rw = tw - qw * a.S;
+          } else {
+            qh = ph * a.S - a.P;
+            qw = pw * a.S - a.P;
+            rh = rw = 0;
+          }
+          boff = b * a.img_stride + (long long)qh * a.LW + qw;
+        }
+      }
+      bool ok = true;
+      int spans_done = 0;
+      const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if constexpr (COLS) {
+          // this lane's contraction position: output pixel q of slice ti.b
+          const long long jq = (long long)kb * BK + lane;
+          const long long q = (long long)ti.b * a.Ks + jq;
+          rh = -1;
+          if (jq < a.Ks && q < a.Q) {
+            const long long b = q / a.NPo;
+            const int p = (int)(q - b * a.NPo);
+            const int oh = p / a.OW, ow = p - (p / a.OW) * a.OW;
+            qh = oh * a.S - a.P;
+            qw = ow * a.S - a.P;
+            rh = rw = 0;
+            boff = b * a.img_stride + (long long)qh * a.LW + qw;
+          }
+        }
+        // All 32 gathered values are loaded before the wait for the stage, so
+        // the loads are in flight while the MMAs drain it.
+        const uint2* te = COLS ? tab + ti.n_blk * BN + gw * 32 : tab + kb * BK;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gather_one(src, boff, te[i], qh, qw, rh, rw, a.LH, a.LW);
+        if (*abort_flag || !jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        uint8_t* bh = smem + stage * STAGE_BYTES + 2 * A_TILE;
+        if constexpr (!COLS) {
+          // row gw*32+lane, 8 chunks of 4 k values, 128-byte swizzle
+          const int row = gw * 32 + lane;
+          uint8_t* rp = bh + row * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float4 h, l;
+            jxd::split_tf32(v[4 * c], h.x, l.x);
+            jxd::split_tf32(v[4 * c + 1], h.y, l.y);
+            jxd::split_tf32(v[4 * c + 2], h.z, l.z);
+            jxd::split_tf32(v[4 * c + 3], h.w, l.w);
+            const int off = (c ^ (row & 7)) << 4;
+            *reinterpret_cast<float4*>(rp + off) = h;
+            *reinterpret_cast<float4*>(rp + B_TILE + off) = l;
+          }
+        } else {
+          // rows gw*32 + r, this lane's k position within each 128-byte row
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const int row = gw * 32 + r;
+            float h, l;
+            jxd::split_tf32(v[r], h, l);
+            const int off = row * 128 + (((lane >> 2) ^ (row & 7)) << 4) + ((lane & 3) << 2);
+            *reinterpret_cast<float*>(bh + off) = h;
+            *reinterpret_cast<float*>(bh + B_TILE + off) = l;
+          }
+        }
+        jxd::fence_proxy_async_smem();  // make the generic-proxy writes visible to the tensor core
+        __syncwarp();
+        if (lane == 0) jxd::mbar_arrive(&full[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        // Once span i is fully written, drain span i-1 (its MMAs have been
+        // issued before any of span i's could be).
+        if ((kb % SPAN_KB == SPAN_KB - 1 || kb == num_kb - 1) && kb >= SPAN_KB) {
+          if (!jxg::drain_span<32, CONV_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          ++span_ctr;
+          ++spans_done;
+        }
+      }
+      while (ok && spans_done < nspan) {
+        if (!jxg::drain_span<32, CONV_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag, err)) ok = false;
+        ++span_ctr;
+        ++spans_done;
+      }
+      if (!ok) break;
+      // ---- store ----
+      const int m = ti.m_blk * BM + q4 * 32 + lane;
+      if (m < a.M) {
+        const long long n0 = (long long)ti.n_blk * BN + half * EPI_COLS;
+        if constexpr (!COLS) {
+          // NCHW: out[b, m, p] for the flattened pixel n = b * NPpix + p
+          long long b = n0 / a.NPpix;
+          int p = (int)(n0 - b * a.NPpix);
+          float* ob = out + b * a.out_img_stride + (long long)m * a.NPpix;
+          const long long nlim = a.N - n0;
+          if ((a.NPpix & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+            for (int v4 = 0; v4 < EPI_COLS / 4; ++v4) {
+              if (4 * v4 < nlim)
+                *reinterpret_cast<float4*>(ob + p) =
+                    make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
+              p += 4;
+              if (p == a.NPpix) {
+                p = 0;
+                ob += a.out_img_stride;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < EPI_COLS; ++j) {
+              if (j < nlim) ob[p] = acc[j];
+              if (++p == a.NPpix) {
+                p = 0;
+                ob += a.out_img_stride;
+              }
+            }
+          }
+        } else {
+          float* crow = out + (long long)ti.b * a.strideC + (long long)m * a.ldc;
+          const long long nlim = a.N - n0;
+          if ((a.ldc & 3) == 0 && (a.strideC & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+              nlim >= EPI_COLS) {
+            float4* dst = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+            for (int v4 = 0; v4 < EPI_COLS / 4; ++v4)
+              dst[v4] = make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < EPI_COLS; ++j)
+              if (j < nlim) crow[n0 + j] = acc[j];
+          }
+        }
+      }
+    }
+  }
+
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    jxd::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// A operand of the input gradient: Wt[c][(o, kh, kw)] = W[o][c][kh][kw],
+// split into tf32 hi/lo, rows padded to Kp with zeros.
+__global__ void split_filter_ocswap(const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo,
+                                    int Kp, const Geo g) {
+  const int kk = g.KH * g.KW;
+  const long long K = (long long)g.O * kk;
+  const long long total = (long long)g.C * Kp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i / Kp), k = (int)(i - (long long)(i / Kp) * Kp);
+    float x = 0.0f;
+    if (k < K) {
+      const int o = k / kk, r = k - (k / kk) * kk;
+      x = w[((long long)o * g.C + c) * kk + r];
+    }
+    float h, l;
+    jxd::split_tf32(x, h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
 int blocks_for(long long work, int cap_per_sm) {
   long long b = work;
   const long long cap = (long long)jx::num_sms() * cap_per_sm;
@@ -189,6 +559,193 @@ long long images_per_pass(long long B, long long per_image_floats) {
   return nb < B ? nb : B;
 }
 
+// ---- implicit GEMM host side ------------------------------------------------
+
+// Shapes the implicit kernel covers: a gather table that fits shared memory,
+// taps that fit its int8 fields, strides that fit its uint8 residues, and
+// 32-bit element offsets within one image.
+bool implicit_fits(const Geo& g, long long table_entries, long long n_cols, long long img_elems) {
+  return table_entries <= TABLE_MAX && g.KH <= 127 && g.KW <= 127 && g.S <= 255 && n_cols < (1LL << 31) &&
+         img_elems < (1LL << 31);
+}
+
+template <bool COLS>
+int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, const float* src, const uint2* tab,
+                     const ImplicitArgs& a, float* out, cudaStream_t st) {
+  CUtensorMap mAh, mAl;
+  int rc = jx::gemm_make_kmajor_map(&mAh, Ah, Kp, a.M, a_batch, BM);
+  if (!rc) rc = jx::gemm_make_kmajor_map(&mAl, Al, Kp, a.M, a_batch, BM);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev & 63]) {
+    JX_CUDA(cudaFuncSetAttribute(conv_gemm_kernel<COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)IMPLICIT_SMEM));
+    attr_set[dev & 63] = true;
+  }
+  // The register split inside the kernel assumes exactly CONV_LAUNCH_REGS per
+  // thread at launch; with any other allocation setmaxnreg.inc could wait for
+  // registers that never come, so refuse to launch.
+  cudaFuncAttributes fa;
+  JX_CUDA(cudaFuncGetAttributes(&fa, conv_gemm_kernel<COLS>));
+  if (fa.numRegs != CONV_LAUNCH_REGS)
+    return jx::fail(JX_EUNSUPPORTED, "conv_gemm_kernel built with %d registers per thread, expected %d", fa.numRegs,
+                    CONV_LAUNCH_REGS);
+  const int grid = std::min(a.num_tiles, jx::num_sms());
+  conv_gemm_kernel<COLS><<<grid, CONV_THREADS, IMPLICIT_SMEM, st>>>(mAh, mAl, src, tab, a, out,
+                                                                  jx::device_error_word());
+  JX_LAUNCH_CHECK("conv_gemm_kernel");
+  return JX_OK;
+}
+
+int table_build(uint2* tab, int n, int count, int mode, const Geo& g, cudaStream_t st) {
+  build_gather_table<<<(n + 255) / 256, 256, 0, st>>>(tab, n, count, mode, g);
+  JX_LAUNCH_CHECK("build_gather_table");
+  return JX_OK;
+}
+
+int conv_fwd_implicit(const float* x, const float* w, float* y, long long B, const Geo& g, cudaStream_t st) {
+  const long long K = g.K(), Kp = jx::gemm_kpad(K), NP = g.NP();
+  void* ws = nullptr;
+  int rc = jx::scratch_get(sizeof(float) * (size_t)(2 * g.O * Kp + 2 * Kp), &ws, st);
+  if (rc) return rc;
+  float* Wh = reinterpret_cast<float*>(ws);
+  float* Wl = Wh + g.O * Kp;
+  uint2* tab = reinterpret_cast<uint2*>(Wl + g.O * Kp);
+  rc = jx::gemm_split_operand(w, Wh, Wl, g.O, (int)K, (int)Kp, K, 0, 1, false, st);
+  if (!rc) rc = table_build(tab, (int)Kp, (int)K, TAB_FWD, g, st);
+  if (!rc) {
+    ImplicitArgs a{};
+    a.M = g.O;
+    a.N = (int)(B * NP);
+    a.num_kb = (int)(Kp / BK);
+    a.tiles_m = (g.O + BM - 1) / BM;
+    a.tiles_n = (a.N + BN - 1) / BN;
+    a.num_tiles = a.tiles_m * a.tiles_n;
+    a.a_bcast = 1;
+    a.table_n = (int)Kp;
+    a.LH = g.H;
+    a.LW = g.W;
+    a.S = g.S;
+    a.P = g.P;
+    a.img_stride = (long long)g.C * g.H * g.W;
+    a.PW = g.OW;
+    a.NPpix = (int)NP;
+    a.dx_mode = 0;
+    a.out_img_stride = (long long)g.O * NP;
+    rc = launch_conv_gemm<false>(Wh, Wl, 1, (int)Kp, x, tab, a, y, st);
+  }
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
+}
+
+int conv_bwd_data_implicit(const float* dy, const float* w, float* dx, long long B, const Geo& g, cudaStream_t st) {
+  const long long Kd = (long long)g.O * g.KH * g.KW, Kdp = jx::gemm_kpad(Kd);
+  void* ws = nullptr;
+  int rc = jx::scratch_get(sizeof(float) * (size_t)(2 * g.C * Kdp + 2 * Kdp), &ws, st);
+  if (rc) return rc;
+  float* Ah = reinterpret_cast<float*>(ws);
+  float* Al = Ah + g.C * Kdp;
+  uint2* tab = reinterpret_cast<uint2*>(Al + g.C * Kdp);
+  split_filter_ocswap<<<blocks_for((g.C * Kdp + 255) / 256, 8), 256, 0, st>>>(w, Ah, Al, (int)Kdp, g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) rc = jx::check_cuda(e, "split_filter_ocswap");
+  if (!rc) rc = table_build(tab, (int)Kdp, (int)Kd, TAB_DX, g, st);
+  if (!rc) {
+    ImplicitArgs a{};
+    a.M = g.C;
+    a.N = (int)(B * g.H * g.W);
+    a.num_kb = (int)(Kdp / BK);
+    a.tiles_m = (g.C + BM - 1) / BM;
+    a.tiles_n = (a.N + BN - 1) / BN;
+    a.num_tiles = a.tiles_m * a.tiles_n;
+    a.a_bcast = 1;
+    a.table_n = (int)Kdp;
+    a.LH = g.OH;
+    a.LW = g.OW;
+    a.S = g.S;
+    a.P = g.P;
+    a.img_stride = (long long)g.O * g.OH * g.OW;
+    a.PW = g.W;
+    a.NPpix = g.H * g.W;
+    a.dx_mode = 1;
+    a.out_img_stride = (long long)g.C * g.H * g.W;
+    rc = launch_conv_gemm<false>(Ah, Al, 1, (int)Kdp, dy, tab, a, dx, st);
+  }
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
+}
+
+// Slices of the weight-gradient contraction: the count in [1, 64] (each slice
+// at least 1024 long) whose tile count fills the SMs' last wave best.
+long long dw_slices(long long tiles, long long Q) {
+  const long long sms = jx::num_sms();
+  long long best = 1;
+  double best_eff = -1.0;
+  for (long long S = 1; S <= 64; ++S) {
+    if (S > 1 && Q / S < 1024) break;
+    const long long total = tiles * S;
+    const long long waves = (total + sms - 1) / sms;
+    const double eff = (double)total / (double)(waves * sms);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = S;
+    }
+  }
+  return best;
+}
+
+int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long long B, const Geo& g, cudaStream_t st) {
+  const long long K = g.K(), NP = g.NP(), Q = B * NP;
+  const int tiles_m = (g.O + BM - 1) / BM, tiles_n = (int)((K + BN - 1) / BN);
+  const long long S = dw_slices((long long)tiles_m * tiles_n, Q);
+  const long long Ks = (Q + S - 1) / S, Ksp = jx::gemm_kpad(Ks);
+  const long long tab_n = (long long)tiles_n * BN;
+  void* ws = nullptr;
+  const size_t floats = (size_t)(2 * S * g.O * Ksp + 2 * tab_n + (S > 1 ? S * g.O * K : 0));
+  int rc = jx::scratch_get(sizeof(float) * floats, &ws, st);
+  if (rc) return rc;
+  float* Ah = reinterpret_cast<float*>(ws);
+  float* Al = Ah + S * g.O * Ksp;
+  uint2* tab = reinterpret_cast<uint2*>(Al + S * g.O * Ksp);
+  float* part = S > 1 ? reinterpret_cast<float*>(tab + tab_n) : dw;
+  dy_rows_split<<<blocks_for(S * g.O, 16), 256, 0, st>>>(dy, Ah, Al, Q, Ks, (int)Ksp, (int)S, g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) rc = jx::check_cuda(e, "dy_rows_split");
+  if (!rc) rc = table_build(tab, (int)tab_n, (int)K, TAB_FWD, g, st);
+  if (!rc) {
+    ImplicitArgs a{};
+    a.M = g.O;
+    a.N = (int)K;
+    a.num_kb = (int)(Ksp / BK);
+    a.tiles_m = tiles_m;
+    a.tiles_n = tiles_n;
+    a.num_tiles = (int)(tiles_m * tiles_n * S);
+    a.a_bcast = 0;
+    a.table_n = (int)tab_n;
+    a.LH = g.H;
+    a.LW = g.W;
+    a.S = g.S;
+    a.P = g.P;
+    a.img_stride = (long long)g.C * g.H * g.W;
+    a.Q = Q;
+    a.Ks = Ks;
+    a.OW = g.OW;
+    a.NPo = (int)NP;
+    a.ldc = K;
+    a.strideC = (long long)g.O * K;
+    rc = launch_conv_gemm<true>(Ah, Al, (int)S, (int)Ksp, x, tab, a, part, st);
+  }
+  if (!rc && S > 1) {
+    slice_sum<<<blocks_for((g.O * K + 255) / 256, 8), 256, 0, st>>>(part, dw, g.O * K, (int)S);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) rc = jx::check_cuda(e, "slice_sum");
+  }
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
+}
+
 }  // namespace
 
 extern "C" {
@@ -202,6 +759,7 @@ int jx_conv2d_fwd_f32(const float* x, const float* w, float* y, int64_t B, int64
   JX_REQUIRE(x && w && y, "conv2d: NULL pointer");
   cudaStream_t st = jx::as_stream(stream);
   const long long K = g.K(), Kp = jx::gemm_kpad(K), NP = g.NP();
+  if (implicit_fits(g, Kp, B * NP, C * H * W)) return conv_fwd_implicit(x, w, y, B, g, st);
   const long long nb = images_per_pass(B, 2 * NP * Kp);
   void* ws = nullptr;
   if ((rc = jx::scratch_get(sizeof(float) * (size_t)(2 * O * Kp + 2 * nb * NP * Kp), &ws, st))) return rc;
@@ -232,6 +790,8 @@ int jx_conv2d_bwd_data_f32(const float* dy, const float* w, float* dx, int64_t B
   if (B == 0) return JX_OK;
   JX_REQUIRE(dy && w && dx, "conv2d: NULL pointer");
   cudaStream_t st = jx::as_stream(stream);
+  if (implicit_fits(g, jx::gemm_kpad(O * KH * KW), B * H * W, O * (long long)g.OH * g.OW))
+    return conv_bwd_data_implicit(dy, w, dx, B, g, st);
   const long long K = g.K(), Op = jx::gemm_kpad(O), NP = g.NP();
   const long long nb = images_per_pass(B, 2 * NP * Op + K * NP);
   void* ws = nullptr;
@@ -271,6 +831,7 @@ int jx_conv2d_bwd_filter_f32(const float* x, const float* dy, float* dw, int64_t
     return JX_OK;
   }
   JX_REQUIRE(x && dy, "conv2d: NULL pointer");
+  if (implicit_fits(g, (K + 255) / 256 * 256, K, C * H * W)) return conv_bwd_filter_implicit(x, dy, dw, B, g, st);
   const long long Q = B * NP;  // contraction length: every image's every output pixel
   // slices: enough output tiles to fill the GPU twice over, each slice >= 1024 long
   const long long tiles = ((O + 127) / 128) * ((K + 255) / 256);

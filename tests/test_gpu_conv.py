@@ -34,6 +34,13 @@ CASES = [
     (2, 16, 14, 14, 32, 3, 3, 1, 1),
     (1, 3, 6, 6, 2, 6, 6, 1, 0),
     (4, 64, 12, 12, 48, 3, 3, 1, 1),
+    # O above one 128-row tile; odd stride and kernel extents
+    (2, 8, 9, 9, 130, 3, 3, 1, 1),
+    (3, 3, 17, 13, 5, 4, 2, 3, 1),
+    # C*KH*KW = 4608 exceeds the implicit kernel's gather table: forward and
+    # weight gradient take the explicit im2col path, the input gradient
+    # (O*KH*KW = 36) the implicit one
+    (1, 512, 5, 5, 4, 3, 3, 1, 1),
 ]
 
 
