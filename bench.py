@@ -49,6 +49,7 @@ def parse():
                    help="GEMM precision of the MLP trainer")
     p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
     p.add_argument("--fft-batch", type=int, default=0, help="override the FFT batch (smaller cases for profiling)")
+    p.add_argument("--conv-batch", type=int, default=0, help="override the conv batch (smaller cases for profiling)")
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -384,7 +385,7 @@ def run_conv_bgemm(args, dist, jx, torch):
     g = torch.Generator(device=dev)
     g.manual_seed(3 + dist.rank)
     if args.workload == "conv":
-        B, C, H, W, O, K = 64, 256, 56, 56, 256, 3
+        B, C, H, W, O, K = args.conv_batch or 64, 256, 56, 56, 256, 3
         geo = (B, C, H, W, O, K, K, 1, 1)
         X = torch.randn((B, C, H, W), device=dev, generator=g)
         Wt = torch.randn((O, C, K, K), device=dev, generator=g) * float(np.sqrt(2.0 / (C * K * K)))
@@ -396,7 +397,7 @@ def run_conv_bgemm(args, dist, jx, torch):
             jx.call("jx_conv2d_bwd_data_f32", G.data_ptr(), Wt.data_ptr(), DX.data_ptr(), *geo, s)
             jx.call("jx_conv2d_bwd_filter_f32", X.data_ptr(), G.data_ptr(), DW.data_ptr(), *geo, s)
         flops = 3 * 2.0 * B * O * C * K * K * H * W
-        wl = "conv2d [64,256,56,56] x [256,256,3,3] s1 p1: forward + input grad + weight grad per step"
+        wl = f"conv2d [{B},256,56,56] x [256,256,3,3] s1 p1: forward + input grad + weight grad per step"
     else:
         nb, n = 64, 2048
         A = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)

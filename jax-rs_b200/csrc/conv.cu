@@ -23,7 +23,7 @@
 // slices whose partial products are added in slice order.
 //
 // Shapes outside the implicit kernel's limits (table of more than 4096
-// indices, kernel extent above 127, stride above 255) take the explicit path:
+// indices, more than 32 filter taps) take the explicit path:
 // fused im2col+split producers into scratch, the plain GEMM, col2im.
 #include <algorithm>
 
@@ -201,30 +201,26 @@ constexpr int TABLE_MAX = 4096;  // gather indices held in shared memory
 constexpr int BAR_BYTES = 256;
 constexpr size_t IMPLICIT_SMEM = (size_t)STAGES * STAGE_BYTES + BAR_BYTES + TABLE_MAX * 8 + 1024 /*align*/;
 
-// Gather table entry for one index of the gathered dimension:
-//   x = element offset of the index in the source image (channel plane + tap)
-//   y = int8 dh | int8 dw << 8 | uint8 mh << 16 | uint8 mw << 24
-// The element for a thread's position (qh, qw, rh, rw) is
-//   src[boff + x]  if mh == rh && mw == rw && 0 <= qh+dh < LH && 0 <= qw+dw < LW, else 0.
-// A padding entry has mh = 255, which matches no position.
-__host__ __device__ inline uint32_t pack_tap(int dh, int dw, int mh, int mw) {
-  return (uint32_t)(dh & 0xff) | ((uint32_t)(dw & 0xff) << 8) | ((uint32_t)(mh & 0xff) << 16) |
-         ((uint32_t)(mw & 0xff) << 24);
-}
-
+// Gather table entry for one index of the gathered dimension (k in rows
+// mode, the GEMM column in cols mode):
+//   x = element offset of the index from a position's base (channel plane + tap)
+//   y = 1 << (kh * KW + kw), the index's filter tap; 0 for a padding entry.
+// A position (a pixel, with its own base pointer) keeps a mask of the taps
+// that land inside the gathered tensor; the element is base[x] when
+// (mask & y) != 0, else 0.
 struct ImplicitArgs {
   int M, N, num_kb;                  // GEMM rows, columns, contraction k-blocks
   int tiles_m, tiles_n, num_tiles;   // num_tiles = tiles_m * tiles_n * slices
   int a_bcast;                       // A has one batch entry (the filter)
   int table_n;
   int LH, LW;                        // spatial extent of the gathered tensor
-  int S, P;                          // stride, padding
+  int KH, KW, S, P;                  // filter extent, stride, padding
   long long img_stride;              // elements per image of the gathered tensor
   // rows mode (forward, input gradient): B rows are pixels of a PH x PW grid
   int PW, NPpix, dx_mode;
   long long out_img_stride;          // M * NPpix: NCHW output
   // cols mode (weight gradient): B columns are output pixels q of all images
-  long long Q, Ks;                   // contraction length, per-slice length
+  int Q, Ks;                         // contraction length, per-slice length
   int OW, NPo;
   long long ldc, strideC;            // row-major partial outputs per slice
 };
@@ -237,26 +233,47 @@ __global__ void build_gather_table(uint2* __restrict__ tab, int n, int count, in
   if (i >= n) return;
   const int kk = g.KH * g.KW;
   if (i >= count) {
-    tab[i] = make_uint2(0u, pack_tap(0, 0, 255, 255));
+    tab[i] = make_uint2(0u, 0u);
     return;
   }
   const int ch = i / kk, r = i - (i / kk) * kk;
   const int kh = r / g.KW, kw = r - (r / g.KW) * g.KW;
   if (mode == TAB_FWD) {
-    tab[i] = make_uint2((uint32_t)(ch * g.H * g.W + kh * g.W + kw), pack_tap(kh, kw, 0, 0));
+    // x[b, c, oh*S - P + kh, ow*S - P + kw]: base at (oh*S - P, ow*S - P)
+    tab[i] = make_uint2((uint32_t)(ch * g.H * g.W + kh * g.W + kw), 1u << r);
   } else {
-    // input position ih + P = S*qh + rh meets tap kh iff rh == kh % S, at output row qh - kh / S
-    const int dh = -(kh / g.S), dw = -(kw / g.S);
-    tab[i] = make_uint2((uint32_t)(ch * g.OH * g.OW + dh * g.OW + dw), pack_tap(dh, dw, kh % g.S, kw % g.S));
+    // dY[b, o, oh, ow] with oh*S = ih + P - kh: writing ih + P = S*qh + rh, tap
+    // kh contributes iff kh % S == rh, at oh = qh - kh / S (base at (qh, qw))
+    tab[i] = make_uint2((uint32_t)(ch * g.OH * g.OW - (kh / g.S) * g.OW - (kw / g.S)), 1u << r);
   }
 }
 
-__device__ __forceinline__ float gather_one(const float* __restrict__ src, long long boff, uint2 e, int qh, int qw,
-                                            int rh, int rw, int LH, int LW) {
-  const int dh = (int)(signed char)(e.y & 0xffu), dw = (int)(signed char)((e.y >> 8) & 0xffu);
-  const int mh = (int)((e.y >> 16) & 0xffu), mw = (int)(e.y >> 24);
-  const bool ok = (mh == rh) & (mw == rw) & ((unsigned)(qh + dh) < (unsigned)LH) & ((unsigned)(qw + dw) < (unsigned)LW);
-  return ok ? __ldg(src + boff + (int)e.x) : 0.0f;
+// Taps of a position that read inside the gathered tensor.  Forward and
+// weight gradient: input row qh + kh (qh = oh*S - P).  Input gradient: tap kh
+// needs kh % S == rh and output row qh - kh / S.
+__device__ __forceinline__ uint32_t tap_mask(int qh, int qw, int rh, int rw, const ImplicitArgs& a, bool dx) {
+  uint32_t cols = 0;
+  for (int kw = 0; kw < a.KW; ++kw) {
+    const int w = dx ? qw - kw / a.S : qw + kw;
+    const bool ok = (!dx || kw % a.S == rw) && (unsigned)w < (unsigned)a.LW;
+    cols |= ok ? 1u << kw : 0u;
+  }
+  uint32_t m = 0;
+  for (int kh = 0; kh < a.KH; ++kh) {
+    const int h = dx ? qh - kh / a.S : qh + kh;
+    const bool ok = (!dx || kh % a.S == rh) && (unsigned)h < (unsigned)a.LH;
+    m |= ok ? cols << (kh * a.KW) : 0u;
+  }
+  return m;
+}
+
+// One predicated load: base[off] when ok != 0, else 0 (no branch).
+__device__ __forceinline__ float gather_one(const float* base, int off, uint32_t ok) {
+  float v = 0.0f;
+  asm("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %2, 0;\n\t@p ld.global.nc.f32 %0, [%1];\n\t}"
+      : "+f"(v)
+      : "l"(base + off), "r"(ok));
+  return v;
 }
 
 // COLS = false: forward / input gradient (B rows = pixels, k = gathered index)
@@ -348,14 +365,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
       for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
       // rows mode: this thread's B row is one pixel for the whole tile
-      int qh = 0, qw = 0, rh = -1, rw = 0;
-      long long boff = 0;
+      const float* base = src;
+      uint32_t mask = 0;
       if constexpr (!COLS) {
         const long long n = (long long)ti.n_blk * BN + gw * 32 + lane;
         if (n < a.N) {
           const long long b = n / a.NPpix;
           const int p = (int)(n - b * a.NPpix);
           const int ph = p / a.PW, pw = p - (p / a.PW) * a.PW;
+          int qh, qw, rh = 0, rw = 0;
           if (a.dx_mode) {
             const int th = ph + a.P, tw = pw + a.P;
             qh = th / a.S;
@@ -365,9 +383,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           } else {
             qh = ph * a.S - a.P;
             qw = pw * a.S - a.P;
-            rh = rw = 0;
           }
-          boff = b * a.img_stride + (long long)qh * a.LW + qw;
+          mask = tap_mask(qh, qw, rh, rw, a, a.dx_mode != 0);
+          base = src + (b * a.img_stride + (long long)qh * a.LW + qw);
         }
       }
       bool ok = true;
@@ -376,25 +394,29 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       for (int kb = 0; kb < num_kb; ++kb) {
         if constexpr (COLS) {
           // this lane's contraction position: output pixel q of slice ti.b
-          const long long jq = (long long)kb * BK + lane;
+          const int jq = kb * BK + lane;
           const long long q = (long long)ti.b * a.Ks + jq;
-          rh = -1;
+          mask = 0;
           if (jq < a.Ks && q < a.Q) {
-            const long long b = q / a.NPo;
-            const int p = (int)(q - b * a.NPo);
+            const int qi = (int)q;
+            const int b = qi / a.NPo;
+            const int p = qi - b * a.NPo;
             const int oh = p / a.OW, ow = p - (p / a.OW) * a.OW;
-            qh = oh * a.S - a.P;
-            qw = ow * a.S - a.P;
-            rh = rw = 0;
-            boff = b * a.img_stride + (long long)qh * a.LW + qw;
+            const int qh = oh * a.S - a.P, qw = ow * a.S - a.P;
+            mask = tap_mask(qh, qw, 0, 0, a, false);
+            base = src + ((long long)b * a.img_stride + (long long)qh * a.LW + qw);
           }
         }
         // All 32 gathered values are loaded before the wait for the stage, so
         // the loads are in flight while the MMAs drain it.
-        const uint2* te = COLS ? tab + ti.n_blk * BN + gw * 32 : tab + kb * BK;
+        const uint4* te = reinterpret_cast<const uint4*>(COLS ? tab + ti.n_blk * BN + gw * 32 : tab + kb * BK);
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = gather_one(src, boff, te[i], qh, qw, rh, rw, a.LH, a.LW);
+        for (int i = 0; i < 16; ++i) {
+          const uint4 e = te[i];
+          v[2 * i] = gather_one(base, (int)e.x, e.y & mask);
+          v[2 * i + 1] = gather_one(base, (int)e.z, e.w & mask);
+        }
         if (*abort_flag || !jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) {
           *abort_flag = 1;
           ok = false;
@@ -562,11 +584,10 @@ long long images_per_pass(long long B, long long per_image_floats) {
 // ---- implicit GEMM host side ------------------------------------------------
 
 // Shapes the implicit kernel covers: a gather table that fits shared memory,
-// taps that fit its int8 fields, strides that fit its uint8 residues, and
-// 32-bit element offsets within one image.
+// at most 32 filter taps (one mask bit each), and 32-bit element offsets
+// within one image.
 bool implicit_fits(const Geo& g, long long table_entries, long long n_cols, long long img_elems) {
-  return table_entries <= TABLE_MAX && g.KH <= 127 && g.KW <= 127 && g.S <= 255 && n_cols < (1LL << 31) &&
-         img_elems < (1LL << 31);
+  return table_entries <= TABLE_MAX && g.KH * g.KW <= 32 && n_cols < (1LL << 31) && img_elems < (1LL << 31);
 }
 
 template <bool COLS>
@@ -627,6 +648,8 @@ int conv_fwd_implicit(const float* x, const float* w, float* y, long long B, con
     a.table_n = (int)Kp;
     a.LH = g.H;
     a.LW = g.W;
+    a.KH = g.KH;
+    a.KW = g.KW;
     a.S = g.S;
     a.P = g.P;
     a.img_stride = (long long)g.C * g.H * g.W;
@@ -664,6 +687,8 @@ int conv_bwd_data_implicit(const float* dy, const float* w, float* dx, long long
     a.table_n = (int)Kdp;
     a.LH = g.OH;
     a.LW = g.OW;
+    a.KH = g.KH;
+    a.KW = g.KW;
     a.S = g.S;
     a.P = g.P;
     a.img_stride = (long long)g.O * g.OH * g.OW;
@@ -726,11 +751,13 @@ int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long lo
     a.table_n = (int)tab_n;
     a.LH = g.H;
     a.LW = g.W;
+    a.KH = g.KH;
+    a.KW = g.KW;
     a.S = g.S;
     a.P = g.P;
     a.img_stride = (long long)g.C * g.H * g.W;
-    a.Q = Q;
-    a.Ks = Ks;
+    a.Q = (int)Q;
+    a.Ks = (int)Ks;
     a.OW = g.OW;
     a.NPo = (int)NP;
     a.ldc = K;
@@ -831,7 +858,8 @@ int jx_conv2d_bwd_filter_f32(const float* x, const float* dy, float* dw, int64_t
     return JX_OK;
   }
   JX_REQUIRE(x && dy, "conv2d: NULL pointer");
-  if (implicit_fits(g, (K + 255) / 256 * 256, K, C * H * W)) return conv_bwd_filter_implicit(x, dy, dw, B, g, st);
+  if (implicit_fits(g, (K + 255) / 256 * 256, std::max(K, B * NP), C * H * W))
+    return conv_bwd_filter_implicit(x, dy, dw, B, g, st);
   const long long Q = B * NP;  // contraction length: every image's every output pixel
   // slices: enough output tiles to fill the GPU twice over, each slice >= 1024 long
   const long long tiles = ((O + 127) / 128) * ((K + 255) / 256);
