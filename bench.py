@@ -430,7 +430,9 @@ def run_conv_bgemm(args, dist, jx, torch):
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": wl,
                                                                                  "parallelism": f"batch shards x{dist.world}"},
-            "roofline": {"bound": "tensor", "kernel": "whole step (operand producers + gemm_3xtf32_kernel)",
+            "roofline": {"bound": "tensor",
+                         "kernel": ("conv_gemm_kernel x3 (implicit GEMM; whole step incl. filter/dY splits)"
+                                    if args.workload == "conv" else "split passes + gemm_3xtf32_kernel"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
                          "traffic": None},

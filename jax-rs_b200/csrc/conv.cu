@@ -391,36 +391,39 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       bool ok = true;
       int spans_done = 0;
       const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
-      for (int kb = 0; kb < num_kb; ++kb) {
+      // gather(v, kb): issue k-block kb's 32 loads (no wait on the stage).
+      auto gather = [&](float (&v)[32], int kb) {
+        const float* gbase = base;
+        uint32_t gmask = mask;
         if constexpr (COLS) {
           // this lane's contraction position: output pixel q of slice ti.b
           const int jq = kb * BK + lane;
           const long long q = (long long)ti.b * a.Ks + jq;
-          mask = 0;
+          gmask = 0;
           if (jq < a.Ks && q < a.Q) {
             const int qi = (int)q;
             const int b = qi / a.NPo;
             const int p = qi - b * a.NPo;
             const int oh = p / a.OW, ow = p - (p / a.OW) * a.OW;
             const int qh = oh * a.S - a.P, qw = ow * a.S - a.P;
-            mask = tap_mask(qh, qw, 0, 0, a, false);
-            base = src + ((long long)b * a.img_stride + (long long)qh * a.LW + qw);
+            gmask = tap_mask(qh, qw, 0, 0, a, false);
+            gbase = src + ((long long)b * a.img_stride + (long long)qh * a.LW + qw);
           }
         }
-        // All 32 gathered values are loaded before the wait for the stage, so
-        // the loads are in flight while the MMAs drain it.
         const uint4* te = reinterpret_cast<const uint4*>(COLS ? tab + ti.n_blk * BN + gw * 32 : tab + kb * BK);
-        float v[32];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const uint4 e = te[i];
-          v[2 * i] = gather_one(base, (int)e.x, e.y & mask);
-          v[2 * i + 1] = gather_one(base, (int)e.z, e.w & mask);
+          v[2 * i] = gather_one(gbase, (int)e.x, e.y & gmask);
+          v[2 * i + 1] = gather_one(gbase, (int)e.z, e.w & gmask);
         }
+      };
+      // publish(v, kb): wait for the stage, write v as tf32 hi/lo, hand the
+      // stage to the tensor core, and drain a span partial when one is due.
+      auto publish = [&](float (&v)[32], int kb) -> bool {
         if (*abort_flag || !jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) {
           *abort_flag = 1;
-          ok = false;
-          break;
+          return false;
         }
         uint8_t* bh = smem + stage * STAGE_BYTES + 2 * A_TILE;
         if constexpr (!COLS) {
@@ -457,12 +460,24 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         // Once span i is fully written, drain span i-1 (its MMAs have been
         // issued before any of span i's could be).
         if ((kb % SPAN_KB == SPAN_KB - 1 || kb == num_kb - 1) && kb >= SPAN_KB) {
-          if (!jxg::drain_span<32, CONV_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag, err)) {
-            ok = false;
-            break;
-          }
+          if (!jxg::drain_span<32, CONV_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag,
+                                                   err))
+            return false;
           ++span_ctr;
           ++spans_done;
+        }
+        return true;
+      };
+      // Software pipeline: k-block kb+1's loads are in flight while k-block kb
+      // waits for its stage and is written.
+      float va[32], vb[32];
+      if (num_kb > 0) gather(va, 0);
+      for (int kb = 0; kb < num_kb; kb += 2) {
+        if (kb + 1 < num_kb) gather(vb, kb + 1);
+        if (!publish(va, kb)) { ok = false; break; }
+        if (kb + 1 < num_kb) {
+          if (kb + 2 < num_kb) gather(va, kb + 2);
+          if (!publish(vb, kb + 1)) { ok = false; break; }
         }
       }
       while (ok && spans_done < nspan) {
