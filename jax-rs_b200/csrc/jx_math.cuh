@@ -26,7 +26,9 @@ constexpr float GELU_C1 = 0.044715f;
 // through); the product's rounding error lo = fma(x, L2E, -hi) is applied as
 // the first-order factor (1 + lo*ln2).  Relative error about 2e-7 for
 // |x| <= 30 and below 1.3e-6 across the range (log2(e)'s own f32 rounding
-// contributes |x|*1.3e-8).
+// contributes |x|*1.3e-8).  Beyond |hi| = 128 the result is +inf or 0 and is
+// returned as is (the correction would turn inf into inf - inf, and lo is NaN
+// for infinite x).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -43,7 +45,7 @@ __device__ __forceinline__ float jx_exp(float x) {
   const float hi = x * L2E;
   const float lo = fmaf(x, L2E, -hi);
   const float e = ex2_approx(hi);
-  return fmaf(e, lo * LN2, e);
+  return fabsf(hi) < 128.0f ? fmaf(e, lo * LN2, e) : e;
 }
 // tanh: odd Taylor series x - x^3/3 + 2x^5/15 for |x| < 0.05 (next term below
 // 5e-11 relative), else 1 - 2/(e^{2|x|} + 1) with the sign restored.  Both are
@@ -88,25 +90,38 @@ static __device__ __noinline__ float jx_powf(float a, float b) { return powf(a, 
 // nn::gelu (src/nn.rs:111-122): coeff = sqrt(2/pi); inner = coeff*(v + 0.044715*v^3);
 // 0.5*v*(1 + tanh(inner)); v.powi(3) = v*(v*v).  coeff is the f32 value of
 // sqrtf(2.0f / PI) (0x3f4c4229), as the reference computes it per element.
+// inner is formed in the reference's order; the identity
+// 0.5*(1 + tanh(z)) = 1/(1 + e^{-2z}) then takes one exponential and one
+// reciprocal instead of tanh's two paths.  The difference from the
+// reference's own evaluation is its rounding of 1 + tanh(z) near tanh = -1
+// (at most 0.5*|v|*2^-24 for |v| <= 5, below 3e-7 in absolute terms); large
+// negative v gives -0 or a tiny negative value there as in the reference.
+// e = 2^(-2z*log2 e) skips jx_exp's product correction: its relative error
+// (|2z|*6e-8) matters only while 1/(1 + e) is not negligible, |2z| <= 16.
 __device__ __forceinline__ float gelu_coeff() { return __int_as_float(0x3f4c4229); }
+__device__ __forceinline__ float gelu_inner(float v) {
+  const float v3 = __fmul_rn(v, __fmul_rn(v, v));
+  return __fmul_rn(gelu_coeff(), __fadd_rn(v, __fmul_rn(GELU_C1, v3)));
+}
+constexpr float NEG2_L2E = -2.0f * 1.44269502162933349609375f;  // exact: -2 * fl(log2 e)
 __device__ __forceinline__ float gelu_f(float v) {
-  const float coeff = gelu_coeff();
-  float v3 = __fmul_rn(v, __fmul_rn(v, v));
-  float inner = __fmul_rn(coeff, __fadd_rn(v, __fmul_rn(GELU_C1, v3)));
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, jx_tanh(inner)));
+  const float e = ex2_approx(gelu_inner(v) * NEG2_L2E);
+  return v * rcp_approx(1.0f + e);
 }
 
 // d/du of gelu_f (restated adjoint; the reference leaves gelu untraced):
-// 0.5*(1+t) + 0.5*u*(1-t^2)*coeff*(1 + 3*0.044715*u^2).
+// 0.5*(1+t) + 0.5*u*(1-t^2)*dinner with t = tanh(inner),
+// dinner = coeff*(1 + 3*0.044715*u^2).  With s = 0.5*(1+t) = 1/(1+e),
+// e = e^{-2 inner}: 0.5*(1 - t^2) = 2 s (1 - s), and 1 - s = e*s without
+// cancellation while e <= 1 (1 - s is exact enough above that, s <= 1/2).
 __device__ __forceinline__ float gelu_grad_f(float u) {
   const float coeff = gelu_coeff();
-  float u2 = __fmul_rn(u, u);
-  float inner = __fmul_rn(coeff, __fadd_rn(u, __fmul_rn(GELU_C1, __fmul_rn(u, u2))));
-  float t = jx_tanh(inner);
-  float dinner = __fmul_rn(coeff, __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, GELU_C1), u2)));
-  float a = __fmul_rn(0.5f, __fadd_rn(1.0f, t));
-  float b = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, u), __fsub_rn(1.0f, __fmul_rn(t, t))), dinner);
-  return __fadd_rn(a, b);
+  const float u2 = __fmul_rn(u, u);
+  const float e = ex2_approx(gelu_inner(u) * NEG2_L2E);
+  const float s = rcp_approx(1.0f + e);
+  const float oms = e <= 1.0f ? e * s : 1.0f - s;
+  const float dinner = __fmul_rn(coeff, __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, GELU_C1), u2)));
+  return s + 2.0f * u * s * oms * dinner;
 }
 
 // nn::sigmoid (src/nn.rs:135-140): 1 / (1 + exp(-v))

@@ -176,19 +176,27 @@ std::string codegen(const jx_tape* t) {
   std::string s;
   s += kParamsDecl;
   s += "extern \"C\" __global__ void __launch_bounds__(256) jx_tape_kernel(const TapeParams p) {\n";
+  // Each iteration: two 4-element groups per thread, one sweep of the grid
+  // apart, so both 128-bit loads of a warp stay fully coalesced and the
+  // second group's math overlaps the first's.
   s += "  const long long n = p.n;\n";
-  s += "  const long long stride = (long long)gridDim.x * blockDim.x * 4;\n";
-  s += "  for (long long base = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; base < n; base += stride) {\n";
-  s += "    const bool full = p.vec_ok && base + 4 <= n;\n";
+  s += "  const long long sweep = (long long)gridDim.x * blockDim.x * 4;\n";
+  s += "  for (long long b0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; b0 < n; b0 += 2 * sweep) {\n";
+  s += "    const long long bs[2] = {b0, b0 + sweep};\n";
   for (int i = 0; i < t->n_in; ++i) {
     const std::string I = std::to_string(i);
-    s += "    float x" + I + "[4];\n";
-    s += "    if (full) { const float4 q = __ldcs(reinterpret_cast<const float4*>(p.in[" + I + "] + base));"
-         " x" + I + "[0] = q.x; x" + I + "[1] = q.y; x" + I + "[2] = q.z; x" + I + "[3] = q.w; }\n";
-    s += "    else { for (int v = 0; v < 4; ++v) x" + I + "[v] = base + v < n ? p.in[" + I + "][base + v] : 0.0f; }\n";
+    s += "    float x" + I + "[8];\n";
+    s += "#pragma unroll\n    for (int u = 0; u < 2; ++u) {\n";
+    s += "      const long long base = bs[u];\n";
+    s += "      if (p.vec_ok && base + 4 <= n) { const float4 q = __ldcs(reinterpret_cast<const float4*>(p.in[" + I +
+         "] + base)); x" + I + "[4 * u] = q.x; x" + I + "[4 * u + 1] = q.y; x" + I + "[4 * u + 2] = q.z; x" + I +
+         "[4 * u + 3] = q.w; }\n";
+    s += "      else { for (int v = 0; v < 4; ++v) x" + I + "[4 * u + v] = base + v < n ? p.in[" + I +
+         "][base + v] : 0.0f; }\n";
+    s += "    }\n";
   }
-  for (int o = 0; o < t->n_out; ++o) s += "    float y" + std::to_string(o) + "[4];\n";
-  s += "#pragma unroll\n    for (int v = 0; v < 4; ++v) {\n";
+  for (int o = 0; o < t->n_out; ++o) s += "    float y" + std::to_string(o) + "[8];\n";
+  s += "#pragma unroll\n    for (int v = 0; v < 8; ++v) {\n";
   // SSA: every definition gets a fresh name; reg_name tracks the current one.
   // First pass: the SSA name each unary op reads, to find values that are fed
   // to both sigmoid and tanh (those share one exponential, jxm::sigmoid_tanh).
@@ -244,13 +252,17 @@ std::string codegen(const jx_tape* t) {
     reg_name[c.y] = nm;
   }
   s += "    }\n";
+  s += "#pragma unroll\n    for (int u = 0; u < 2; ++u) {\n";
+  s += "      const long long base = bs[u];\n";
   for (int o = 0; o < t->n_out; ++o) {
     const std::string O = std::to_string(o);
-    s += "    if (full) __stcs(reinterpret_cast<float4*>(p.out[" + O + "] + base), make_float4(y" + O + "[0], y" + O +
-         "[1], y" + O + "[2], y" + O + "[3]));\n";
-    s += "    else { for (int v = 0; v < 4; ++v) if (base + v < n) p.out[" + O + "][base + v] = y" + O + "[v]; }\n";
+    s += "      if (p.vec_ok && base + 4 <= n) __stcs(reinterpret_cast<float4*>(p.out[" + O +
+         "] + base), make_float4(y" + O + "[4 * u], y" + O + "[4 * u + 1], y" + O + "[4 * u + 2], y" + O +
+         "[4 * u + 3]));\n";
+    s += "      else { for (int v = 0; v < 4; ++v) if (base + v < n) p.out[" + O + "][base + v] = y" + O +
+         "[4 * u + v]; }\n";
   }
-  s += "  }\n}\n";
+  s += "    }\n  }\n}\n";
   return s;
 }
 
@@ -384,7 +396,7 @@ int jx_tape_run(const jx_tape* tape, const float* const* ins, float* const* outs
   CUfunction f;
   int rc = jx::compile_tape(tape, &f);
   if (rc) return rc;
-  const long long work = (n + V - 1) / V;
+  const long long work = (n + 2 * V - 1) / (2 * V);  // threads: 2 groups of V elements each
   long long blocks = (work + 255) / 256;
   const long long cap = (long long)jx::num_sms() * 8;
   if (blocks > cap) blocks = cap;

@@ -213,6 +213,28 @@ def test_transcendental_error_bounds(jx, dev, oracle, op, rel, absol):
     assert np.all(err <= bound), (op, float(x[worst]), y[worst], o[worst])
 
 
+@pytest.mark.parametrize("op,rel,absol", [("exp", 1.5e-6, 0.0), ("tanh", 5e-6, 3e-7), ("sigmoid", 1.5e-6, 1e-30),
+                                          ("gelu", 5e-6, 3e-7)])
+def test_transcendental_overflow_and_special_values(jx, dev, oracle, op, rel, absol):
+    """Arguments where exp overflows or underflows (|x| up to 1e30), infinities
+    and NaN: same infinities and NaNs as the reference, finite values within
+    the bound (results below 2^-126 flush to zero)."""
+    big = np.concatenate([np.linspace(-200, 200, 8001), np.logspace(1, 30, 200), -np.logspace(1, 30, 200)])
+    x = np.concatenate([big, [np.inf, -np.inf, np.nan, 88.7, 88.8, -88.7, -103.9, -104.0]]).astype(np.float32)
+    X, Y = dev.put(x), dev.full(x.shape, 7.0)
+    jx.unary(op, X.data_ptr(), Y.data_ptr(), x.size, dev.stream)
+    y = dev.get(Y).astype(np.float64)
+    o = oracle.unary(op, x).astype(np.float64)
+    assert np.array_equal(np.isnan(y), np.isnan(o)), (op, x[np.isnan(y) != np.isnan(o)])
+    inf = np.isinf(o)
+    assert np.array_equal(y[inf], o[inf])
+    fin = np.isfinite(o) & (np.abs(o) >= 2.0 ** -126)
+    err = np.abs(y[fin] - o[fin])
+    assert np.all(err <= rel * np.abs(o[fin]) + absol), (op, x[fin][np.argmax(err - rel * np.abs(o[fin]))])
+    tiny = np.isfinite(o) & (np.abs(o) < 2.0 ** -126)
+    assert np.all(np.abs(y[tiny]) <= 2.0 ** -126 + absol)
+
+
 def test_tanh_small_arguments_keep_relative_accuracy(jx, dev):
     """Below |x| = 0.05 tanh uses its odd series: relative accuracy holds down
     to the smallest inputs; above it the absolute error stays below 3e-7."""
