@@ -141,9 +141,13 @@ struct Addr {
   __device__ __forceinline__ long long estride() const { return COLS ? w : 1; }
 };
 
-// One CTA: TPC transforms of N = 2^LOGN points; T = N/16 threads each.
+// One CTA: TPC transforms of N = 2^LOGN points; T = N/16 threads each.  The
+// launch bound keeps at least 1024 threads per SM resident (64 registers), so
+// loads of one CTA overlap the butterflies of another.
 template <int LOGN, int TPC, bool COLS, bool INV>
-__global__ void __launch_bounds__(TPC * ((1 << LOGN) / 16)) fft_kernel(const float2* __restrict__ in,
+__global__ void __launch_bounds__(TPC*((1 << LOGN) / 16),
+                                  (TPC * ((1 << LOGN) / 16)) >= 1024 ? 1 : 1024 / (TPC * ((1 << LOGN) / 16)))
+    fft_kernel(const float2* __restrict__ in,
                                                                         float2* __restrict__ out,
                                                                         long long ntrans, Addr<COLS> ad,
                                                                         const float2* __restrict__ tw, float scale) {
