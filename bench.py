@@ -57,6 +57,28 @@ def parse():
     return p.parse_args()
 
 
+# DRAM bytes (read + write) per launch of each workload's dominant kernel at
+# the default size, from one ncu capture of dram__bytes_read.sum +
+# dram__bytes_write.sum (commands and figures: profiles/dram_traffic_by_kernel.md).
+# FFT and conv were captured on a smaller batch and scaled by the batch; their
+# traffic is proportional to it.  None for any other size.
+TRAFFIC = {
+    "sgemm": 4.5905e9 + 0.2583e9,            # gemm_3xtf32_kernel, 8192^3
+    "chain": 1.0738e9 + 1.0275e9,            # jx_tape_kernel, 2^28
+    "rowsum": 1.0738e9 + 0.0039e9,           # reduce_rows_kernel<sum>
+    "argmax": 1.0738e9 + 0.0033e9,           # argreduce_rows_kernel<max>
+    "fullsum": 1.0738e9 + 0.0049e9,          # reduce_all_pass1<sum>
+    "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
+    "fft2d": 8 * (0.2685e9 + 0.2121e9),      # column pass fft_kernel<10,8,cols>, batch 32 x 8
+    "conv": 2 * (0.1082e9 + 0.0551e9 + 0.1079e9 + 0.0530e9 + 0.3201e9 + 0.0709e9),  # 3 conv_gemm_kernel, B 32 x 2
+}
+
+
+def traffic_for(args):
+    default = (args.size == 8192 and not args.fft_batch and not args.conv_batch)
+    return TRAFFIC.get(args.workload) if default else None
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -271,7 +293,7 @@ def run_sgemm(args, dist, jx, torch):
         "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
                      "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
-                     "traffic": None, "kernel_ms": round(kern_ms, 4)},
+                     "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
                 "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": 3 * args.steps,
@@ -321,9 +343,9 @@ def run_chain(args, dist, jx, torch):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
             "config": {"workload": "jit tape y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2 over 2^28 f32 per rank",
                        "l2": "1 GiB in + 1 GiB out > L2"},
-            "roofline": {"bound": "hbm", "kernel": "tape_kernel", "achieved": round(gbs / dist.world, 1),
+            "roofline": {"bound": "hbm", "kernel": "jx_tape_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
-                         "peak_basis": basis, "traffic": None},
+                         "peak_basis": basis, "traffic": traffic_for(args)},
             "gpu_launches": args.steps, "clocks": clocks}
 
 
@@ -372,7 +394,7 @@ def run_reduce(args, dist, jx, torch):
             "config": {"workload": f"{args.workload} over [{rows}, {cols}] f32 per rank", "l2": "1 GiB input > L2"},
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
-                         "traffic": None},
+                         "traffic": traffic_for(args)},
             "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
 
 
@@ -435,7 +457,7 @@ def run_conv_bgemm(args, dist, jx, torch):
                                     if args.workload == "conv" else "split passes + gemm_3xtf32_kernel"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
-                         "traffic": None},
+                         "traffic": traffic_for(args)},
             "clocks": clocks}
 
 
@@ -479,17 +501,30 @@ def run_fft(args, dist, jx, torch):
     clocks = clk.stop()
     nbytes = 2.0 * X.numel() * 4  # algorithmic: one read and one write of the batch
     gbs = nbytes * dist.world / (ms * 1e-3) / 1e9
+    kern_ms, kern_note = ms, ""
+    if launches == 2:
+        # The column pass alone: the row pass is the same kernel launch as a
+        # batched 1-D transform of the h*batch rows, timed the same way.
+        for _ in range(args.warmup):
+            jx.fft_c2c(X.data_ptr(), Y.data_ptr(), w, h * batch, False, s)
+        e0.record(st)
+        for _ in range(args.steps):
+            jx.fft_c2c(X.data_ptr(), Y.data_ptr(), w, h * batch, False, s)
+        e1.record(st)
+        torch.cuda.synchronize()
+        row_ms = e0.elapsed_time(e1) / args.steps
+        kern_ms = max(ms - row_ms, 1e-6)
+        kern, kern_note = "fft_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
     hbm, _, basis = load_peaks()
+    kgbs = nbytes / (kern_ms * 1e-3) / 1e9
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (complex64)", "data": "synthetic N(0,1) real and imaginary parts",
             "config": {"workload": wl, "l2": "2 GiB per pass > L2",
                        "parallelism": f"batch shards x{dist.world}, no collective"},
-            "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
-                         "traffic": None,
-                         "note": "2-D counts one read + one write; the row and column passes move it twice"
-                         if launches == 2 else ""},
+            "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(kgbs, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(kgbs / hbm, 4), "peak_basis": basis,
+                         "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4), "note": kern_note},
             "gpu_launches": args.steps * launches, "clocks": clocks}
 
 
