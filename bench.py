@@ -184,17 +184,147 @@ class Dist:
 # ---------------------------------------------------------------------------
 # CPU reference (oracle) timing -- the only place bench.py runs oracle code
 # ---------------------------------------------------------------------------
-def cpu_sgemm(size, rows, threads, reps=1):
+def _split_run(fn, parts, threads):
+    """Run fn over parts on `threads` host threads (the oracle's C calls
+    release the GIL)."""
+    if threads <= 1 or len(parts) <= 1:
+        return [fn(p) for p in parts]
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(threads) as ex:
+        return list(ex.map(fn, parts))
+
+
+def cpu_measure(args, threads, budget_s=8.0):
+    """The reference's CPU path (the oracle's restatement, same loop order) on
+    a bounded sample of the workload, repeated until about budget_s seconds.
+    Returns (value, unit, seconds per repetition, sample description)."""
     import oracle as O
     O.build()
-    rng = np.random.default_rng(1)
-    a = rng.uniform(-1, 1, (rows, size)).astype(np.float32)
-    b = rng.uniform(-1, 1, (size, size)).astype(np.float32)
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        O.matmul(a, b, nthreads=threads)
-    dt = (time.perf_counter() - t0) / reps
-    return 2.0 * rows * size * size / dt / 1e12, dt
+    wl = args.workload
+    rng = np.random.default_rng(7)
+    par = f"{threads} host thread{'s' if threads > 1 else ''}"
+    if wl == "sgemm":
+        rows = args.cpu_rows
+        a = rng.uniform(-1, 1, (rows, args.size)).astype(np.float32)
+        b = rng.uniform(-1, 1, (args.size, args.size)).astype(np.float32)
+        fn, work, unit = (lambda: O.matmul(a, b, nthreads=threads)), 2.0 * rows * args.size ** 2 / 1e12, "TFLOP/s"
+        sample = f"{rows} rows of the {args.size}^3 product"
+    elif wl == "bgemm":
+        rows, n = 64, 2048
+        a = rng.uniform(-1, 1, (rows, n)).astype(np.float32)
+        b = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+        fn, work, unit = (lambda: O.matmul(a, b, nthreads=threads)), 2.0 * rows * n * n / 1e12, "TFLOP/s"
+        sample = f"{rows} rows of one [2048,2048] x [2048,2048] batch entry"
+    elif wl == "chain":
+        n = 1 << 22
+        x = rng.standard_normal(n).astype(np.float32)
+        parts = np.array_split(x, max(1, threads))
+        fn = lambda: _split_run(lambda p: O.chain_fwd(p, np.float32(1.1), np.float32(0.9)), parts, threads)
+        work, unit, sample = 8.0 * n / 1e9, "GB/s", f"2^22 elements of the 2^28 chain"
+    elif wl in ("rowsum", "argmax"):
+        x = rng.standard_normal((4096, 4096)).astype(np.float32)
+        if wl == "rowsum":
+            fn = lambda: O.reduce_axis(x, 1, "sum", nthreads=threads)
+        else:
+            fn = lambda: O.arg_rows(x, True, nthreads=threads)
+        work, unit, sample = (4.0 * x.size + 4.0 * 4096) / 1e9, "GB/s", "4096 of the 65536 rows"
+    elif wl == "fullsum":
+        n = 1 << 24
+        x = rng.standard_normal(n).astype(np.float32)
+        parts = np.array_split(x, max(1, threads))
+        fn = lambda: _split_run(lambda p: O.reduce_all(p, "sum"), parts, threads)
+        work, unit, sample = 4.0 * n / 1e9, "GB/s", "2^24 of the 2^28 elements"
+    elif wl == "fft1d":
+        x = rng.standard_normal((256, 4096, 2)).astype(np.float32)
+        fn = lambda: O.fft_c2c(x, nthreads=threads)
+        work, unit, sample = 16.0 * 256 * 4096 / 1e9, "GB/s", "256 of the 65536 transforms"
+    elif wl == "fft2d":
+        x = rng.standard_normal((2, 1024, 1024, 2)).astype(np.float32)
+        fn = lambda: O.fft2_c2c(x, nthreads=threads)
+        work, unit, sample = 16.0 * 2 * 1024 * 1024 / 1e9, "GB/s", "2 of the 256 images"
+    elif wl == "conv":
+        C = O_ = 256
+        x = rng.standard_normal((1, C, 56, 56)).astype(np.float32)
+        w = (rng.standard_normal((O_, C, 3, 3)) * np.sqrt(2.0 / (C * 9))).astype(np.float32)
+        g = rng.standard_normal((1, O_, 56, 56)).astype(np.float32)
+
+        def fn():
+            O.conv2d_fwd(x, w, 1, 1, nthreads=threads)
+            O.conv2d_bwd_data(g, w, x.shape, 1, 1, nthreads=threads)
+            O.conv2d_bwd_filter(x, g, w.shape, 1, 1, nthreads=threads)
+        work, unit, sample = 3 * 2.0 * O_ * C * 9 * 56 * 56 / 1e12, "TFLOP/s", "1 of the 64 images, forward + dX + dW"
+    elif wl == "mlp":
+        from oracle import mlp as OM
+        Ws, bs = OM.xavier_params([784, 256, 128, 10])
+        data = OM.batches(4, 128, 784, 10)
+        fn = lambda: OM.train([w.copy() for w in Ws], [b.copy() for b in bs], data, nthreads=threads)
+        work, unit, sample = 4 * 128, "samples/s", "4 training steps of batch 128"
+    elif wl == "wide_mlp":
+        rows = 1
+        widths = [8192] * 5 + [1000]
+        Ws = [rng.uniform(-0.01, 0.01, (widths[i], widths[i + 1])).astype(np.float32) for i in range(5)]
+        xs = [rng.standard_normal((rows, widths[i])).astype(np.float32) for i in range(5)]
+        ds = [rng.standard_normal((rows, widths[i + 1])).astype(np.float32) for i in range(5)]
+
+        def fn():
+            for i in range(5):
+                O.matmul(xs[i], Ws[i], nthreads=threads)                  # forward
+                O.matmul(ds[i], np.ascontiguousarray(Ws[i].T), nthreads=threads)  # dX
+                O.matmul(np.ascontiguousarray(xs[i].T), ds[i], nthreads=threads)  # dW
+        work, unit, sample = rows, "samples/s", f"{rows} sample through the 15 GEMMs of one step (elementwise parts left out)"
+    else:
+        return None
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or reps >= 1000:
+            break
+    per = dt / reps
+    return work / per, unit, per, f"{sample}, {reps} repetition(s) of {per:.3f} s on {par}"
+
+
+def attach_cpu_baseline(line, args, threads=1):
+    r = cpu_measure(args, threads)
+    if r is None:
+        return
+    value, unit, _, sample = r
+    line["cpu_baseline"] = {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
+                            "sample": sample + " (oracle restatement of the reference CPU loop; the reference is "
+                                               "single-threaded)"}
+
+
+def measure_e2e(jx, torch, dist, st, inputs, outputs, step, steps):
+    """End to end through the C ABI: per step, jx_memcpy_h2d of every input
+    from pinned host memory, the step, jx_memcpy_d2h of every output into
+    pinned host memory; CUDA events on the launching stream, max over ranks.
+    Returns (ms per step, h2d bytes per step, d2h bytes per step)."""
+    s = st.cuda_stream
+    hin = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in inputs]
+    for h, d in zip(hin, inputs):
+        h.copy_(d.cpu())
+    hout = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+    nin = [t.numel() * t.element_size() for t in inputs]
+    nout = [t.numel() * t.element_size() for t in outputs]
+
+    def one():
+        for h, d, nb in zip(hin, inputs, nin):
+            jx.call("jx_memcpy_h2d", d.data_ptr(), h.data_ptr(), nb, s)
+        step()
+        for h, d, nb in zip(hout, outputs, nout):
+            jx.call("jx_memcpy_d2h", h.data_ptr(), d.data_ptr(), nb, s)
+
+    one()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        one()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return dist.max(e0.elapsed_time(e1) / steps), sum(nin), sum(nout)
 
 
 # ---------------------------------------------------------------------------
@@ -338,6 +468,7 @@ def run_chain(args, dist, jx, torch):
     bytes_step = 8.0 * n
     gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
     hbm, _, basis = load_peaks()
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], [Y], step, args.e2e_steps)
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
@@ -346,6 +477,8 @@ def run_chain(args, dist, jx, torch):
             "roofline": {"bound": "hbm", "kernel": "jx_tape_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
                          "peak_basis": basis, "traffic": traffic_for(args)},
+            "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps, "clocks": clocks}
 
 
@@ -388,10 +521,14 @@ def run_reduce(args, dist, jx, torch):
     clocks = clk.stop()
     gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
     hbm, _, basis = load_peaks()
+    res = [idx] if args.workload == "argmax" else ([out] if args.workload == "rowsum" else [out[:1]])
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], res, step, args.e2e_steps)
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
             "config": {"workload": f"{args.workload} over [{rows}, {cols}] f32 per rank", "l2": "1 GiB input > L2"},
+            "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
                          "traffic": traffic_for(args)},
@@ -448,6 +585,10 @@ def run_conv_bgemm(args, dist, jx, torch):
     tf = flops * dist.world / (ms * 1e-3) / 1e12
     _, bf16, basis = load_peaks()
     peak = bf16 / 2.0 / 3.0
+    if args.workload == "conv":
+        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X, Wt, G], [Y, DX, DW], step, args.e2e_steps)
+    else:
+        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [A, Bm], [Cm], step, args.e2e_steps)
     return {"metric": METRIC, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": wl,
@@ -458,6 +599,9 @@ def run_conv_bgemm(args, dist, jx, torch):
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
                          "traffic": traffic_for(args)},
+            "e2e": {"value": round(flops * dist.world / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
+            "gpu_launches": args.steps * (10 if args.workload == "conv" else 3),
             "clocks": clocks}
 
 
@@ -517,6 +661,7 @@ def run_fft(args, dist, jx, torch):
         kern, kern_note = "fft_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
     hbm, _, basis = load_peaks()
     kgbs = nbytes / (kern_ms * 1e-3) / 1e9
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], [Y], step, args.e2e_steps)
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (complex64)", "data": "synthetic N(0,1) real and imaginary parts",
@@ -525,6 +670,8 @@ def run_fft(args, dist, jx, torch):
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(kgbs, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(kgbs / hbm, 4), "peak_basis": basis,
                          "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4), "note": kern_note},
+            "e2e": {"value": round(nbytes * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps * launches, "clocks": clocks}
 
 
@@ -675,46 +822,39 @@ def main():
         line = run_conv_bgemm(args, dist, jx, torch)
     else:
         line = run_reduce(args, dist, jx, torch)
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and args.workload == "sgemm":
-        tflops, dt = cpu_sgemm(args.size, args.cpu_rows, 1)
-        line["cpu_baseline"] = {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
-                                "sample": f"{args.cpu_rows} rows of the {args.size}^3 product "
-                                          f"({dt:.1f} s, jax-rs CPU loop order, 1 thread like the reference)"}
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        attach_cpu_baseline(line, args, threads=1)
     dist.close()
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
 
 
 def reference_arm(args):
-    """The reference's CPU implementation of the same workload (oracle restatement)."""
+    """The reference's CPU implementation of the same workload (the oracle's
+    restatement of its loops) on all host threads, a bounded sample per step."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    rows = max(8, args.cpu_rows)
-    if args.workload != "sgemm":
-        print(json.dumps({"impl": "reference", "unavailable": f"reference arm wired for sgemm only"}))
-        return
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_sgemm(args.size, min(rows, 8), threads)
     steps = max(1, min(args.steps, 3))
-    vals, dts = [], []
+    vals, pers, sample, unit = [], [], "", ""
     for _ in range(steps):
-        v, dt = cpu_sgemm(args.size, rows, threads)
+        r = cpu_measure(args, threads, budget_s=4.0)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": f"no CPU restatement for {args.workload}"}))
+            return
+        v, unit, per, sample = r
         vals.append(v)
-        dts.append(dt)
+        pers.append(per)
     value = statistics.median(vals)
-    sample = (f"{rows} rows of the {args.size}^3 product per step (jax-rs CPU loop order, "
-              f"row-parallel over {threads} host threads)")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(dts) * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic U(-1,1)",
-        "config": {"workload": f"sgemm {args.size}x{args.size}x{args.size} f32 (row sample)"},
-        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(pers) * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} (sample of the GPU arm's workload)"},
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
+                         "sample": sample + " (oracle restatement of the reference CPU loop)"},
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
