@@ -675,6 +675,15 @@ def run_fft(args, dist, jx, torch):
             "gpu_launches": args.steps * launches, "clocks": clocks}
 
 
+def mlp_launches(L, exact):
+    """Kernels in one jx_mlp_train_step of L Dense layers: per GEMM 1 (exact) or
+    3 (two tf32 splits + the tcgen05 kernel); forward GEMM + bias/activation per
+    layer; softmax-xent (2); backward dW GEMM + column sums (2) per layer, dh
+    GEMM + activation backward below the top layer; Adam + step counter (2)."""
+    g = 1 if exact else 3
+    return L * (g + 1) + 2 + L * (g + 2) + (L - 1) * (g + 1) + 2
+
+
 def run_mlp(args, dist, jx, torch):
     """MLP training through the native trainer (jx_mlp_train_step).
 
@@ -792,6 +801,7 @@ def run_mlp(args, dist, jx, torch):
         "e2e": {"value": round(samples / (e2e_ms * 1e-3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": (hx.numel() + hy.numel()) * 4, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps * mlp_launches(len(widths) - 1, prec == jx.PREC_EXACT),
         "clocks": clocks,
     }
     if comm is not None:
