@@ -595,13 +595,14 @@ def run_conv_bgemm(args, dist, jx, torch):
                                                                                  "parallelism": f"batch shards x{dist.world}"},
             "roofline": {"bound": "tensor",
                          "kernel": ("conv_gemm_kernel x3 (implicit GEMM; whole step incl. filter/dY splits)"
-                                    if args.workload == "conv" else "split passes + gemm_3xtf32_kernel"),
+                                    if args.workload == "conv" else "gemm_fused_split_kernel (whole batched call)"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
                          "traffic": traffic_for(args)},
             "e2e": {"value": round(flops * dist.world / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
-            "gpu_launches": args.steps * (10 if args.workload == "conv" else 3),
+            "gpu_launches": args.steps * (10 if args.workload == "conv" else
+                                          gemm_kernels(2048, 2048, 2048, False, False, False, batch=64)),
             "clocks": clocks}
 
 
@@ -675,13 +676,32 @@ def run_fft(args, dist, jx, torch):
             "gpu_launches": args.steps * launches, "clocks": clocks}
 
 
-def mlp_launches(L, exact):
-    """Kernels in one jx_mlp_train_step of L Dense layers: per GEMM 1 (exact) or
-    3 (two tf32 splits + the tcgen05 kernel); forward GEMM + bias/activation per
-    layer; softmax-xent (2); backward dW GEMM + column sums (2) per layer, dh
-    GEMM + activation backward below the top layer; Adam + step counter (2)."""
-    g = 1 if exact else 3
-    return L * (g + 1) + 2 + L * (g + 2) + (L - 1) * (g + 1) + 2
+def gemm_kernels(M, N, K, transA, transB, exact, batch=1, sms=148):
+    """Kernels one jx_gemm_f32 call launches: 1 (exact, or the fused-split
+    kernel: untransposed rows of multiples of 4 floats, 250*(1/M + 1/N) > 0.2,
+    at least one 128x256 tile per SM) or 3 (two tf32 split passes + the
+    tcgen05 kernel)."""
+    if exact:
+        return 1
+    tiles = -(-M // 128) * -(-N // 256) * batch
+    fused = (not transA and not transB and K % 4 == 0 and N % 4 == 0 and 250.0 * (1.0 / M + 1.0 / N) > 0.2
+             and tiles >= sms)
+    return 1 if fused else 3
+
+
+def mlp_launches(widths, batch, exact):
+    """Kernels in one jx_mlp_train_step: forward GEMM + bias/activation per
+    layer; softmax-xent (2); backward dW GEMM (A transposed) + column sums (2)
+    per layer, dh GEMM (B transposed) + activation backward below the top
+    layer; Adam + step counter (2)."""
+    L, n = len(widths) - 1, 4
+    for l in range(L):
+        K, N = widths[l], widths[l + 1]
+        n += gemm_kernels(batch, N, K, False, False, exact) + 1
+        n += gemm_kernels(K, N, batch, True, False, exact) + 2
+        if l > 0:
+            n += gemm_kernels(batch, K, N, False, True, exact) + 1
+    return n
 
 
 def run_mlp(args, dist, jx, torch):
@@ -801,7 +821,7 @@ def run_mlp(args, dist, jx, torch):
         "e2e": {"value": round(samples / (e2e_ms * 1e-3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": (hx.numel() + hy.numel()) * 4, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps * mlp_launches(len(widths) - 1, prec == jx.PREC_EXACT),
+        "gpu_launches": args.steps * mlp_launches(widths, batch, prec == jx.PREC_EXACT),
         "clocks": clocks,
     }
     if comm is not None:

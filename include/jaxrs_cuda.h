@@ -74,6 +74,13 @@ JX_API int jx_stream_sync(jx_stream_t stream);
  *      src/ops/linalg.rs:154-237; einsum "bij,bjk->bik" src/ops/einsum.rs:488-523) */
 #define JX_PREC_3XTF32 0 /* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32 */
 #define JX_PREC_EXACT 1  /* sequential-k f32, no FMA: the reference's CPU loop order, bit-exact */
+/* JX_PREC_3XTF32 with the hi/lo split done inside the GEMM kernel from the
+ * caller's f32 buffers: no split pass and no workspace.  Needs untransposed A
+ * and B, 16-byte aligned, lda, ldb and batch strides multiples of 4 (and non-zero
+ * batch strides when batch > 1); otherwise JX_EINVAL.  JX_PREC_3XTF32 already
+ * picks this kernel where it is faster (products of at least one 128x256 tile
+ * per SM with small M or N). */
+#define JX_PREC_3XTF32_FUSED 2
 /* C[b] = op(A[b]) . op(B[b]) for b < batch, row-major.  op(X) = X or X^T per
  * trans flags: A is [M,K] (or [K,M] when transA), B is [K,N] (or [N,K]).
  * lda/ldb/ldc: row strides in elements; stride*: batch strides in elements. */

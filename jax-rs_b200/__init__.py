@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(HERE, "libjaxrs_cuda.so")
 JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, JX_EDEVICE = range(8)
 STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "JX_ENCCL", 5: "JX_ETIMEOUT",
                 6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE"}
-PREC_3XTF32, PREC_EXACT = 0, 1
+PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED = 0, 1, 2
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
       "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12, "gelu_grad": 13}

@@ -18,6 +18,9 @@
 //      The tensor core's internal accumulation truncates; short TMEM sums
 //      keep that bias from growing with K, so the result holds f32 accuracy
 //      at any K.  The epilogue stores C once per tile.
+//   Row-major A and B (no transpose, 16-byte aligned rows) skip the split
+//   pass: gemm_fused_split_kernel streams the raw f32 tiles by TMA (B as an
+//   MN-major operand) and splits them in shared memory.
 // JX_PREC_EXACT: one thread per output, sequential k, no FMA contraction: the
 //   reference CPU loop's exact rounding sequence (bit-identical results).
 #include <algorithm>
@@ -125,6 +128,188 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       if (!ok) break;
       TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+      const int row = ti.m_blk * BM + q * 32 + lane;
+      if (row < M) {
+        float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
+        const int col0 = ti.n_blk * BN + half * EPI_COLS;
+        if (vec_ok && col0 + EPI_COLS <= N) {
+          float4* dst = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+          for (int v = 0; v < EPI_COLS / 4; ++v)
+            dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; ++j)
+            if (col0 + j < N) crow[col0 + j] = acc[j];
+        }
+      }
+    }
+  }
+
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    jxd::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused split: C = A . B with A [batch][M][K] and B [batch][K][N] both
+// row-major, straight from the caller's f32 buffers (no split pass, no
+// workspace).  TMA streams the raw tiles -- A K-major with 128-byte swizzle,
+// B MN-major as eight 32 x 32 boxes in the SWIZZLE_128B_ATOM_32B layout --
+// into the hi slots of the stage; the eight epilogue warps then split every
+// value in place (hi over the raw value, lo into the lo slot, same offset, so
+// the layout is kept), publish the stage to the tensor core and, as in the
+// pre-split kernel, drain the TMEM span partials and store C.  K beyond the
+// matrix reads TMA's zero fill.  Warpgroup 0 (TMA, MMA, two idle warps) gives
+// registers to the two epilogue warpgroups: 128 x 40 + 256 x 232 = 384 x 168.
+// ---------------------------------------------------------------------------
+constexpr int FS_THREADS = 384;
+constexpr int FS_FIRST_EPI = 4;
+constexpr int FS_LAUNCH_REGS = 168;
+constexpr int FS_LOW_REGS = 40;
+constexpr int FS_HIGH_REGS = 232;
+static_assert(128 * FS_LOW_REGS + 256 * FS_HIGH_REGS <= FS_THREADS * FS_LAUNCH_REGS,
+              "register split exceeds the launch allocation");
+constexpr int B_BOX_BYTES = 32 * BK * 4;  // one 32 (N) x 32 (K) box of B
+constexpr size_t FS_SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+__global__ void __launch_bounds__(FS_THREADS, 1)
+    gemm_fused_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            float* __restrict__ C, int M, int N, int num_kb, long long ldc, long long strideC,
+                            int tiles_m, int tiles_n, int num_tiles, unsigned int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = jxd::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* raw_full = bars;                 // [STAGES] TMA landed the raw tiles
+  uint64_t* full = bars + STAGES;            // [STAGES] hi/lo written (epilogue warps -> MMA)
+  uint64_t* empty = bars + 2 * STAGES;       // [STAGES] MMA done with the stage
+  uint64_t* sfull = bars + 3 * STAGES;       // [2] span partial ready
+  uint64_t* sempty = bars + 3 * STAGES + 2;  // [2] span partial drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      jxd::mbar_init(&raw_full[s], 1);
+      jxd::mbar_init(&full[s], EPI_WARPS);
+      jxd::mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      jxd::mbar_init(&sfull[s], 1);
+      jxd::mbar_init(&sempty[s], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    jxd::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    jxd::tma_prefetch_desc(&tmA);
+    jxd::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    jxd::tmem_alloc(tmem_slot, TMEM_COLS);
+    jxd::tmem_relinquish();
+  }
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < FS_FIRST_EPI) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FS_LOW_REGS));
+    // ---------------- TMA: raw A and B tiles ----------------
+    if (warp == 0 && jxd::elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+        const int ya = ti.m_blk * BM, xb = ti.n_blk * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          jxd::mbar_arrive_expect_tx(&raw_full[stage], A_TILE + B_TILE);
+          jxd::tma_load_3d(st, &tmA, &raw_full[stage], kb * BK, ya, ti.b);
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i)
+            jxd::tma_load_3d(st + 2 * A_TILE + i * B_BOX_BYTES, &tmB, &raw_full[stage], xb + 32 * i, kb * BK, ti.b);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        if (!wait_bounded(&empty[stage], phase ^ 1u, err)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // ---------------- MMA issuer ----------------
+    if (warp == 1 && jxd::elect_one())
+      mma_issuer<true>(smem, full, empty, sfull, sempty, tmem_base, num_tiles, num_kb, abort_flag, err);
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FS_HIGH_REGS));
+    // ---------------- split the stage in place, drain spans, store C ----------------
+    const int gt = threadIdx.x - FS_FIRST_EPI * 32;  // 0..255
+    const int q = warp & 3, half = (warp - FS_FIRST_EPI) >> 2;
+    const bool vec_ok = ((ldc & 3) == 0) && ((strideC & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t span_ctr = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+      bool ok = true;
+      int spans_done = 0;
+      const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (*abort_flag || !wait_bounded(&raw_full[stage], phase, err)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + stage * STAGE_BYTES;
+        // 3072 float4 per stage (A: 1024, B: 2048), 12 per thread, consecutive
+        // threads on consecutive 16-byte chunks
+#pragma unroll
+        for (int j = 0; j < (A_TILE + B_TILE) / 16 / 256; ++j) {
+          const int f = gt + 256 * j;
+          uint8_t* hp = f < A_TILE / 16 ? st + f * 16 : st + 2 * A_TILE + (f - A_TILE / 16) * 16;
+          const int lo_off = f < A_TILE / 16 ? A_TILE : B_TILE;
+          const float4 x = *reinterpret_cast<const float4*>(hp);
+          float4 h, l;
+          jxd::split_tf32(x.x, h.x, l.x);
+          jxd::split_tf32(x.y, h.y, l.y);
+          jxd::split_tf32(x.z, h.z, l.z);
+          jxd::split_tf32(x.w, h.w, l.w);
+          *reinterpret_cast<float4*>(hp) = h;
+          *reinterpret_cast<float4*>(hp + lo_off) = l;
+        }
+        jxd::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+        __syncwarp();
+        if (lane == 0) jxd::mbar_arrive(&full[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        // Once span i is fully split, drain span i-1.
+        if ((kb % SPAN_KB == SPAN_KB - 1 || kb == num_kb - 1) && kb >= SPAN_KB) {
+          if (!drain_span<32, FS_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          ++span_ctr;
+          ++spans_done;
+        }
+      }
+      while (ok && spans_done < nspan) {
+        if (!drain_span<32, FS_FIRST_EPI>(acc, tmem_base, span_ctr, sfull, sempty, warp, lane, abort_flag, err))
+          ok = false;
+        ++span_ctr;
+        ++spans_done;
+      }
+      if (!ok) break;
+      const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
       const int row = ti.m_blk * BM + q * 32 + lane;
       if (row < M) {
         float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
@@ -292,6 +477,77 @@ int make_kmajor_map(CUtensorMap* map, const float* base, int Kp, int rows, int b
 
 inline long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
 
+// 3-D f32 tensor map: dims {d0 (contiguous), d1, d2}, byte strides s1, s2,
+// box {b0, b1, 1}, the given swizzle.
+int make_map_3d(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+                uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return jx::fail(JX_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return JX_OK;
+}
+
+// The fused-split kernel reads A and B straight from the caller: both
+// row-major (no transpose), rows and batch entries 16-byte aligned, one batch
+// entry per product (no broadcast operand).
+bool fused_split_ok(const float* A, const float* B, int transA, int transB, long long lda, long long ldb,
+                    long long batch, long long sA, long long sB) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (transA || transB || !a16(A) || !a16(B) || (lda & 3) || (ldb & 3)) return false;
+  if (batch > 1 && (sA <= 0 || sB <= 0 || (sA & 3) || (sB & 3))) return false;
+  return true;
+}
+
+// Per device, once: the fused kernel's shared-memory limit and its register
+// count at launch.
+int fused_prepare(int* regs_out) {
+  static int regs[64] = {0};
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  if (!regs[dev & 63]) {
+    cudaFuncAttributes fa;
+    JX_CUDA(cudaFuncGetAttributes(&fa, gemm_fused_split_kernel));
+    JX_CUDA(cudaFuncSetAttribute(gemm_fused_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FS_SMEM));
+    regs[dev & 63] = fa.numRegs;
+  }
+  if (regs_out) *regs_out = regs[dev & 63];
+  return JX_OK;
+}
+
+int launch_fused_split(const float* A, const float* B, float* C, long long M, long long N, long long K, long long lda,
+                       long long ldb, long long ldc, long long batch, long long sA, long long sB, long long sC,
+                       cudaStream_t st) {
+  int rc = get_encode();
+  if (rc) return rc;
+  // The register split inside the kernel assumes exactly FS_LAUNCH_REGS per
+  // thread at launch; with any other allocation setmaxnreg.inc could wait for
+  // registers that never come, so refuse to launch.
+  int regs = 0;
+  if ((rc = fused_prepare(&regs))) return rc;
+  if (regs != FS_LAUNCH_REGS)
+    return jx::fail(JX_EUNSUPPORTED, "gemm_fused_split_kernel built with %d registers per thread, expected %d",
+                    regs, FS_LAUNCH_REGS);
+  CUtensorMap mA, mB;
+  const uint64_t sa = batch > 1 ? (uint64_t)sA * 4 : (uint64_t)lda * 4 * (uint64_t)M;
+  const uint64_t sb = batch > 1 ? (uint64_t)sB * 4 : (uint64_t)ldb * 4 * (uint64_t)K;
+  if ((rc = make_map_3d(&mA, A, K, M, batch, lda * 4, sa, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = make_map_3d(&mB, B, N, K, batch, ldb * 4, sb, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))) return rc;
+  const int tiles_m = (int)((M + BM - 1) / BM), tiles_n = (int)((N + BN - 1) / BN);
+  const long long nt = (long long)tiles_m * tiles_n * batch;
+  if (nt > 0x7fffffffLL) return jx::fail(JX_EINVAL, "gemm: too many tiles");
+  const int grid = (int)std::min<long long>(nt, jx::num_sms());
+  const int num_kb = (int)((K + BK - 1) / BK);
+  gemm_fused_split_kernel<<<grid, FS_THREADS, FS_SMEM, st>>>(mA, mB, C, (int)M, (int)N, num_kb, ldc, sC, tiles_m,
+                                                             tiles_n, (int)nt, jx::device_error_word());
+  JX_LAUNCH_CHECK("gemm_fused_split_kernel");
+  return JX_OK;
+}
+
 int launch_split(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
                  int batch, bool transposed, cudaStream_t st) {
   if (!transposed) {
@@ -349,7 +605,7 @@ int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float
 // front (jx_init), so no later call -- e.g. one inside a stream capture -- has to.
 int gemm_prepare() {
   JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-  return JX_OK;
+  return fused_prepare(nullptr);
 }
 
 int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
@@ -428,7 +684,23 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
     JX_LAUNCH_CHECK("gemm_exact_kernel");
     return JX_OK;
   }
+  if (precision == JX_PREC_3XTF32_FUSED) {
+    JX_REQUIRE(fused_split_ok(A, B, transA, transB, lda, ldb, batch, strideA, strideB),
+               "matmul: JX_PREC_3XTF32_FUSED needs untransposed, 16-byte aligned operands with lda, ldb and batch "
+               "strides multiples of 4");
+    return launch_fused_split(A, B, C, M, N, K, lda, ldb, ldc, batch, strideA, strideB, strideC, st);
+  }
   JX_REQUIRE(precision == JX_PREC_3XTF32, "matmul: unknown precision %d", precision);
+  // The split pass costs about 250 * (1/M + 1/N) of the main kernel's time
+  // (12 bytes of HBM traffic per operand element against 2*M*N*K flop);
+  // the fused kernel runs about 20% slower than the main kernel (its in-place
+  // split sits on every k-block's critical path with two stages), so it wins
+  // below that crossover, given enough tiles to fill the GPU (a product of a
+  // few tiles is latency-bound, and the longer per-k-block path then costs more).
+  const long long tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+  if (fused_split_ok(A, B, transA, transB, lda, ldb, batch, strideA, strideB) &&
+      250.0 * (1.0 / (double)M + 1.0 / (double)N) > 0.2 && tiles >= jx::num_sms())
+    return launch_fused_split(A, B, C, M, N, K, lda, ldb, ldc, batch, strideA, strideB, strideC, st);
   const long long Kp = round_up(K, BK);
   size_t ws = 0;
   jx_gemm_workspace_size(M, N, K, batch, &ws);

@@ -209,6 +209,21 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major 32-bit tile written by TMA
+// with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B: rows of 32 MN-consecutive values
+// (128 B) one per k, groups of 4 k-rows 512 B apart (SBO), 32-wide MN blocks
+// `mn_block_bytes` apart (LBO), layout type 1 = SWIZZLE_128B_BASE32B (the only
+// MN-major layout tf32 operands accept).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128_32b(uint32_t smem_addr, uint32_t mn_block_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn_block_bytes >> 4) & 0x3FFFu) << 16;  // LBO
+  d |= (uint64_t)((512u >> 4) & 0x3FFFu) << 32;            // SBO
+  d |= (uint64_t)1u << 46;                                  // version
+  d |= (uint64_t)1u << 61;                                  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // Instruction descriptor: kind::tf32, D=f32, A=B=tf32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4)                 // D format f32

@@ -76,10 +76,13 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, uns
 // of two TMEM partial buffers (ping-pong) that the epilogue drains; the
 // tensor core's own accumulation truncates, so keeping each TMEM sum short
 // bounds that bias (over a full K it would grow linearly with K).
+// B_MN: the B tiles are MN-major (row-major B streamed as 32 x 32 boxes, 4 KB
+// apart, in the SWIZZLE_128B_ATOM_32B layout) instead of K-major.
+template <bool B_MN = false>
 __device__ __forceinline__ void mma_issuer(uint8_t* smem, uint64_t* full, uint64_t* empty, uint64_t* sfull,
                                            uint64_t* sempty, uint32_t tmem_base, int num_tiles, int num_kb,
                                            volatile int* abort_flag, unsigned int* err) {
-  constexpr uint32_t idesc = jxd::idesc_tf32(BM, BN);
+  constexpr uint32_t idesc = jxd::idesc_tf32(BM, BN) | (B_MN ? (1u << 16) : 0u);
   int stage = 0;
   uint32_t phase = 0;
   uint32_t span_ctr = 0;
@@ -103,8 +106,15 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, uint64_t* full, uint64
           const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
           const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + off);
           const uint64_t al = jxd::smem_desc_k_sw128(sa_l + off);
-          const uint64_t bh = jxd::smem_desc_k_sw128(sb_h + off);
-          const uint64_t bl = jxd::smem_desc_k_sw128(sb_l + off);
+          uint64_t bh, bl;
+          if constexpr (B_MN) {
+            // 8 k-rows of 128 B per MMA step
+            bh = jxd::smem_desc_mn_sw128_32b(sb_h + k * 1024, 32 * BK * 4);
+            bl = jxd::smem_desc_mn_sw128_32b(sb_l + k * 1024, 32 * BK * 4);
+          } else {
+            bh = jxd::smem_desc_k_sw128(sb_h + off);
+            bl = jxd::smem_desc_k_sw128(sb_l + off);
+          }
           jxd::mma_tf32(d_tmem, al, bh, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           jxd::mma_tf32(d_tmem, ah, bl, idesc, 1u);
           jxd::mma_tf32(d_tmem, ah, bh, idesc, 1u);

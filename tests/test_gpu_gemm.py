@@ -114,6 +114,43 @@ def test_leading_dimensions(jx, dev, oracle):
     assert np.all(c[:, N:] == -7.0)  # untouched padding
 
 
+FUSED_SHAPES = [
+    # (batch, M, N, K, lda_pad, ldb_pad) through JX_PREC_3XTF32_FUSED: the
+    # split inside the kernel (raw f32 tiles by TMA, B MN-major); ragged M, N
+    # and K exercise TMA's zero fill
+    (1, 1, 4, 4, 0, 0), (1, 5, 36, 8, 0, 0), (1, 129, 260, 36, 0, 0), (1, 200, 516, 1028, 0, 0),
+    (1, 300, 4, 100, 0, 0), (3, 96, 300, 132, 0, 0), (2, 130, 264, 68, 4, 8), (1, 1024, 1024, 1024, 0, 0),
+]
+
+
+@pytest.mark.parametrize("bt,M,N,K,pa,pb", FUSED_SHAPES)
+def test_fused_split_path(jx, dev, oracle, bt, M, N, K, pa, pb):
+    ka, kb = oracle.key_from_seed(13 + M).split()
+    a = oracle.uniform_range(ka, bt * M * K, -1, 1).reshape(bt, M, K)
+    b = oracle.uniform_range(kb, bt * K * N, -1, 1).reshape(bt, K, N)
+    abig = np.zeros((bt, M, K + pa), np.float32); abig[:, :, :K] = a
+    bbig = np.zeros((bt, K, N + pb), np.float32); bbig[:, :, :N] = b
+    A, B = dev.put(abig), dev.put(bbig)
+    C = dev.full((bt, M, N), np.nan)
+    jx.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, lda=K + pa, ldb=N + pb, batch=bt,
+            strideA=M * (K + pa), strideB=K * (N + pb), strideC=M * N, precision=jx.PREC_3XTF32_FUSED,
+            stream=dev.stream)
+    c = dev.get(C)
+    ref = oracle.bmm(a, b, nthreads=8)
+    for i in range(bt):
+        assert normwise_rel(c[i], ref[i]) <= TOL
+        ref64 = a[i].astype(np.float64) @ b[i].astype(np.float64)
+        assert normwise_rel(c[i], ref64) <= TOL
+
+
+def test_fused_precision_rejects_transposed_operands(jx, dev):
+    A, B, C = dev.full((8, 8), 1.0), dev.full((8, 8), 1.0), dev.full((8, 8), 0.0)
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), 8, 8, 8, transA=True, precision=jx.PREC_3XTF32_FUSED,
+                stream=dev.stream)
+    assert "JX_PREC_3XTF32_FUSED" in e.value.message
+
+
 def test_8192_cubed_sampled_rows(jx, dev, oracle):
     """Full-size headline shape: every output is computed on the device, and
     16 sampled rows are checked against the oracle's own loop."""
@@ -129,3 +166,21 @@ def test_8192_cubed_sampled_rows(jx, dev, oracle):
     # checksum of checksums: sum over rows of C equals (1^T A) B
     colsum = a.astype(np.float64).sum(0) @ b.astype(np.float64)
     assert normwise_rel(c.astype(np.float64).sum(0), colsum) <= 1e-5
+
+
+def test_many_small_products_default_precision(jx, dev, oracle):
+    """160 products of 256^3 under JX_PREC_3XTF32: enough tiles per SM and small
+    M, N, so the dispatcher takes the fused-split kernel on its own."""
+    bt, n = 160, 256
+    rng = np.random.default_rng(17)
+    a = rng.uniform(-1, 1, (bt, n, n)).astype(np.float32)
+    b = rng.uniform(-1, 1, (bt, n, n)).astype(np.float32)
+    A, B = dev.put(a), dev.put(b)
+    C = dev.full((bt, n, n), np.nan)
+    jx.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), n, n, n, batch=bt, strideA=n * n, strideB=n * n,
+            strideC=n * n, stream=dev.stream)
+    c = dev.get(C)
+    for i in (0, 77, bt - 1):
+        assert normwise_rel(c[i], oracle.matmul(a[i], b[i], nthreads=8)) <= TOL
+    assert normwise_rel(c.astype(np.float64).sum(axis=1), np.einsum("bij,bjk->bk", a.astype(np.float64),
+                                                                    b.astype(np.float64))) <= TOL
