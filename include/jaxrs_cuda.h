@@ -34,6 +34,7 @@ extern "C" {
 #define JX_ETIMEOUT 5    /* a bounded wait (device or host watchdog) expired */
 #define JX_EUNSUPPORTED 6
 #define JX_EDEVICE 7     /* a kernel flagged bad input (see jx_device_status) */
+#define JX_EINTERNAL 8   /* a library invariant did not hold (a bug in this library) */
 
 typedef void *jx_stream_t; /* a cudaStream_t */
 
@@ -181,6 +182,39 @@ JX_API int jx_tape_check(const jx_tape *tape);
 /* ins/outs: host arrays of device pointers, each of n elements. */
 JX_API int jx_tape_run(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
                 jx_stream_t stream);
+
+/* ---- tracer: record, differentiate and fuse elementwise programs
+ *      (TraceContext src/trace/tracer.rs:22-165; IRNode src/trace/ir.rs:8-386;
+ *      find_fusible_groups src/trace/fusion.rs:97-294; VJPEngine
+ *      src/trace/grad.rs:450-837 over src/trace/transpose_rules.rs;
+ *      JitFunction::call src/trace/jit.rs:44-107)
+ * A graph holds nodes over equal-length f32 vectors; node ids come back
+ * through the last argument and are in topological order.  Identical nodes
+ * are shared.  jx_graph_vjp appends, for cotangent nodes cts[i] of outputs
+ * outs[i], the reverse-mode gradient nodes of every wrt[j] into grads[j]
+ * (a zero constant when wrt[j] does not reach any output).  jx_graph_compile
+ * fuses the nodes the outputs need into op-tapes (as many as the tape limits
+ * require, with scratch buffers between them); jx_program_run runs them:
+ * ins[i] is graph input i (in jx_graph_input call order), outs[j] receives
+ * outs[j] of the compile call, all of n elements. */
+typedef struct jx_graph jx_graph;
+typedef struct jx_program jx_program;
+JX_API int jx_graph_create(jx_graph **out);
+JX_API int jx_graph_destroy(jx_graph *g);
+JX_API int jx_graph_input(jx_graph *g, int *node);
+JX_API int jx_graph_const(jx_graph *g, float value, int *node);
+JX_API int jx_graph_unary(jx_graph *g, int op /* JX_UN_* */, int x, int *node);
+JX_API int jx_graph_binary(jx_graph *g, int op /* JX_BIN_* */, int x, int y, int *node);
+JX_API int jx_graph_select_gt(jx_graph *g, int x, int y, int *node); /* x > 0 ? y : 0 */
+JX_API int jx_graph_size(const jx_graph *g, int *n_nodes, int *n_inputs);
+JX_API int jx_graph_vjp(jx_graph *g, int n_out, const int *outs, const int *cts, int n_wrt, const int *wrt,
+                        int *grads);
+JX_API int jx_graph_compile(const jx_graph *g, int n_out, const int *outs, jx_program **out);
+JX_API int jx_program_info(const jx_program *p, int *n_tapes, int *n_inputs, int *n_outputs, int *n_scratch);
+JX_API int jx_program_tape(const jx_program *p, int index, const jx_tape **tape);
+JX_API int jx_program_run(const jx_program *p, const float *const *ins, float *const *outs, int64_t n,
+                          jx_stream_t stream);
+JX_API int jx_program_destroy(jx_program *p);
 
 /* ---- reductions (gpu_reduce_all src/backend/ops.rs:639-643; reduce_axis
  *      src/ops/reduce.rs:53-135; argmax/argmin src/ops/reduce.rs:281-309) ---- */

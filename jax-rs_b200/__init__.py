@@ -17,9 +17,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libjaxrs_cuda.so")
 
 # status codes (include/jaxrs_cuda.h)
-JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, JX_EDEVICE = range(8)
+JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, JX_EDEVICE, JX_EINTERNAL = range(9)
 STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "JX_ENCCL", 5: "JX_ETIMEOUT",
-                6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE"}
+                6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE", 8: "JX_EINTERNAL"}
 PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED = 0, 1, 2
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
@@ -73,6 +73,21 @@ _SIGS = {
     "jx_tape_source": [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
     "jx_tape_check": [vp],
     "jx_tape_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
+    "jx_graph_create": [C.POINTER(vp)],
+    "jx_graph_destroy": [vp],
+    "jx_graph_input": [vp, C.POINTER(C.c_int)],
+    "jx_graph_const": [vp, cf, C.POINTER(C.c_int)],
+    "jx_graph_unary": [vp, C.c_int, C.c_int, C.POINTER(C.c_int)],
+    "jx_graph_binary": [vp, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)],
+    "jx_graph_select_gt": [vp, C.c_int, C.c_int, C.POINTER(C.c_int)],
+    "jx_graph_size": [vp, C.POINTER(C.c_int), C.POINTER(C.c_int)],
+    "jx_graph_vjp": [vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, C.POINTER(C.c_int),
+                     C.POINTER(C.c_int)],
+    "jx_graph_compile": [vp, C.c_int, C.POINTER(C.c_int), C.POINTER(vp)],
+    "jx_program_info": [vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)],
+    "jx_program_tape": [vp, C.c_int, C.POINTER(vp)],
+    "jx_program_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
+    "jx_program_destroy": [vp],
     "jx_reduce_all_f32": [vp, vp, i64, ci, vp],
     "jx_reduce_axis_f32": [vp, vp, i64, i64, i64, ci, vp],
     "jx_argreduce_rows_f32": [vp, vp, vp, i64, i64, ci, vp],

@@ -207,7 +207,7 @@ std::string codegen(const jx_tape* t) {
     int nx = 0;
     for (size_t i = 0; i < t->code.size(); ++i) {
       const int4& c = t->code[i];
-      src_name[i] = rn[c.z];
+      if (c.x != JX_OP_CONST) src_name[i] = rn[c.z];  // a constant's src0 is a constant slot, not a register
       if (c.x != JX_OP_STORE) rn[c.y] = "t" + std::to_string(nx++);
     }
   }
