@@ -43,7 +43,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "chain", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
+                   choices=["sgemm", "chain", "chain_grad", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
                             "conv", "bgemm"])
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer")
@@ -221,6 +221,12 @@ def cpu_measure(args, threads, budget_s=8.0):
         parts = np.array_split(x, max(1, threads))
         fn = lambda: _split_run(lambda p: O.chain_fwd(p, np.float32(1.1), np.float32(0.9)), parts, threads)
         work, unit, sample = 8.0 * n / 1e9, "GB/s", f"2^22 elements of the 2^28 chain"
+    elif wl == "chain_grad":
+        n = 1 << 22
+        x = rng.standard_normal(n).astype(np.float32)
+        parts = np.array_split(x, max(1, threads))
+        fn = lambda: _split_run(lambda p: O.chain_vjp(p, np.float32(1.1), np.float32(0.9)), parts, threads)
+        work, unit, sample = 12.0 * n / 1e9, "GB/s", f"2^22 elements of the 2^28 chain, value and gradient"
     elif wl in ("rowsum", "argmax"):
         x = rng.standard_normal((4096, 4096)).astype(np.float32)
         if wl == "rowsum":
@@ -433,6 +439,9 @@ def run_sgemm(args, dist, jx, torch):
 
 
 def run_chain(args, dist, jx, torch):
+    """chain: the fused forward y = gelu(x*a+b)*sigmoid(x) - tanh(x)/2 as a
+    hand-written op-tape.  chain_grad: value_and_grad of the same function
+    through the tracer (forward + VJP with a ones cotangent), y and dx out."""
     n = 1 << 28
     dev = torch.device("cuda", dist.local)
     st = torch.cuda.current_stream()
@@ -441,15 +450,24 @@ def run_chain(args, dist, jx, torch):
     g.manual_seed(2 + dist.rank)
     X = torch.randn(n, device=dev, generator=g)
     Y = torch.empty_like(X)
-    U, B = jx.OP_UNARY, jx.OP_BINARY
-    code = [(jx.OP_CONST, 1, 0, 0), (jx.OP_CONST, 2, 1, 0), (jx.OP_CONST, 3, 2, 0),
-            (B + jx.BIN["mul"], 4, 0, 1), (B + jx.BIN["add"], 4, 4, 2), (U + jx.UN["gelu"], 4, 4, 0),
-            (U + jx.UN["sigmoid"], 5, 0, 0), (B + jx.BIN["mul"], 4, 4, 5), (U + jx.UN["tanh"], 5, 0, 0),
-            (B + jx.BIN["div"], 5, 5, 3), (B + jx.BIN["sub"], 4, 4, 5), (jx.OP_STORE, 0, 4, 0)]
-    tape = jx.Tape(code, [1.1, 0.9, 2.0], 1, 1)
+    grad = args.workload == "chain_grad"
+    if grad:
+        tr = importlib.import_module("jax-rs_b200.trace")
+        DX = torch.empty_like(X)
+        prog = tr.value_and_grad(lambda x: tr.gelu(x * 1.1 + 0.9) * tr.sigmoid(x) - tr.tanh(x) / 2, 1)
 
-    def step():
-        tape.run([X.data_ptr()], [Y.data_ptr()], n, s)
+        def step():
+            prog.run([X.data_ptr()], [Y.data_ptr(), DX.data_ptr()], n, s)
+    else:
+        U, B = jx.OP_UNARY, jx.OP_BINARY
+        code = [(jx.OP_CONST, 1, 0, 0), (jx.OP_CONST, 2, 1, 0), (jx.OP_CONST, 3, 2, 0),
+                (B + jx.BIN["mul"], 4, 0, 1), (B + jx.BIN["add"], 4, 4, 2), (U + jx.UN["gelu"], 4, 4, 0),
+                (U + jx.UN["sigmoid"], 5, 0, 0), (B + jx.BIN["mul"], 4, 4, 5), (U + jx.UN["tanh"], 5, 0, 0),
+                (B + jx.BIN["div"], 5, 5, 3), (B + jx.BIN["sub"], 4, 4, 5), (jx.OP_STORE, 0, 4, 0)]
+        tape = jx.Tape(code, [1.1, 0.9, 2.0], 1, 1)
+
+        def step():
+            tape.run([X.data_ptr()], [Y.data_ptr()], n, s)
 
     for _ in range(args.warmup):
         step()
@@ -465,15 +483,17 @@ def run_chain(args, dist, jx, torch):
     torch.cuda.synchronize()
     ms = dist.max(e0.elapsed_time(e1) / args.steps)
     clocks = clk.stop()
-    bytes_step = 8.0 * n
+    bytes_step = (12.0 if grad else 8.0) * n
     gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
     hbm, _, basis = load_peaks()
-    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], [Y], step, args.e2e_steps)
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], [Y, DX] if grad else [Y], step, args.e2e_steps)
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
-            "config": {"workload": "jit tape y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2 over 2^28 f32 per rank",
-                       "l2": "1 GiB in + 1 GiB out > L2"},
+            "config": {"workload": ("value_and_grad (tracer) of y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2, y and dx, "
+                                    "over 2^28 f32 per rank" if grad else
+                                    "jit tape y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2 over 2^28 f32 per rank"),
+                       "l2": "1 GiB in + 1 GiB out > L2", "bytes_per_element": 12 if grad else 8},
             "roofline": {"bound": "hbm", "kernel": "jx_tape_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
                          "peak_basis": basis, "traffic": traffic_for(args)},
@@ -842,7 +862,7 @@ def main():
     jx.init(dist.local)
     if args.workload == "sgemm":
         line = run_sgemm(args, dist, jx, torch)
-    elif args.workload == "chain":
+    elif args.workload in ("chain", "chain_grad"):
         line = run_chain(args, dist, jx, torch)
     elif args.workload in ("mlp", "wide_mlp"):
         line = run_mlp(args, dist, jx, torch)
