@@ -183,6 +183,21 @@ JX_API int jx_tape_check(const jx_tape *tape);
 JX_API int jx_tape_run(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
                 jx_stream_t stream);
 
+/* ---- random streams (PRNGKey src/random.rs:15-97; uniform_range :161-181;
+ *      randint :189-210; normal's CPU arm :259-285)
+ * (s0, s1) is a PRNGKey's state.  out[i] is exactly what the reference's
+ * host loop writes at position i for the same key: uniform and randint
+ * bit-identical, normal (Box-Muller, cos then sin per pair) within a few ulp
+ * (CUDA's logf/cosf/sinf against glibc).  The device reaches position i by a
+ * GF(2) jump-ahead of the xorshift128+ state, so any n runs fully parallel. */
+JX_API int jx_random_uniform_f32(uint64_t s0, uint64_t s1, float *out, int64_t n, float minval, float maxval,
+                                 jx_stream_t stream);
+JX_API int jx_random_randint_f32(uint64_t s0, uint64_t s1, float *out, int64_t n, int32_t minval, int32_t maxval,
+                                 jx_stream_t stream);
+JX_API int jx_random_normal_f32(uint64_t s0, uint64_t s1, float *out, int64_t n, jx_stream_t stream);
+/* Host: advance a key's state by `steps` draws of next_u64 (no GPU needed). */
+JX_API int jx_random_jump(uint64_t *s0, uint64_t *s1, uint64_t steps);
+
 /* ---- tracer: record, differentiate and fuse elementwise programs
  *      (TraceContext src/trace/tracer.rs:22-165; IRNode src/trace/ir.rs:8-386;
  *      find_fusible_groups src/trace/fusion.rs:97-294; VJPEngine

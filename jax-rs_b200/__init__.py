@@ -73,6 +73,10 @@ _SIGS = {
     "jx_tape_source": [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
     "jx_tape_check": [vp],
     "jx_tape_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
+    "jx_random_uniform_f32": [C.c_uint64, C.c_uint64, vp, i64, cf, cf, vp],
+    "jx_random_randint_f32": [C.c_uint64, C.c_uint64, vp, i64, C.c_int32, C.c_int32, vp],
+    "jx_random_normal_f32": [C.c_uint64, C.c_uint64, vp, i64, vp],
+    "jx_random_jump": [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_uint64],
     "jx_graph_create": [C.POINTER(vp)],
     "jx_graph_destroy": [vp],
     "jx_graph_input": [vp, C.POINTER(C.c_int)],
