@@ -43,7 +43,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "chain", "chain_grad", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
+                   choices=["sgemm", "chain", "chain_grad", "rng", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
                             "conv", "bgemm"])
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer")
@@ -221,6 +221,11 @@ def cpu_measure(args, threads, budget_s=8.0):
         parts = np.array_split(x, max(1, threads))
         fn = lambda: _split_run(lambda p: O.chain_fwd(p, np.float32(1.1), np.float32(0.9)), parts, threads)
         work, unit, sample = 8.0 * n / 1e9, "GB/s", f"2^22 elements of the 2^28 chain"
+    elif wl == "rng":
+        n = 1 << 24
+        k = O.key_from_seed(1).split()[0]
+        fn = lambda: O.uniform_range(k, n, -1.0, 1.0)
+        work, unit, sample = 4.0 * n / 1e9, "GB/s", "2^24 of the 2^28 draws (the stream is sequential: 1 thread)"
     elif wl == "chain_grad":
         n = 1 << 22
         x = rng.standard_normal(n).astype(np.float32)
@@ -495,6 +500,50 @@ def run_chain(args, dist, jx, torch):
                                     "jit tape y=gelu(x*a+b)*sigmoid(x)-tanh(x)/2 over 2^28 f32 per rank"),
                        "l2": "1 GiB in + 1 GiB out > L2", "bytes_per_element": 12 if grad else 8},
             "roofline": {"bound": "hbm", "kernel": "jx_tape_kernel", "achieved": round(gbs / dist.world, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
+                         "peak_basis": basis, "traffic": traffic_for(args)},
+            "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
+            "gpu_launches": args.steps, "clocks": clocks}
+
+
+def run_rng(args, dist, jx, torch):
+    """uniform_range(key, [2^28], -1, 1) on the device: the reference's host
+    stream reproduced by jump-ahead (4 B written per value)."""
+    n = 1 << 28
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    Y = torch.empty(n, device=dev)
+    key = jx.key_split(jx.key_from_seed(1 + dist.rank))[0]
+
+    def step():
+        jx.call("jx_random_uniform_f32", key[0], key[1], Y.data_ptr(), n, -1.0, 1.0, s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    bytes_step = 4.0 * n
+    gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
+    hbm, _, basis = load_peaks()
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [], [Y], step, args.e2e_steps)
+    return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 state -> f32", "data": "PRNGKey::from_seed(1).split().0 stream",
+            "config": {"workload": "uniform_range(key, [2^28], -1, 1) per rank (xorshift128+ stream, jump-ahead)",
+                       "l2": "1 GiB out > L2"},
+            "roofline": {"bound": "hbm", "kernel": "rng_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
                          "peak_basis": basis, "traffic": traffic_for(args)},
             "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -864,6 +913,8 @@ def main():
         line = run_sgemm(args, dist, jx, torch)
     elif args.workload in ("chain", "chain_grad"):
         line = run_chain(args, dist, jx, torch)
+    elif args.workload == "rng":
+        line = run_rng(args, dist, jx, torch)
     elif args.workload in ("mlp", "wide_mlp"):
         line = run_mlp(args, dist, jx, torch)
     elif args.workload in ("fft1d", "fft2d"):

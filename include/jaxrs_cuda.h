@@ -197,6 +197,9 @@ JX_API int jx_random_randint_f32(uint64_t s0, uint64_t s1, float *out, int64_t n
 JX_API int jx_random_normal_f32(uint64_t s0, uint64_t s1, float *out, int64_t n, jx_stream_t stream);
 /* Host: advance a key's state by `steps` draws of next_u64 (no GPU needed). */
 JX_API int jx_random_jump(uint64_t *s0, uint64_t *s1, uint64_t steps);
+/* Host: PRNGKey::from_seed and PRNGKey::split (src/random.rs:29-48). */
+JX_API int jx_random_key_from_seed(uint64_t seed, uint64_t *s0, uint64_t *s1);
+JX_API int jx_random_key_split(uint64_t s0, uint64_t s1, uint64_t *a0, uint64_t *a1, uint64_t *b0, uint64_t *b1);
 
 /* ---- tracer: record, differentiate and fuse elementwise programs
  *      (TraceContext src/trace/tracer.rs:22-165; IRNode src/trace/ir.rs:8-386;

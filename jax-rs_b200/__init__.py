@@ -77,6 +77,8 @@ _SIGS = {
     "jx_random_randint_f32": [C.c_uint64, C.c_uint64, vp, i64, C.c_int32, C.c_int32, vp],
     "jx_random_normal_f32": [C.c_uint64, C.c_uint64, vp, i64, vp],
     "jx_random_jump": [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_uint64],
+    "jx_random_key_from_seed": [C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)],
+    "jx_random_key_split": [C.c_uint64, C.c_uint64] + [C.POINTER(C.c_uint64)] * 4,
     "jx_graph_create": [C.POINTER(vp)],
     "jx_graph_destroy": [vp],
     "jx_graph_input": [vp, C.POINTER(C.c_int)],
@@ -351,3 +353,17 @@ class MLP:
                 _lib.jx_mlp_destroy(self.handle)
         except Exception:
             pass
+
+
+def key_from_seed(seed):
+    """PRNGKey::from_seed (src/random.rs:29-32) -> (s0, s1)."""
+    a, b = C.c_uint64(), C.c_uint64()
+    call("jx_random_key_from_seed", seed, C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def key_split(key):
+    """PRNGKey::split (src/random.rs:35-48) -> ((s0, s1), (s0, s1))."""
+    v = [C.c_uint64() for _ in range(4)]
+    call("jx_random_key_split", key[0], key[1], *[C.byref(x) for x in v])
+    return (v[0].value, v[1].value), (v[2].value, v[3].value)

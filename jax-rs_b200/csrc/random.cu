@@ -282,6 +282,26 @@ int launch_rng(uint64_t s0, uint64_t s1, float* out, long long n, float lo, floa
 
 extern "C" {
 
+// PRNGKey::from_seed (src/random.rs:29-32): [seed, seed * 0x9e3779b97f4a7c15]
+int jx_random_key_from_seed(uint64_t seed, uint64_t* s0, uint64_t* s1) {
+  JX_REQUIRE(s0 && s1, "jx_random_key_from_seed: NULL");
+  *s0 = seed;
+  *s1 = seed * 0x9e3779b97f4a7c15ull;
+  return JX_OK;
+}
+
+// PRNGKey::split (src/random.rs:35-48): the first key adds 0x9e3779b97f4a7c15
+// to word 0 and rotates word 1 left by 27; the second adds 0x3c6ef372fe94f82a
+// and rotates right by 17.
+int jx_random_key_split(uint64_t s0, uint64_t s1, uint64_t* a0, uint64_t* a1, uint64_t* b0, uint64_t* b1) {
+  JX_REQUIRE(a0 && a1 && b0 && b1, "jx_random_key_split: NULL");
+  *a0 = s0 + 0x9e3779b97f4a7c15ull;
+  *a1 = (s1 << 27) | (s1 >> 37);
+  *b0 = s0 + 0x3c6ef372fe94f82aull;
+  *b1 = (s1 >> 17) | (s1 << 47);
+  return JX_OK;
+}
+
 int jx_random_jump(uint64_t* s0, uint64_t* s1, uint64_t steps) {
   JX_REQUIRE(s0 && s1, "jx_random_jump: NULL");
   int rc = poly_init();

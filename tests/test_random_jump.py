@@ -17,3 +17,14 @@ def test_jump_equals_stepping(oracle, steps):
     for _ in range(steps):
         oracle.next_u64(k)
     assert (a.value, b.value) == (k.s0, k.s1)
+
+
+@pytest.mark.parametrize("seed", [0, 1, 42, 2 ** 63 + 5])
+def test_key_from_seed_and_split_match_the_oracle(oracle, seed):
+    jx = importlib.import_module("jax-rs_b200")
+    k = jx.key_from_seed(seed)
+    ko = oracle.key_from_seed(seed)
+    assert k == (ko.s0, ko.s1)
+    a, b = jx.key_split(k)
+    ao, bo = ko.split()
+    assert a == (ao.s0, ao.s1) and b == (bo.s0, bo.s1)
