@@ -13,9 +13,9 @@
 // characteristic polynomial P (found once on the host by Berlekamp-Massey on
 // one state bit).  Advancing j steps is M^j s = sum_i q_i M^i s for
 // q(x) = x^j mod P(x): 128 generator steps with a conditional XOR each,
-// whatever j is.  The host precomputes q for every block start and every
-// thread offset inside a block (jump tables, cached per device); each thread
-// makes two jumps, then draws RNG_DRAWS values in order and writes them
+// whatever j is.  The host precomputes q for every chunk's start (a jump
+// table cached per device); each thread jumps to two chunks and draws them
+// side by side (two independent dependency chains), and writes them
 // through a per-warp shared-memory transpose so every store is a 128-byte
 // row.  uniform and randint are bit-identical to the host stream; normal
 // uses CUDA's logf/cosf/sinf (within a few ulp of glibc) with the
@@ -29,7 +29,7 @@
 namespace {
 
 constexpr int RNG_THREADS = 256;
-constexpr int RNG_DRAWS = 1024;  // draws per thread (uniform/randint: values; normal: 512 pairs)
+constexpr int RNG_CHUNK = 1024;  // draws per chunk; each thread draws two chunks side by side
 
 struct P128 {
   uint64_t lo = 0, hi = 0;
@@ -163,40 +163,27 @@ int poly_init() {
   return JX_OK;
 }
 
-// Per device: jump polynomials for thread offsets t*RNG_DRAWS (t < 256) and
-// block starts b*256*RNG_DRAWS (b < cap, grown on demand).
+// Per device: the jump polynomial x^(c * RNG_CHUNK) mod P of every chunk c
+// (grown on demand; 16 B per chunk).
 struct Tables {
-  ulonglong2* thread_q = nullptr;
-  ulonglong2* block_q = nullptr;
-  long long blocks = 0;
+  ulonglong2* q = nullptr;
+  long long threads = 0;
 };
 Tables g_tab[64];
 std::mutex g_tab_mu;
 
-int tables(long long blocks, const ulonglong2** tq, const ulonglong2** bq) {
+int tables(long long chunks, const ulonglong2** q) {
   int rc = poly_init();
   if (rc) return rc;
   int dev = 0;
   JX_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_tab_mu);
   Tables& t = g_tab[dev & 63];
-  const P128& p = g_poly.p;
-  if (!t.thread_q) {
-    std::vector<ulonglong2> h(RNG_THREADS);
-    const P128 step = powx(RNG_DRAWS, p);
-    P128 cur;
-    cur.lo = 1;
-    for (int i = 0; i < RNG_THREADS; ++i) {
-      h[i] = make_ulonglong2(cur.lo, cur.hi);
-      cur = mulmod(cur, step, p);
-    }
-    JX_CUDA(cudaMalloc(&t.thread_q, sizeof(ulonglong2) * RNG_THREADS));
-    JX_CUDA(cudaMemcpy(t.thread_q, h.data(), sizeof(ulonglong2) * RNG_THREADS, cudaMemcpyHostToDevice));
-  }
-  if (t.blocks < blocks) {
-    long long cap = std::max<long long>(blocks, 8192);
+  if (t.threads < chunks) {
+    const P128& p = g_poly.p;
+    const long long cap = std::max<long long>(chunks, 1LL << 18);
     std::vector<ulonglong2> h(cap);
-    const P128 step = powx((uint64_t)RNG_THREADS * RNG_DRAWS, p);
+    const P128 step = powx(RNG_CHUNK, p);
     P128 cur;
     cur.lo = 1;
     for (long long i = 0; i < cap; ++i) {
@@ -206,58 +193,91 @@ int tables(long long blocks, const ulonglong2** tq, const ulonglong2** bq) {
     ulonglong2* d = nullptr;
     JX_CUDA(cudaMalloc(&d, sizeof(ulonglong2) * cap));
     JX_CUDA(cudaMemcpy(d, h.data(), sizeof(ulonglong2) * cap, cudaMemcpyHostToDevice));
-    if (t.block_q) cudaFree(t.block_q);
-    t.block_q = d;
-    t.blocks = cap;
+    if (t.q) JX_CUDA(cudaFree(t.q));
+    t.q = d;
+    t.threads = cap;
   }
-  *tq = t.thread_q;
-  *bq = t.block_q;
+  *q = t.q;
   return JX_OK;
 }
 
 // ---- device -----------------------------------------------------------------
-__device__ __forceinline__ float u24(uint64_t u) { return __fmul_rn((float)(u >> 40), 5.9604644775390625e-8f); }
+__device__ __forceinline__ float u24(uint64_t u) {
+  return __fmul_rn((float)(uint32_t)(u >> 40), 5.9604644775390625e-8f);  // top 24 bits / 2^24, exact
+}
 
 enum { RNG_UNIFORM = 0, RNG_RANDINT = 1, RNG_NORMAL = 2 };
 
+// two states advanced side by side (independent chains: twice the
+// instruction-level parallelism of one)
+__device__ __forceinline__ void xs_jump2(uint64_t& a0, uint64_t& b0, ulonglong2 q0, uint64_t& a1, uint64_t& b1,
+                                         ulonglong2 q1) {
+  uint64_t r0 = 0, t0 = 0, r1 = 0, t1 = 0;
+#pragma unroll 4
+  for (int i = 0; i < 128; ++i) {
+    const uint64_t m0 = 0ull - ((i < 64 ? q0.x >> i : q0.y >> (i - 64)) & 1ull);
+    const uint64_t m1 = 0ull - ((i < 64 ? q1.x >> i : q1.y >> (i - 64)) & 1ull);
+    r0 ^= a0 & m0;
+    t0 ^= b0 & m0;
+    r1 ^= a1 & m1;
+    t1 ^= b1 & m1;
+    xs_next(a0, b0);
+    xs_next(a1, b1);
+  }
+  a0 = r0;
+  b0 = t0;
+  a1 = r1;
+  b1 = t1;
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(RNG_THREADS) rng_kernel(uint64_t s0, uint64_t s1, const ulonglong2* __restrict__ bq,
-                                                        const ulonglong2* __restrict__ tq, float* __restrict__ out,
-                                                        long long n, float lo, float width, uint64_t range,
-                                                        int minval) {
+__device__ __forceinline__ void emit2(float* row, int jj, uint64_t& a, uint64_t& b, float lo, float width,
+                                      uint64_t range, int minval) {
+  if constexpr (MODE == RNG_NORMAL) {
+    float u1 = u24(xs_next(a, b));
+    const float u2 = u24(xs_next(a, b));
+    u1 = fmaxf(u1, 1e-10f);
+    const float r = __fsqrt_rn(__fmul_rn(-2.0f, logf(u1)));
+    const float theta = __fmul_rn(6.28318548202514648438f, u2);  // 2.0f * PI (exact doubling)
+    row[jj] = __fmul_rn(r, cosf(theta));
+    row[jj + 1] = __fmul_rn(r, sinf(theta));
+  } else {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint64_t u = xs_next(a, b);
+      if constexpr (MODE == RNG_UNIFORM) row[jj + k] = __fadd_rn(lo, __fmul_rn(width, u24(u)));
+      else row[jj + k] = (float)((int)(u % range) + minval);
+    }
+  }
+}
+
+// Thread g draws chunks 2g and 2g+1 (RNG_CHUNK values each, starting at
+// chunk * RNG_CHUNK), 16 of each per step into its row of the warp's tile
+// (columns 0-15 chunk 2g, 16-31 chunk 2g+1); the warp then writes row by row,
+// each store two 64-byte segments.
+template <int MODE>
+__global__ void __launch_bounds__(RNG_THREADS) rng_kernel(uint64_t s0, uint64_t s1, const ulonglong2* __restrict__ tq,
+                                                        float* __restrict__ out, long long n, float lo, float width,
+                                                        uint64_t range, int minval) {
   __shared__ float tile[RNG_THREADS / 32][32][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long warp_first = (long long)blockIdx.x * RNG_THREADS + warp * 32;  // global thread of lane 0
-  if (warp_first * RNG_DRAWS >= n) return;  // whole warp past the end
-  uint64_t a = s0, b = s1;
-  const ulonglong2 qb = bq[blockIdx.x], qt = tq[threadIdx.x];
-  xs_jump(a, b, qb.x, qb.y);
-  xs_jump(a, b, qt.x, qt.y);
+  if (warp_first * 2 * RNG_CHUNK >= n) return;  // whole warp past the end
+  const long long g = warp_first + lane;
+  uint64_t a0 = s0, b0 = s1, a1 = s0, b1 = s1;
+  xs_jump2(a0, b0, tq[2 * g], a1, b1, tq[2 * g + 1]);
   float (*T)[33] = tile[warp];
-  for (int j0 = 0; j0 < RNG_DRAWS; j0 += 32) {
-    if constexpr (MODE == RNG_NORMAL) {
-#pragma unroll 4
-      for (int jj = 0; jj < 32; jj += 2) {
-        float u1 = u24(xs_next(a, b));
-        const float u2 = u24(xs_next(a, b));
-        u1 = fmaxf(u1, 1e-10f);
-        const float r = __fsqrt_rn(__fmul_rn(-2.0f, logf(u1)));
-        const float theta = __fmul_rn(6.28318548202514648438f, u2);  // 2.0f * PI (exact doubling)
-        T[lane][jj] = __fmul_rn(r, cosf(theta));
-        T[lane][jj + 1] = __fmul_rn(r, sinf(theta));
-      }
-    } else {
-#pragma unroll 8
-      for (int jj = 0; jj < 32; ++jj) {
-        const uint64_t u = xs_next(a, b);
-        if constexpr (MODE == RNG_UNIFORM) T[lane][jj] = __fadd_rn(lo, __fmul_rn(width, u24(u)));
-        else T[lane][jj] = (float)((int)(u % range) + minval);
-      }
+  for (int j0 = 0; j0 < RNG_CHUNK; j0 += 16) {
+#pragma unroll 2
+    for (int jj = 0; jj < 16; jj += 2) {
+      emit2<MODE>(T[lane], jj, a0, b0, lo, width, range, minval);
+      emit2<MODE>(T[lane] + 16, jj, a1, b1, lo, width, range, minval);
     }
     __syncwarp();
+    const int c = lane >> 4, col = lane & 15;
 #pragma unroll 4
     for (int r = 0; r < 32; ++r) {
-      const long long idx = (warp_first + r) * RNG_DRAWS + j0 + lane;
+      const long long idx = (2 * (warp_first + r) + c) * RNG_CHUNK + j0 + col;
       if (idx < n) __stcs(out + idx, T[r][lane]);
     }
     __syncwarp();
@@ -267,13 +287,13 @@ __global__ void __launch_bounds__(RNG_THREADS) rng_kernel(uint64_t s0, uint64_t 
 template <int MODE>
 int launch_rng(uint64_t s0, uint64_t s1, float* out, long long n, float lo, float width, uint64_t range, int minval,
                cudaStream_t st) {
-  const long long per_block = (long long)RNG_THREADS * RNG_DRAWS;
+  const long long per_block = (long long)RNG_THREADS * 2 * RNG_CHUNK;
   const long long blocks = (n + per_block - 1) / per_block;
   JX_REQUIRE(blocks < (1LL << 31), "random: too many elements");
-  const ulonglong2 *tq = nullptr, *bq = nullptr;
-  int rc = tables(blocks, &tq, &bq);
+  const ulonglong2* tq = nullptr;
+  int rc = tables(blocks * RNG_THREADS * 2, &tq);
   if (rc) return rc;
-  rng_kernel<MODE><<<(unsigned)blocks, RNG_THREADS, 0, st>>>(s0, s1, bq, tq, out, n, lo, width, range, minval);
+  rng_kernel<MODE><<<(unsigned)blocks, RNG_THREADS, 0, st>>>(s0, s1, tq, out, n, lo, width, range, minval);
   JX_LAUNCH_CHECK("rng_kernel");
   return JX_OK;
 }
