@@ -144,6 +144,26 @@ JX_API int jx_binary_f32(int op, const float *a, const int64_t *a_shape, int a_n
 #define JX_UN_GELU 11
 #define JX_UN_SIGMOID 12
 #define JX_UN_GELU_GRAD 13 /* d/dx nn::gelu (restated adjoint, used by grad tapes) */
+/* The remaining Array unary methods (src/ops/unary.rs:82-541): Rust f32 semantics;
+ * ceil/floor/round (half away from zero)/trunc and sign (NaN -> 0) bit-identical. */
+#define JX_UN_TAN 14
+#define JX_UN_SIGN 15
+#define JX_UN_SINH 16
+#define JX_UN_COSH 17
+#define JX_UN_ASIN 18
+#define JX_UN_ACOS 19
+#define JX_UN_ATAN 20
+#define JX_UN_ASINH 21
+#define JX_UN_ACOSH 22
+#define JX_UN_ATANH 23
+#define JX_UN_CEIL 24
+#define JX_UN_FLOOR 25
+#define JX_UN_ROUND 26
+#define JX_UN_TRUNC 27
+#define JX_UN_EXPM1 28
+#define JX_UN_LOG1P 29
+#define JX_UN_CBRT 30
+#define JX_UN_LOG2 31
 JX_API int jx_unary_f32(int op, const float *x, float *y, int64_t n, jx_stream_t stream);
 
 /* ---- jit op-tape (FusedGroup src/trace/ir.rs:8-17; gpu_fused_execute

@@ -23,7 +23,9 @@ STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "J
 PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED = 0, 1, 2
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
-      "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12, "gelu_grad": 13}
+      "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12, "gelu_grad": 13, "tan": 14, "sign": 15, "sinh": 16,
+      "cosh": 17, "asin": 18, "acos": 19, "atan": 20, "asinh": 21, "acosh": 22, "atanh": 23, "ceil": 24,
+      "floor": 25, "round": 26, "trunc": 27, "expm1": 28, "log1p": 29, "cbrt": 30, "log2": 31}
 RED = {"sum": 0, "max": 1, "min": 2, "prod": 3}
 OP_CONST, OP_STORE, OP_UNARY, OP_BINARY, OP_SELECT_GT = 1, 2, 16, 48, 64
 DEVERR_NAN, DEVERR_TIMEOUT = 1, 2

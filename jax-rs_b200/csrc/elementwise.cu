@@ -88,7 +88,7 @@ int grid_for(long long work, int threads) {
 extern "C" {
 
 int jx_unary_f32(int op, const float* x, float* y, int64_t n, jx_stream_t stream) {
-  JX_REQUIRE(op >= 0 && op <= JX_UN_GELU_GRAD, "unary: unknown op %d", op);
+  JX_REQUIRE(op >= 0 && op <= JX_UN_LOG2, "unary: unknown op %d", op);
   JX_REQUIRE(n >= 0, "unary: negative size");
   if (n == 0) return JX_OK;
   JX_REQUIRE(x && y, "unary: NULL pointer");

@@ -334,7 +334,7 @@ int jx_graph_const(jx_graph* g, float value, int* node) {
 
 int jx_graph_unary(jx_graph* g, int op, int x, int* node) {
   JX_REQUIRE(g && node, "jx_graph_unary: NULL");
-  JX_REQUIRE(op >= JX_UN_NEG && op <= JX_UN_GELU_GRAD, "jx_graph_unary: unknown op %d", op);
+  JX_REQUIRE(op >= JX_UN_NEG && op <= JX_UN_LOG2, "jx_graph_unary: unknown op %d", op);
   JX_REQUIRE(valid(g, x), "jx_graph_unary: operand %d is not a node of this graph", x);
   return add_node(g, K_UN, op, x, -1, 0.f, node);
 }
@@ -400,6 +400,24 @@ int jx_graph_vjp(jx_graph* g, int n_out, const int* outs, const int* cts, int n_
         case JX_UN_RELU: acc(x, b.sel(x, gv)); break;
         case JX_UN_GELU: acc(x, b.mul(gv, b.un(JX_UN_GELU_GRAD, x))); break;
         case JX_UN_SIGMOID: acc(x, b.mul(gv, b.mul(v, b.sub(b.c(1.0f), v)))); break;
+        // transpose_tan (:123-134): sec^2 = (cos x * cos x)^-1
+        case JX_UN_TAN: { const int cx = b.un(JX_UN_COS, x); acc(x, b.mul(gv, b.recip(b.mul(cx, cx)))); break; }
+        // transpose_sign (:227-229) and the rounding family: zero almost everywhere
+        case JX_UN_SIGN: case JX_UN_CEIL: case JX_UN_FLOOR: case JX_UN_ROUND: case JX_UN_TRUNC:
+          acc(x, b.c(0.0f));
+          break;
+        case JX_UN_SINH: acc(x, b.mul(gv, b.un(JX_UN_COSH, x))); break;
+        case JX_UN_COSH: acc(x, b.mul(gv, b.un(JX_UN_SINH, x))); break;
+        case JX_UN_ASIN: acc(x, b.mul(gv, b.recip(b.un(JX_UN_SQRT, b.sub(b.c(1.0f), b.mul(x, x)))))); break;
+        case JX_UN_ACOS: acc(x, b.neg(b.mul(gv, b.recip(b.un(JX_UN_SQRT, b.sub(b.c(1.0f), b.mul(x, x))))))); break;
+        case JX_UN_ATAN: acc(x, b.mul(gv, b.recip(b.add(b.c(1.0f), b.mul(x, x))))); break;
+        case JX_UN_ASINH: acc(x, b.mul(gv, b.recip(b.un(JX_UN_SQRT, b.add(b.mul(x, x), b.c(1.0f)))))); break;
+        case JX_UN_ACOSH: acc(x, b.mul(gv, b.recip(b.un(JX_UN_SQRT, b.sub(b.mul(x, x), b.c(1.0f)))))); break;
+        case JX_UN_ATANH: acc(x, b.mul(gv, b.recip(b.sub(b.c(1.0f), b.mul(x, x))))); break;
+        case JX_UN_EXPM1: acc(x, b.mul(gv, b.add(v, b.c(1.0f)))); break;
+        case JX_UN_LOG1P: acc(x, b.mul(gv, b.recip(b.add(b.c(1.0f), x)))); break;
+        case JX_UN_CBRT: acc(x, b.mul(gv, b.recip(b.mul(b.c(3.0f), b.mul(v, v))))); break;
+        case JX_UN_LOG2: acc(x, b.mul(gv, b.recip(b.mul(x, b.c(0.693147180559945309f))))); break;
         default:
           return jx::fail(JX_EUNSUPPORTED, "jx_graph_vjp: no derivative for unary op %d", n.op);
       }

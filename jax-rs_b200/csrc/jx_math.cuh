@@ -86,6 +86,27 @@ static __device__ __noinline__ float jx_logf(float x) { return logf(x); }
 static __device__ __noinline__ float jx_sinf(float x) { return sinf(x); }
 static __device__ __noinline__ float jx_cosf(float x) { return cosf(x); }
 static __device__ __noinline__ float jx_powf(float a, float b) { return powf(a, b); }
+// The remaining unary methods (src/ops/unary.rs:82-541), CUDA's functions;
+// the rounding family and sign are exact.
+static __device__ __noinline__ float jx_unary_more(int op, float x) {
+  switch (op) {
+    case JX_UN_TAN: return tanf(x);
+    case JX_UN_SINH: return sinhf(x);
+    case JX_UN_COSH: return coshf(x);
+    case JX_UN_ASIN: return asinf(x);
+    case JX_UN_ACOS: return acosf(x);
+    case JX_UN_ATAN: return atanf(x);
+    case JX_UN_ASINH: return asinhf(x);
+    case JX_UN_ACOSH: return acoshf(x);
+    case JX_UN_ATANH: return atanhf(x);
+    case JX_UN_EXPM1: return expm1f(x);
+    case JX_UN_LOG1P: return log1pf(x);
+    case JX_UN_CBRT: return cbrtf(x);
+    default: return log2f(x);
+  }
+}
+// Array::sign (src/ops/unary.rs:117-127): 1, -1, else 0 (NaN gives 0 too).
+__device__ __forceinline__ float sign_f(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f); }
 
 // nn::gelu (src/nn.rs:111-122): coeff = sqrt(2/pi); inner = coeff*(v + 0.044715*v^3);
 // 0.5*v*(1 + tanh(inner)); v.powi(3) = v*(v*v).  coeff is the f32 value of
@@ -143,6 +164,12 @@ __device__ __forceinline__ float unary_t(float x) {
   else if constexpr (OP == JX_UN_GELU) return gelu_f(x);
   else if constexpr (OP == JX_UN_SIGMOID) return sigmoid_f(x);
   else if constexpr (OP == JX_UN_GELU_GRAD) return gelu_grad_f(x);
+  else if constexpr (OP == JX_UN_SIGN) return sign_f(x);
+  else if constexpr (OP == JX_UN_CEIL) return ceilf(x);
+  else if constexpr (OP == JX_UN_FLOOR) return floorf(x);
+  else if constexpr (OP == JX_UN_ROUND) return roundf(x);  // half away from zero, as f32::round
+  else if constexpr (OP == JX_UN_TRUNC) return truncf(x);
+  else if constexpr (OP >= JX_UN_TAN && OP <= JX_UN_LOG2) return jx_unary_more(OP, x);
   else return x;
 }
 
@@ -175,7 +202,14 @@ __device__ __forceinline__ float unary_f(int op, float x) {
     case JX_UN_GELU: return unary_t<JX_UN_GELU>(x);
     case JX_UN_SIGMOID: return unary_t<JX_UN_SIGMOID>(x);
     case JX_UN_GELU_GRAD: return unary_t<JX_UN_GELU_GRAD>(x);
-    default: return x;
+    case JX_UN_SIGN: return unary_t<JX_UN_SIGN>(x);
+    case JX_UN_CEIL: return unary_t<JX_UN_CEIL>(x);
+    case JX_UN_FLOOR: return unary_t<JX_UN_FLOOR>(x);
+    case JX_UN_ROUND: return unary_t<JX_UN_ROUND>(x);
+    case JX_UN_TRUNC: return unary_t<JX_UN_TRUNC>(x);
+    default:
+      if (op >= JX_UN_TAN && op <= JX_UN_LOG2) return jx_unary_more(op, x);
+      return x;
   }
 }
 

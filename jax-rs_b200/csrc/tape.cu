@@ -11,9 +11,10 @@
 // the constant bank, so re-running a tape with new scalars never recompiles.
 //
 // The generated kernel is straight-line code over SSA values: each thread
-// loads 4 consecutive elements per input with one 128-bit load, applies the
-// ops (the per-element semantics of jx_math.cuh, the same header the plain
-// elementwise kernels use) and stores 4 elements per output.  The reference
+// loads two groups of 4 consecutive elements per input (one 128-bit load
+// each, one grid sweep apart), applies the ops (the per-element semantics of
+// jx_math.cuh, the same header the plain elementwise kernels use) and stores
+// the same groups per output.  The reference
 // formats literals with {:.6} (src/trace/fusion.rs:359) and turns constants
 // it cannot see into 0.0 (:360-363); here constants keep all their bits.
 #include <cudaTypedefs.h>
@@ -114,7 +115,7 @@ int tape_validate(const int32_t* code, int n_instr, int n_consts, int n_inputs, 
       JX_REQUIRE(reg_ok(dst) && reg_ok(s0) && reg_ok(s1) && defined[s0] && defined[s1],
                  "tape[%d]: bad binary instruction (op %d): undefined source or register range", pc, op);
       defined[dst] = true;
-    } else if (op >= JX_OP_UNARY && op <= JX_OP_UNARY + JX_UN_GELU_GRAD) {
+    } else if (op >= JX_OP_UNARY && op <= JX_OP_UNARY + JX_UN_LOG2) {
       JX_REQUIRE(reg_ok(dst) && reg_ok(s0) && defined[s0],
                  "tape[%d]: bad unary instruction (op %d): undefined source or register range", pc, op);
       defined[dst] = true;

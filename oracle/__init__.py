@@ -193,7 +193,9 @@ def bmm(a, b, nthreads=1):
 
 
 UNOPS = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
-         "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12}
+         "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12, "tan": 14, "sign": 15, "sinh": 16, "cosh": 17,
+         "asin": 18, "acos": 19, "atan": 20, "asinh": 21, "acosh": 22, "atanh": 23, "ceil": 24, "floor": 25,
+         "round": 26, "trunc": 27, "expm1": 28, "log1p": 29, "cbrt": 30, "log2": 31}
 
 
 def unary(name, x):

@@ -219,9 +219,25 @@ void jxo_relu(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; 
 void jxo_tanh(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = tanhf(x[i]); }
 void jxo_exp(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = expf(x[i]); }
 
+/* Rust std's own f32 formulas for the inverse hyperbolic functions (they do
+ * not call libm's asinhf/acoshf/atanhf): asinh = copysign(ln_1p(|x| +
+ * |x| / (hypot(1, 1/|x|) + 1/|x|)), x); acosh = x < 1 ? NaN :
+ * ln(x + sqrt(x - 1) * sqrt(x + 1)); atanh = 0.5 * ln_1p(2x / (1 - x)). */
+static inline float rust_asinh(float x) {
+    float ax = fabsf(x), ix = 1.0f / ax;
+    return copysignf(log1pf(ax + (ax / (hypotf(1.0f, ix) + ix))), x);
+}
+static inline float rust_acosh(float x) {
+    return x < 1.0f ? NAN : logf(x + (sqrtf(x - 1.0f) * sqrtf(x + 1.0f)));
+}
+static inline float rust_atanh(float x) { return 0.5f * log1pf((2.0f * x) / (1.0f - x)); }
+/* Array::sign (src/ops/unary.rs:117-127): 1, -1, else 0 (NaN included). */
+static inline float sign1(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f); }
+
 /* unary_op (src/ops/unary.rs:30-49) with the element function of each method
  * (neg, abs, sin, cos, tanh, exp, ln, sqrt, recip, square at :60-160; relu,
- * gelu, sigmoid from src/nn.rs).  Codes follow JX_UN_* of the C ABI. */
+ * gelu, sigmoid from src/nn.rs; tan through log2 at :82-541).  Codes follow
+ * JX_UN_* of the C ABI. */
 static inline float unary1(int op, float x) {
     switch (op) {
     case 0: return -x;
@@ -237,6 +253,24 @@ static inline float unary1(int op, float x) {
     case 10: return relu1(x);
     case 11: return gelu1(x);
     case 12: return sigmoid1(x);
+    case 14: return tanf(x);
+    case 15: return sign1(x);
+    case 16: return sinhf(x);
+    case 17: return coshf(x);
+    case 18: return asinf(x);
+    case 19: return acosf(x);
+    case 20: return atanf(x);
+    case 21: return rust_asinh(x);
+    case 22: return rust_acosh(x);
+    case 23: return rust_atanh(x);
+    case 24: return ceilf(x);
+    case 25: return floorf(x);
+    case 26: return roundf(x);
+    case 27: return truncf(x);
+    case 28: return expm1f(x);
+    case 29: return log1pf(x);
+    case 30: return cbrtf(x);
+    case 31: return log2f(x);
     default: return x;
     }
 }

@@ -257,3 +257,33 @@ def test_div_by_power_of_two_constant_is_exact(jx, dev, oracle):
         X, Y = dev.put(x), dev.full(x.shape, np.nan)
         tape.run([X.data_ptr()], [Y.data_ptr()], x.size, dev.stream)
         assert np.array_equal(dev.get(Y), (x / np.float32(c)).astype(np.float32))
+
+
+MORE_UNARY = {  # op -> (domain lo, hi, exact)
+    "sign": (-3, 3, True), "ceil": (-50, 50, True), "floor": (-50, 50, True), "round": (-50, 50, True),
+    "trunc": (-50, 50, True), "tan": (-1.4, 1.4, False), "sinh": (-20, 20, False), "cosh": (-20, 20, False),
+    "asin": (-0.999, 0.999, False), "acos": (-0.999, 0.999, False), "atan": (-50, 50, False),
+    "asinh": (-50, 50, False), "acosh": (1.0, 50, False), "atanh": (-0.99, 0.99, False),
+    "expm1": (-10, 10, False), "log1p": (-0.99, 50, False), "cbrt": (-100, 100, False), "log2": (1e-3, 1e3, False),
+}
+
+
+@pytest.mark.parametrize("op", sorted(MORE_UNARY))
+def test_remaining_unary_methods_vs_oracle(jx, dev, oracle, op):
+    """Array::tan .. log2 (src/ops/unary.rs:82-541) against the oracle's
+    restatement (glibc, and Rust std's own asinh/acosh/atanh formulas):
+    the rounding family and sign bit-identical, the rest within
+    |d - o| <= 1e-5 |o| + 1e-6."""
+    lo, hi, exact = MORE_UNARY[op]
+    rng = np.random.default_rng(len(op))
+    x = rng.uniform(lo, hi, 100003).astype(np.float32)
+    x[:6] = np.array([lo, hi, 0.5 * (lo + hi), 2.5, -2.5, 0.0], np.float32).clip(lo, hi)
+    if op == "sign":
+        x[6:9] = [np.nan, -0.0, np.inf]
+    X, Y = dev.put(x), dev.full(x.shape, 7.0)
+    jx.unary(op, X.data_ptr(), Y.data_ptr(), x.size, dev.stream)
+    y, o = dev.get(Y), oracle.unary(op, x)
+    if exact:
+        assert np.array_equal(y, o, equal_nan=True)
+    else:
+        assert _close(y, o)

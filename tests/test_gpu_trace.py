@@ -166,3 +166,26 @@ def test_wide_sum_and_repeated_outputs(tr, dev):
     assert np.array_equal(outs[1], data[2])
     assert np.all(outs[2] == 2.5)
     assert np.array_equal(outs[3], ref)
+
+
+@pytest.mark.parametrize("op,lo,hi", [("tan", -1.2, 1.2), ("sinh", -3, 3), ("cosh", -3, 3), ("asin", -0.9, 0.9),
+                                      ("acos", -0.9, 0.9), ("atan", -3, 3), ("asinh", -3, 3), ("acosh", 1.1, 4),
+                                      ("atanh", -0.9, 0.9), ("expm1", -3, 3), ("log1p", -0.9, 3),
+                                      ("cbrt", 0.2, 8), ("log2", 0.1, 8), ("floor", -3, 3)])
+def test_unary_method_gradients_vs_central_differences(tr, dev, op, lo, hi):
+    g = tr.Graph()
+    x = g.input()
+    y = g.unary(op, x)
+    (dx,) = g.vjp([y], [g.const(1.0)], [x])
+    prog = g.compile([y, dx])
+    xs = np.random.default_rng(3).uniform(lo, hi, 4096).astype(np.float32)
+    yv, dxv = _run(dev, prog, [xs], 2)
+    f = {"tan": np.tan, "sinh": np.sinh, "cosh": np.cosh, "asin": np.arcsin, "acos": np.arccos,
+         "atan": np.arctan, "asinh": np.arcsinh, "acosh": np.arccosh, "atanh": np.arctanh, "expm1": np.expm1,
+         "log1p": np.log1p, "cbrt": np.cbrt, "log2": np.log2, "floor": np.floor}[op]
+    x64 = xs.astype(np.float64)
+    h = 1e-5
+    fd = (f(x64 + h) - f(x64 - h)) / (2 * h)
+    if op == "floor":
+        fd = np.zeros_like(x64)  # zero almost everywhere, as the reference's rule
+    assert np.linalg.norm(dxv - fd) <= 1e-4 * np.linalg.norm(fd) + 1e-4 * np.sqrt(xs.size), op
