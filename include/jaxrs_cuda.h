@@ -285,6 +285,18 @@ JX_API int jx_fft_c2c_f32(const float *in, float *out, int64_t n, int64_t batch,
 /* Batched 2-D transform of [batch, h, w] complex images: rows, then columns. */
 JX_API int jx_fft2_c2c_f32(const float *in, float *out, int64_t h, int64_t w, int64_t batch, int inverse,
                     jx_stream_t stream);
+/* Real input / real output (ops::fft::fft with real input :91-126, rfft
+ * :212-234, irfft :417-462, rfftn / irfftn in 2-D :474-628).  in [batch][n]
+ * real -> out [batch][bins] interleaved complex, bins = full ? n : n/2+1
+ * (full = 1 is fft's whole spectrum, 0 is rfft's).  n >= 2, a power of two,
+ * up to 16384. */
+JX_API int jx_fft_r2c_f32(const float *in, float *out, int64_t n, int64_t batch, int full, jx_stream_t stream);
+/* irfft: in [batch][n/2+1] complex -> out [batch][n] real, scaled 1/n; the
+ * imaginary parts of the DC and Nyquist bins do not affect the result. */
+JX_API int jx_fft_c2r_f32(const float *in, float *out, int64_t n, int64_t batch, jx_stream_t stream);
+/* rfftn / irfftn of [batch][h][w] real <-> [batch][h][w/2+1] complex. */
+JX_API int jx_rfft2_f32(const float *in, float *out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream);
+JX_API int jx_irfft2_f32(const float *in, float *out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream);
 
 /* ---- conv2d (gpu_conv2d src/backend/ops.rs:815-828; nn::conv2d_batched
  *      src/nn.rs:2048-2144), NCHW input, OIHW weight --------------------- */

@@ -75,6 +75,10 @@ _SIGS = {
     "jx_tape_source": [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
     "jx_tape_check": [vp],
     "jx_tape_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
+    "jx_fft_r2c_f32": [vp, vp, i64, i64, C.c_int, vp],
+    "jx_fft_c2r_f32": [vp, vp, i64, i64, vp],
+    "jx_rfft2_f32": [vp, vp, i64, i64, i64, vp],
+    "jx_irfft2_f32": [vp, vp, i64, i64, i64, vp],
     "jx_random_uniform_f32": [C.c_uint64, C.c_uint64, vp, i64, cf, cf, vp],
     "jx_random_randint_f32": [C.c_uint64, C.c_uint64, vp, i64, C.c_int32, C.c_int32, vp],
     "jx_random_normal_f32": [C.c_uint64, C.c_uint64, vp, i64, vp],

@@ -135,8 +135,12 @@ constexpr int region() {
 template <bool COLS>
 struct Addr {
   long long n, w, hw;  // COLS: image width w, image size hw; element i of transform t
+  long long os;        // rows: distance between consecutive output transforms (0: n)
   __device__ __forceinline__ long long base(long long t) const {
     return COLS ? (t / w) * hw + (t % w) : t * n;
+  }
+  __device__ __forceinline__ long long obase(long long t) const {
+    return COLS ? base(t) : t * (os ? os : n);
   }
   __device__ __forceinline__ long long estride() const { return COLS ? w : 1; }
 };
@@ -164,6 +168,7 @@ __global__ void __launch_bounds__(TPC*((1 << LOGN) / 16),
   const long long t = (long long)blockIdx.x * TPC + tl;
   const bool active = t < ntrans;
   const long long gbase = ad.base(active ? t : 0);
+  const long long obase = ad.obase(active ? t : 0);
   const long long es = ad.estride();
   cf2* S = sm + tl * NPAD;
   cf2 v[16];
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(TPC*((1 << LOGN) / 16),
       if (active) {
 #pragma unroll
         for (int r = 0; r < 16; ++r)
-          __stcs(out + gbase + (long long)(idxD + r * Ns) * es, make_float2(v[r].x * scale, v[r].y * scale));
+          __stcs(out + obase + (long long)(idxD + r * Ns) * es, make_float2(v[r].x * scale, v[r].y * scale));
       }
     } else {
 #pragma unroll
@@ -250,10 +255,11 @@ __global__ void __launch_bounds__(TPC*((1 << LOGN) / 16),
 // n in {1, 2, 4, 8}: one thread per transform, direct radix pass.
 template <int R, bool INV>
 __global__ void fft_tiny_kernel(const float2* __restrict__ in, float2* __restrict__ out, long long ntrans,
-                                long long n_img_w, long long hw, int cols, float scale) {
+                                long long n_img_w, long long hw, int cols, float scale, long long os) {
   const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (t >= ntrans) return;
   const long long base = cols ? (t / n_img_w) * hw + (t % n_img_w) : t * R;
+  const long long ob = cols ? base : t * (os ? os : R);
   const long long es = cols ? n_img_w : 1;
   cf2 u[R > 1 ? R : 1];
   for (int i = 0; i < R; ++i) {
@@ -261,12 +267,12 @@ __global__ void fft_tiny_kernel(const float2* __restrict__ in, float2* __restric
     u[i] = {x.x, x.y};
   }
   if constexpr (R > 1) dft_r<R, INV>(u);
-  for (int i = 0; i < R; ++i) out[base + i * es] = make_float2(u[i].x * scale, u[i].y * scale);
+  for (int i = 0; i < R; ++i) out[ob + i * es] = make_float2(u[i].x * scale, u[i].y * scale);
 }
 
 // ---- twiddle tables: exp(-2 pi i t / 2^logn), t < 2^logn, per device -------
 std::mutex g_tw_mu;
-float2* g_tw[64][MAX_LOGN + 1];
+float2* g_tw[64][MAX_LOGN + 2];  // sizes up to 2^(MAX_LOGN+1): real transforms use size n for n/2 points
 
 int twiddles(int logn, const float2** out) {
   int dev = 0;
@@ -316,15 +322,15 @@ int launch_fft(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, b
 // 8 adjacent columns when the width allows.
 template <int LOGN>
 int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, long long w, long long hw, bool inv,
-                  float scale, cudaStream_t st) {
+                  float scale, cudaStream_t st, long long os) {
   constexpr int N = 1 << LOGN;
   constexpr int T = N / 16;
   if (!cols) {
-    Addr<false> ad{N, 0, 0};
+    Addr<false> ad{N, 0, 0, os};
     constexpr int TPC = T >= 256 ? 1 : 256 / T;
     return launch_fft<LOGN, TPC, false>(in, out, ntrans, ad, inv, scale, st);
   }
-  Addr<true> ad{N, w, hw};
+  Addr<true> ad{N, w, hw, 0};
   if constexpr (N <= 1024) {
     // 8 adjacent columns (64-byte row segments) per CTA: small enough that
     // several CTAs share an SM, so one CTA's loads overlap another's math.
@@ -334,16 +340,17 @@ int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, lo
   return launch_fft<LOGN, 1, true>(in, out, ntrans, ad, inv, scale, st);
 }
 
+// os: rows only, the distance between consecutive output transforms (0: n).
 int fft_batched(const float2* in, float2* out, int logn, long long ntrans, bool cols, long long w, long long hw,
-                bool inv, cudaStream_t st) {
+                bool inv, cudaStream_t st, long long os = 0) {
   const float scale = inv ? 1.0f / (float)(1LL << logn) : 1.0f;  // ifft: 1.0 / (n as f32)
   if (logn <= 3) {
     const int threads = 256;
     const long long blocks = (ntrans + threads - 1) / threads;
     const int c = cols ? 1 : 0;
 #define JX_TINY(R)                                                                                 \
-  if (inv) fft_tiny_kernel<R, true><<<(unsigned)blocks, threads, 0, st>>>(in, out, ntrans, w, hw, c, scale); \
-  else fft_tiny_kernel<R, false><<<(unsigned)blocks, threads, 0, st>>>(in, out, ntrans, w, hw, c, scale);
+  if (inv) fft_tiny_kernel<R, true><<<(unsigned)blocks, threads, 0, st>>>(in, out, ntrans, w, hw, c, scale, os); \
+  else fft_tiny_kernel<R, false><<<(unsigned)blocks, threads, 0, st>>>(in, out, ntrans, w, hw, c, scale, os);
     switch (logn) {
       case 0: JX_TINY(1) break;
       case 1: JX_TINY(2) break;
@@ -355,17 +362,89 @@ int fft_batched(const float2* in, float2* out, int logn, long long ntrans, bool 
     return JX_OK;
   }
   switch (logn) {
-    case 4: return dispatch_size<4>(in, out, ntrans, cols, w, hw, inv, 1.0f * scale, st);
-    case 5: return dispatch_size<5>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 6: return dispatch_size<6>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 7: return dispatch_size<7>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 8: return dispatch_size<8>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 9: return dispatch_size<9>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 10: return dispatch_size<10>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 11: return dispatch_size<11>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    case 12: return dispatch_size<12>(in, out, ntrans, cols, w, hw, inv, scale, st);
-    default: return dispatch_size<13>(in, out, ntrans, cols, w, hw, inv, scale, st);
+    case 4: return dispatch_size<4>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 5: return dispatch_size<5>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 6: return dispatch_size<6>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 7: return dispatch_size<7>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 8: return dispatch_size<8>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 9: return dispatch_size<9>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 10: return dispatch_size<10>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 11: return dispatch_size<11>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    case 12: return dispatch_size<12>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
+    default: return dispatch_size<13>(in, out, ntrans, cols, w, hw, inv, scale, st, os);
   }
+}
+
+// ---- real input / real output (fft, rfft, irfft, rfftn, irfftn) -----------
+// An n-point real transform is an n/2-point complex transform of the real
+// array read as interleaved complex, z[j] = x[2j] + i x[2j+1], followed by
+// the split into even and odd spectra: with N2 = n/2 and W = e^{-2 pi i/n},
+//   Fe[k] = (Z[k] + conj Z[N2-k]) / 2,   Fo[k] = -i (Z[k] - conj Z[N2-k]) / 2,
+//   X[k] = Fe[k] + W^k Fo[k]   (k = 0..N2, indices of Z mod N2),
+// and X[n-k] = conj X[k] for the full spectrum.  One thread handles the
+// pair (k, N2-k): it reads exactly the two values it overwrites, so the split
+// runs in place on the output.  rs: complex elements between output rows.
+__device__ __forceinline__ cf2 r2c_bin(cf2 a, cf2 b_conj, cf2 w) {
+  const cf2 fe{0.5f * (a.x + b_conj.x), 0.5f * (a.y + b_conj.y)};
+  const cf2 d{a.x - b_conj.x, a.y - b_conj.y};
+  const cf2 fo{0.5f * d.y, -0.5f * d.x};  // -i d / 2
+  return cadd(fe, cmul(w, fo));
+}
+
+__global__ void r2c_split_kernel(float2* __restrict__ out, long long n, long long rs, long long rows, int full,
+                                 const float2* __restrict__ tw) {
+  const long long N2 = n / 2, pairs = N2 / 2 + 1;
+  const long long total = rows * pairs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / pairs, k = i - r * pairs, k2 = N2 - k;
+    float2* row = out + r * rs;
+    const float2 zk = row[k % N2], zk2 = row[k2 % N2];
+    const cf2 a{zk.x, zk.y}, b{zk2.x, zk2.y};
+    const float2 wk = tw[k], wk2 = tw[k2];
+    const cf2 xk = r2c_bin(a, cf2{b.x, -b.y}, cf2{wk.x, wk.y});
+    const cf2 xk2 = r2c_bin(b, cf2{a.x, -a.y}, cf2{wk2.x, wk2.y});
+    row[k] = make_float2(xk.x, xk.y);
+    row[k2] = make_float2(xk2.x, xk2.y);
+    if (full) {
+      if (k > 0) row[n - k] = make_float2(xk.x, -xk.y);
+      if (k2 > 0 && k2 < N2) row[n - k2] = make_float2(xk2.x, -xk2.y);
+    }
+  }
+}
+
+// irfft: from bins X[0..N2] (rows is = N2+1 complex apart; the imaginary parts
+// of DC and Nyquist do not reach the real output, as in the reference's
+// conjugate-symmetric extension), build
+//   Z[k] = Xe[k] + i Xo[k],  Xe = (X[k] + conj X[N2-k]) / 2,
+//   Xo = conj(W^k) (X[k] - conj X[N2-k]) / 2,
+// whose N2-point inverse transform (scale 1/N2) is x[2j] + i x[2j+1].
+__global__ void c2r_merge_kernel(const float2* __restrict__ in, long long is, float2* __restrict__ out, long long n,
+                                 long long rows, const float2* __restrict__ tw) {
+  const long long N2 = n / 2;
+  const long long total = rows * N2;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / N2, k = i - r * N2;
+    const float2* row = in + r * is;
+    float2 a = row[k], b = row[N2 - k];
+    if (k == 0) {
+      a.y = 0.f;
+      b.y = 0.f;
+    }
+    const cf2 xe{0.5f * (a.x + b.x), 0.5f * (a.y - b.y)};  // (a + conj b) / 2
+    const cf2 d{0.5f * (a.x - b.x), 0.5f * (a.y + b.y)};   // (a - conj b) / 2
+    const float2 w = tw[k];
+    const cf2 xo = cmul(cf2{w.x, -w.y}, d);
+    out[r * N2 + k] = make_float2(xe.x - xo.y, xe.y + xo.x);  // xe + i xo
+  }
+}
+
+int grid_for_elems(long long work) {
+  long long b = (work + 255) / 256;
+  const long long cap = (long long)jx::num_sms() * 8;
+  if (b > cap) b = cap;
+  return b < 1 ? 1 : (int)b;
 }
 
 int log2_exact(long long n) {
@@ -407,6 +486,88 @@ int jx_fft2_c2c_f32(const float* in, float* out, int64_t h, int64_t w, int64_t b
   if (rc) return rc;
   return fft_batched(reinterpret_cast<const float2*>(out), reinterpret_cast<float2*>(out), lh, w * batch, true, w,
                      h * w, inverse != 0, st);
+}
+
+int jx_fft_r2c_f32(const float* in, float* out, int64_t n, int64_t batch, int full, jx_stream_t stream) {
+  JX_REQUIRE(n >= 2 && batch >= 0, "fft: bad size");
+  const int logn = log2_exact(n);
+  JX_REQUIRE(logn >= 0, "FFT size must be power of 2");
+  JX_REQUIRE(logn - 1 <= MAX_LOGN, "fft: n = %lld exceeds the largest supported size %d", (long long)n,
+             2 << MAX_LOGN);
+  if (batch == 0) return JX_OK;
+  JX_REQUIRE(in && out, "fft: NULL pointer");
+  JX_REQUIRE((reinterpret_cast<uintptr_t>(in) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+             "fft: buffers must be 8-byte aligned");
+  cudaStream_t st = jx::as_stream(stream);
+  const long long bins = full ? n : n / 2 + 1;
+  const float2* tw = nullptr;
+  int rc = twiddles(logn, &tw);
+  if (!rc)
+    rc = fft_batched(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), logn - 1, batch, false, 0,
+                     0, false, st, bins);
+  if (rc) return rc;
+  const long long work = batch * (n / 4 + 1);
+  r2c_split_kernel<<<grid_for_elems(work), 256, 0, st>>>(reinterpret_cast<float2*>(out), n, bins, batch, full ? 1 : 0,
+                                                         tw);
+  JX_LAUNCH_CHECK("r2c_split_kernel");
+  return JX_OK;
+}
+
+int jx_fft_c2r_f32(const float* in, float* out, int64_t n, int64_t batch, jx_stream_t stream) {
+  JX_REQUIRE(n >= 2 && batch >= 0, "irfft: bad size");
+  const int logn = log2_exact(n);
+  JX_REQUIRE(logn >= 0, "FFT size must be power of 2");
+  JX_REQUIRE(logn - 1 <= MAX_LOGN, "irfft: n = %lld exceeds the largest supported size %d", (long long)n,
+             2 << MAX_LOGN);
+  if (batch == 0) return JX_OK;
+  JX_REQUIRE(in && out, "irfft: NULL pointer");
+  JX_REQUIRE((reinterpret_cast<uintptr_t>(in) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+             "irfft: buffers must be 8-byte aligned");
+  cudaStream_t st = jx::as_stream(stream);
+  const float2* tw = nullptr;
+  int rc = twiddles(logn, &tw);
+  if (rc) return rc;
+  c2r_merge_kernel<<<grid_for_elems(batch * (n / 2)), 256, 0, st>>>(reinterpret_cast<const float2*>(in), n / 2 + 1,
+                                                                   reinterpret_cast<float2*>(out), n, batch, tw);
+  JX_LAUNCH_CHECK("c2r_merge_kernel");
+  return fft_batched(reinterpret_cast<const float2*>(out), reinterpret_cast<float2*>(out), logn - 1, batch, false, 0,
+                     0, true, st);
+}
+
+int jx_rfft2_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream) {
+  JX_REQUIRE(h >= 1 && w >= 2 && batch >= 0, "rfftn: bad size");
+  const int lh = log2_exact(h), lw = log2_exact(w);
+  JX_REQUIRE(lh >= 0 && lw >= 0, "FFT size must be power of 2");
+  JX_REQUIRE(lh <= MAX_LOGN && lw - 1 <= MAX_LOGN, "rfftn: size not supported");
+  if (batch == 0) return JX_OK;
+  // rows: w real -> w/2+1 bins (the reference keeps those of the full row
+  // transform, src/ops/fft.rs:474-553); then the columns of the bins
+  int rc = jx_fft_r2c_f32(in, out, w, h * batch, 0, stream);
+  if (rc) return rc;
+  const long long m = w / 2 + 1;
+  return fft_batched(reinterpret_cast<const float2*>(out), reinterpret_cast<float2*>(out), lh, m * batch, true, m,
+                     h * m, false, jx::as_stream(stream));
+}
+
+int jx_irfft2_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream) {
+  JX_REQUIRE(h >= 1 && w >= 2 && batch >= 0, "irfftn: bad size");
+  const int lh = log2_exact(h), lw = log2_exact(w);
+  JX_REQUIRE(lh >= 0 && lw >= 0, "FFT size must be power of 2");
+  JX_REQUIRE(lh <= MAX_LOGN && lw - 1 <= MAX_LOGN, "irfftn: size not supported");
+  if (batch == 0) return JX_OK;
+  JX_REQUIRE(in && out, "irfftn: NULL pointer");
+  // columns first (inverse, 1/h), then each row's real inverse (1/w), as
+  // src/ops/fft.rs:554-628 orders them; the column result goes to scratch
+  cudaStream_t st = jx::as_stream(stream);
+  const long long m = w / 2 + 1;
+  void* ws = nullptr;
+  int rc = jx::scratch_get(sizeof(float2) * (size_t)(batch * h * m), &ws, st);
+  if (rc) return rc;
+  float2* cols = reinterpret_cast<float2*>(ws);
+  rc = fft_batched(reinterpret_cast<const float2*>(in), cols, lh, m * batch, true, m, h * m, true, st);
+  if (!rc) rc = jx_fft_c2r_f32(reinterpret_cast<const float*>(cols), out, w, h * batch, stream);
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
 }
 
 }  // extern "C"

@@ -94,6 +94,10 @@ def lib():
         L.jxo_max_rows_vjp.argtypes = [f32p, f32p, f32p, i64, i64]
         L.jxo_fft_c2c.argtypes = [f32p, f32p, i64, i64, C.c_int, C.c_int]
         L.jxo_fft2_c2c.argtypes = [f32p, f32p, i64, i64, i64, C.c_int, C.c_int]
+        L.jxo_fft_real.argtypes = [f32p, f32p, i64, i64, C.c_int]
+        L.jxo_irfft.argtypes = [f32p, f32p, i64, i64]
+        L.jxo_rfftn2.argtypes = [f32p, f32p, i64, i64, i64]
+        L.jxo_irfftn2.argtypes = [f32p, f32p, i64, i64, i64]
         L.jxo_dft_f64.argtypes = [f32p, f64p, i64, C.c_int]
         conv = [i64] * 9 + [C.c_int]
         L.jxo_conv2d_fwd.argtypes = [f32p, f32p, f32p] + conv
@@ -329,6 +333,51 @@ def fft2_c2c(x, inverse=False, nthreads=1):
     batch = x.size // (2 * h * w)
     y = np.empty_like(x)
     if lib().jxo_fft2_c2c(x, y, h, w, batch, 1 if inverse else 0, nthreads) != 0:
+        raise ValueError("FFT size must be a power of 2")
+    return y
+
+
+def fft_real(x, full=True):
+    """fft of real rows (src/ops/fft.rs:91-126; rfft :212-234 when not full):
+    x float32 [..., n] -> [..., bins, 2], bins = n or n/2+1."""
+    x = _c(x)
+    n = x.shape[-1]
+    batch = x.size // n
+    bins = n if full else n // 2 + 1
+    y = np.empty(x.shape[:-1] + (bins, 2), np.float32)
+    if lib().jxo_fft_real(x, y, n, batch, 1 if full else 0) != 0:
+        raise ValueError("FFT size must be a power of 2")
+    return y
+
+
+def irfft(x, n):
+    """irfft (src/ops/fft.rs:417-462): x float32 [..., n/2+1, 2] -> [..., n]."""
+    x = _c(x)
+    batch = x.size // (2 * (n // 2 + 1))
+    y = np.empty(x.shape[:-2] + (n,), np.float32)
+    if lib().jxo_irfft(x, y, n, batch) != 0:
+        raise ValueError("FFT size must be a power of 2")
+    return y
+
+
+def rfftn2(x):
+    """rfftn of 2-D images (src/ops/fft.rs:474-553): [..., h, w] -> [..., h, w/2+1, 2]."""
+    x = _c(x)
+    h, w = x.shape[-2], x.shape[-1]
+    batch = x.size // (h * w)
+    y = np.empty(x.shape[:-1] + (w // 2 + 1, 2), np.float32)
+    if lib().jxo_rfftn2(x, y, h, w, batch) != 0:
+        raise ValueError("FFT size must be a power of 2")
+    return y
+
+
+def irfftn2(x, w):
+    """irfftn of 2-D spectra (src/ops/fft.rs:554-628): [..., h, w/2+1, 2] -> [..., h, w]."""
+    x = _c(x)
+    h = x.shape[-3]
+    batch = x.size // (2 * h * (w // 2 + 1))
+    y = np.empty(x.shape[:-3] + (h, w), np.float32)
+    if lib().jxo_irfftn2(x, y, h, w, batch) != 0:
         raise ValueError("FFT size must be a power of 2")
     return y
 

@@ -583,6 +583,91 @@ int jxo_fft2_c2c(const float *in, float *out, int64_t h, int64_t w, int64_t batc
     return 0;
 }
 
+/* Real-input and real-output transforms, per batch row.  fft (real input,
+ * src/ops/fft.rs:91-126): widen to complex (imaginary 0), fft_recursive,
+ * all n bins.  rfft (:212-234): the same, first n/2+1 bins. */
+int jxo_fft_real(const float *in, float *out, int64_t n, int64_t batch, int full) {
+    if (n <= 0 || (n & (n - 1)) != 0) return -1;
+    int64_t bins = full ? n : n / 2 + 1;
+    cpx *x = (cpx *)malloc(sizeof(cpx) * n), *y = (cpx *)malloc(sizeof(cpx) * n);
+    cpx *scratch = (cpx *)malloc(sizeof(cpx) * (4 * n + 4));
+    for (int64_t b = 0; b < batch; ++b) {
+        for (int64_t i = 0; i < n; ++i) { x[i].re = in[b * n + i]; x[i].im = 0.0f; }
+        fft_rec(x, y, n, 0, scratch);
+        for (int64_t k = 0; k < bins; ++k) { out[2 * (b * bins + k)] = y[k].re; out[2 * (b * bins + k) + 1] = y[k].im; }
+    }
+    free(x); free(y); free(scratch);
+    return 0;
+}
+
+/* irfft (src/ops/fft.rs:417-462): bins 0..m-1 as given, then conj(X[i]) for
+ * i = n-m down to 1; fft_recursive(.., inverse); times 1/n; real parts. */
+int jxo_irfft(const float *in, float *out, int64_t n, int64_t batch) {
+    if (n <= 0 || (n & (n - 1)) != 0) return -1;
+    int64_t m = n / 2 + 1;
+    cpx *x = (cpx *)malloc(sizeof(cpx) * n), *y = (cpx *)malloc(sizeof(cpx) * n);
+    cpx *scratch = (cpx *)malloc(sizeof(cpx) * (4 * n + 4));
+    for (int64_t b = 0; b < batch; ++b) {
+        const float *d = in + 2 * m * b;
+        int64_t p = 0;
+        for (int64_t i = 0; i < m; ++i) { x[p].re = d[2 * i]; x[p].im = d[2 * i + 1]; ++p; }
+        for (int64_t i = n - m; i >= 1; --i) { x[p].re = d[2 * i]; x[p].im = -d[2 * i + 1]; ++p; }
+        fft_rec(x, y, n, 1, scratch);
+        float scale = 1.0f / (float)n;
+        for (int64_t i = 0; i < n; ++i) out[b * n + i] = y[i].re * scale;
+    }
+    free(x); free(y); free(scratch);
+    return 0;
+}
+
+/* rfftn 2-D (src/ops/fft.rs:474-553): full fft of each row, then fft of each
+ * of the first w/2+1 columns; result [h][w/2+1] complex. */
+int jxo_rfftn2(const float *in, float *out, int64_t h, int64_t w, int64_t batch) {
+    int64_t m = w / 2 + 1;
+    float *rows = (float *)malloc(sizeof(float) * 2 * h * w);
+    float *col = (float *)malloc(sizeof(float) * 2 * h), *colo = (float *)malloc(sizeof(float) * 2 * h);
+    for (int64_t b = 0; b < batch; ++b) {
+        if (jxo_fft_real(in + b * h * w, rows, w, h, 1) != 0) return -1;
+        for (int64_t j = 0; j < m; ++j) {
+            for (int64_t i = 0; i < h; ++i) { col[2 * i] = rows[2 * (i * w + j)]; col[2 * i + 1] = rows[2 * (i * w + j) + 1]; }
+            if (jxo_fft_c2c(col, colo, h, 1, 0, 1) != 0) return -1;
+            for (int64_t i = 0; i < h; ++i) {
+                out[2 * (b * h * m + i * m + j)] = colo[2 * i];
+                out[2 * (b * h * m + i * m + j) + 1] = colo[2 * i + 1];
+            }
+        }
+    }
+    free(rows); free(col); free(colo);
+    return 0;
+}
+
+/* irfftn 2-D (src/ops/fft.rs:554-628): inverse fft of each of the w/2+1
+ * columns (times 1/h), then per row the conjugate-symmetric extension, the
+ * inverse fft and times 1/w, real parts. */
+int jxo_irfftn2(const float *in, float *out, int64_t h, int64_t w, int64_t batch) {
+    int64_t m = w / 2 + 1;
+    float *cols = (float *)malloc(sizeof(float) * 2 * h * m);
+    float *col = (float *)malloc(sizeof(float) * 2 * h), *colo = (float *)malloc(sizeof(float) * 2 * h);
+    for (int64_t b = 0; b < batch; ++b) {
+        const float *d = in + 2 * h * m * b;
+        for (int64_t j = 0; j < m; ++j) {
+            for (int64_t i = 0; i < h; ++i) { col[2 * i] = d[2 * (i * m + j)]; col[2 * i + 1] = d[2 * (i * m + j) + 1]; }
+            /* fft_recursive(.., true), then * (1/h) */
+            cpx *scratch = (cpx *)malloc(sizeof(cpx) * (4 * h + 4));
+            fft_rec((const cpx *)col, (cpx *)colo, h, 1, scratch);
+            free(scratch);
+            float scale = 1.0f / (float)h;
+            for (int64_t i = 0; i < h; ++i) {
+                cols[2 * (i * m + j)] = colo[2 * i] * scale;
+                cols[2 * (i * m + j) + 1] = colo[2 * i + 1] * scale;
+            }
+        }
+        if (jxo_irfft(cols, out + b * h * w, w, h) != 0) return -1;
+    }
+    free(cols); free(col); free(colo);
+    return 0;
+}
+
 /* Plain O(n^2) DFT in f64 (yardstick for the FFT tests). */
 void jxo_dft_f64(const float *in, double *out, int64_t n, int inverse) {
     for (int64_t k = 0; k < n; ++k) {

@@ -105,3 +105,62 @@ def test_full_config_1d_properties(jx, dev, oracle):
     jx.fft_c2c(Y.data_ptr(), Y.data_ptr(), n, batch, True, dev.stream)
     err = float(((Y - X).double() ** 2).sum().sqrt() / (X.double() ** 2).sum().sqrt())
     assert err <= 1e-5
+
+
+# ---- real input / real output (fft, rfft, irfft, rfftn, irfftn) --------------
+@pytest.mark.parametrize("n,batch", [(2, 3), (4, 1), (8, 5), (16, 7), (64, 3), (1024, 9), (4096, 4), (16384, 2)])
+@pytest.mark.parametrize("full", [True, False])
+def test_real_input_fft_vs_oracle(jx, dev, oracle, n, batch, full):
+    rng = np.random.default_rng(n + batch)
+    x = rng.standard_normal((batch, n)).astype(np.float32)
+    bins = n if full else n // 2 + 1
+    X, Y = dev.put(x), dev.full((batch, bins, 2), np.nan)
+    jx.call("jx_fft_r2c_f32", X.data_ptr(), Y.data_ptr(), n, batch, 1 if full else 0, dev.stream)
+    y = dev.get(Y)
+    ref = oracle.fft_real(x, full=full)
+    for b in range(batch):
+        assert normwise_rel(y[b], ref[b]) <= 1e-5
+    y64 = np.fft.fft(x.astype(np.float64), axis=1)[:, :bins]
+    assert normwise_rel(y, np.stack([y64.real, y64.imag], axis=-1)) <= 1e-5
+
+
+@pytest.mark.parametrize("n,batch", [(2, 3), (4, 2), (8, 5), (64, 3), (1024, 9), (4096, 4), (16384, 2)])
+def test_irfft_vs_oracle_and_round_trip(jx, dev, oracle, n, batch):
+    rng = np.random.default_rng(7 * n + batch)
+    x = rng.standard_normal((batch, n)).astype(np.float32)
+    spec = oracle.fft_real(x, full=False)
+    spec[:, 0, 1] = 0.37    # imaginary parts of DC and Nyquist do not reach the output
+    spec[:, -1, 1] = -1.25
+    S, Y = dev.put(spec), dev.full((batch, n), np.nan)
+    jx.call("jx_fft_c2r_f32", S.data_ptr(), Y.data_ptr(), n, batch, dev.stream)
+    y = dev.get(Y)
+    ref = oracle.irfft(spec, n)
+    for b in range(batch):
+        assert normwise_rel(y[b], ref[b]) <= 1e-5
+        assert normwise_rel(y[b], x[b]) <= 1e-5
+
+
+@pytest.mark.parametrize("h,w,batch", [(1, 2, 2), (4, 4, 1), (8, 16, 3), (64, 128, 2), (256, 512, 2)])
+def test_rfftn_irfftn_2d_vs_oracle(jx, dev, oracle, h, w, batch):
+    rng = np.random.default_rng(h * w + batch)
+    x = rng.standard_normal((batch, h, w)).astype(np.float32)
+    m = w // 2 + 1
+    X, S = dev.put(x), dev.full((batch, h, m, 2), np.nan)
+    jx.call("jx_rfft2_f32", X.data_ptr(), S.data_ptr(), h, w, batch, dev.stream)
+    s = dev.get(S)
+    ref = oracle.rfftn2(x)
+    for b in range(batch):
+        assert normwise_rel(s[b], ref[b]) <= 1e-5
+    Y = dev.full((batch, h, w), np.nan)
+    jx.call("jx_irfft2_f32", S.data_ptr(), Y.data_ptr(), h, w, batch, dev.stream)
+    y = dev.get(Y)
+    yref = oracle.irfftn2(ref, w)
+    for b in range(batch):
+        assert normwise_rel(y[b], yref[b]) <= 1e-5
+        assert normwise_rel(y[b], x[b]) <= 1e-5
+
+
+def test_real_fft_rejects_bad_sizes(jx, dev):
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.call("jx_fft_r2c_f32", None, None, 12, 1, 1, dev.stream)
+    assert "power of 2" in e.value.message

@@ -171,3 +171,20 @@ def test_oracle_adam_first_steps(oracle):
     assert np.all(p1 < p)
     np.testing.assert_allclose(p - p1, 0.001, rtol=1e-3)  # first step magnitude ~= lr
     np.testing.assert_allclose(m1, np.float32(0.1) * g, rtol=1e-6)
+
+
+def test_real_fft_known_answers(oracle):
+    """src/ops/fft.rs:666-676 test_rfft (3 bins, DC 10), :721-737
+    test_irfft_reconstruction (|irfft(rfft(x)) - x| < 1e-4), :740-750 rfftn of
+    a 1-D array equals rfft, and fft of real input (:635-646, DC 10, imag 0)."""
+    x = np.array([1, 2, 3, 4], np.float32)
+    r = oracle.fft_real(x, full=False)
+    assert r.size == 6 and abs(r[0, 0] - 10.0) < 1e-5
+    f = oracle.fft_real(x)
+    assert f.size == 8 and abs(f[0, 0] - 10.0) < 1e-5 and abs(f[0, 1]) < 1e-5
+    x8 = np.arange(1, 9, dtype=np.float32)
+    assert np.max(np.abs(oracle.irfft(oracle.fft_real(x8, full=False), 8) - x8)) < 1e-4
+    img = np.arange(1, 17, dtype=np.float32).reshape(4, 4)
+    s = oracle.rfftn2(img)
+    assert s.shape == (4, 3, 2)
+    assert np.max(np.abs(oracle.irfftn2(s, 4) - img)) < 1e-4
