@@ -113,6 +113,15 @@ JX_API int jx_gemm_presplit_f32(const float *Ah, const float *Al, const float *B
  * call on each device looks up the array's address (cudaGetSymbolAddress), so
  * make that first call before any stream capture.  All calls share the array:
  * calls that overlap on the GPU race and must be serialised by the caller. */
+/* No counterpart in the reference (its readback is one blocking copy,
+ * src/buffer.rs:711-749).  C = A . B (3xTF32) with A, B and C in host memory
+ * (pinned for overlap), untransposed: B is uploaded and split once, then row
+ * blocks of block_rows rows (0: about M/8) of A stream through the device
+ * while the product of the previous block runs and the block before that
+ * downloads, on three streams.  The caller's stream waits for the last
+ * download. */
+JX_API int jx_gemm_f32_host(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int64_t ldc, int64_t block_rows, jx_stream_t stream);
 JX_API int jx_gemm_f32_noalloc(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
                                int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                                int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream);
@@ -202,6 +211,14 @@ JX_API int jx_tape_check(const jx_tape *tape);
 /* ins/outs: host arrays of device pointers, each of n elements. */
 JX_API int jx_tape_run(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
                 jx_stream_t stream);
+/* Inputs, outputs and instructions (after the tape's own rewrites). */
+JX_API int jx_tape_info(const jx_tape *tape, int *n_inputs, int *n_outputs, int *n_instr);
+/* jx_tape_run over host buffers (pinned for overlap): blocks of block_elems
+ * elements (0: 8 Mi) stream through the device, uploads, the tape and
+ * downloads on three streams overlapping.  The caller's stream waits for the
+ * last download. */
+JX_API int jx_tape_run_host(const jx_tape *tape, const float *const *ins, float *const *outs, int64_t n,
+                            int64_t block_elems, jx_stream_t stream);
 
 /* ---- random streams (PRNGKey src/random.rs:15-97; uniform_range :161-181;
  *      randint :189-210; normal's CPU arm :259-285)

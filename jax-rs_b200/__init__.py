@@ -75,6 +75,9 @@ _SIGS = {
     "jx_tape_source": [vp, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
     "jx_tape_check": [vp],
     "jx_tape_run": [vp, C.POINTER(vp), C.POINTER(vp), i64, vp],
+    "jx_tape_info": [vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)],
+    "jx_tape_run_host": [vp, C.POINTER(vp), C.POINTER(vp), i64, i64, vp],
+    "jx_gemm_f32_host": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp],
     "jx_fft_r2c_f32": [vp, vp, i64, i64, C.c_int, vp],
     "jx_fft_c2r_f32": [vp, vp, i64, i64, vp],
     "jx_rfft2_f32": [vp, vp, i64, i64, i64, vp],

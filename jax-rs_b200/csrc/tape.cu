@@ -371,6 +371,14 @@ int jx_tape_compile(const jx_tape* tape) {
   return jx::compile_tape(tape, &f);
 }
 
+int jx_tape_info(const jx_tape* tape, int* n_inputs, int* n_outputs, int* n_instr) {
+  JX_REQUIRE(tape, "jx_tape_info: NULL tape");
+  if (n_inputs) *n_inputs = tape->n_in;
+  if (n_outputs) *n_outputs = tape->n_out;
+  if (n_instr) *n_instr = (int)tape->code.size();
+  return JX_OK;
+}
+
 int jx_tape_run(const jx_tape* tape, const float* const* ins, float* const* outs, int64_t n, jx_stream_t stream) {
   JX_REQUIRE(tape, "jx_tape_run: NULL tape");
   JX_REQUIRE(n >= 0, "jx_tape_run: negative size");

@@ -1,0 +1,50 @@
+"""Host-buffer entry points with overlapped transfers (jx_gemm_f32_host,
+jx_tape_run_host): the same results as the device-buffer calls, with pinned
+and with pageable host memory, for ragged block splits."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import normwise_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def _ptr(a):
+    return a.ctypes.data if isinstance(a, np.ndarray) else a.data_ptr()
+
+
+@pytest.mark.parametrize("M,N,K,block", [(1000, 520, 300, 0), (1000, 520, 300, 128), (257, 64, 33, 100),
+                                         (4096, 1024, 2048, 0)])
+@pytest.mark.parametrize("pinned", [True, False])
+def test_gemm_host_matches_oracle(jx, dev, oracle, M, N, K, block, pinned):
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    if pinned:
+        A, B = torch.from_numpy(a).pin_memory(), torch.from_numpy(b).pin_memory()
+        Cm = torch.full((M, N), float("nan")).pin_memory()
+    else:
+        A, B, Cm = a, b, np.full((M, N), np.nan, np.float32)
+    jx.call("jx_gemm_f32_host", _ptr(A), _ptr(B), _ptr(Cm), M, N, K, K, N, N, block, dev.stream)
+    dev.sync()
+    c = Cm.numpy() if pinned else Cm
+    rows = np.unique(np.linspace(0, M - 1, 12).astype(int))
+    ref = oracle.matmul(a[rows], b, nthreads=8)
+    assert normwise_rel(c[rows], ref) <= 1e-5
+    assert np.isfinite(c).all()
+
+
+@pytest.mark.parametrize("n,block", [(1, 0), (1000, 256), (1 << 20, 100000), (3_000_001, 0)])
+def test_tape_run_host_matches_device_run(jx, dev, oracle, n, block):
+    from test_gpu_elementwise import chain_tape, _close
+    x = np.random.default_rng(n).standard_normal(n).astype(np.float32)
+    y = np.full(n, np.nan, np.float32)
+    tape = chain_tape(jx, 1.1, 0.9)
+    ia = (C.c_void_p * 1)(x.ctypes.data)
+    oa = (C.c_void_p * 1)(y.ctypes.data)
+    jx.call("jx_tape_run_host", tape.handle, ia, oa, n, block, dev.stream)
+    dev.sync()
+    assert _close(y, oracle.chain_fwd(x, np.float32(1.1), np.float32(0.9)))
