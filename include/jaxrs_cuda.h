@@ -302,6 +302,14 @@ JX_API int jx_fft_c2c_f32(const float *in, float *out, int64_t n, int64_t batch,
 /* Batched 2-D transform of [batch, h, w] complex images: rows, then columns. */
 JX_API int jx_fft2_c2c_f32(const float *in, float *out, int64_t h, int64_t w, int64_t batch, int inverse,
                     jx_stream_t stream);
+/* jx_fft_c2c_f32 / jx_fft2_c2c_f32 over host buffers (pinned for overlap):
+ * blocks of block_items transforms or images (0: about 32 MiB) stream through
+ * the device, uploads, transforms and downloads overlapping on three
+ * streams; the caller's stream waits for the last download. */
+JX_API int jx_fft_c2c_f32_host(const float *in, float *out, int64_t n, int64_t batch, int inverse,
+                               int64_t block_items, jx_stream_t stream);
+JX_API int jx_fft2_c2c_f32_host(const float *in, float *out, int64_t h, int64_t w, int64_t batch, int inverse,
+                                int64_t block_items, jx_stream_t stream);
 /* Real input / real output (ops::fft::fft with real input :91-126, rfft
  * :212-234, irfft :417-462, rfftn / irfftn in 2-D :474-628).  in [batch][n]
  * real -> out [batch][bins] interleaved complex, bins = full ? n : n/2+1

@@ -79,6 +79,8 @@ _SIGS = {
     "jx_tape_run_host": [vp, C.POINTER(vp), C.POINTER(vp), i64, i64, vp],
     "jx_gemm_f32_host": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp],
     "jx_fft_r2c_f32": [vp, vp, i64, i64, C.c_int, vp],
+    "jx_fft_c2c_f32_host": [vp, vp, i64, i64, C.c_int, i64, vp],
+    "jx_fft2_c2c_f32_host": [vp, vp, i64, i64, i64, C.c_int, i64, vp],
     "jx_fft_c2r_f32": [vp, vp, i64, i64, vp],
     "jx_rfft2_f32": [vp, vp, i64, i64, i64, vp],
     "jx_irfft2_f32": [vp, vp, i64, i64, i64, vp],

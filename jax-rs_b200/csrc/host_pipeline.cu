@@ -74,6 +74,48 @@ struct Events {
   }
 };
 
+// Streams nblk blocks through NBUF device slots: up(i, slot, stream) issues
+// block i's uploads, math(i, slot, stream) its computation, down(i, slot,
+// stream) its downloads.  Slot reuse waits for the block NBUF earlier: its
+// math before the next upload, its download before the next math.  `ready`
+// (may be null) gates the first math (operands shared by every block).
+template <class Up, class Math, class Down>
+int pipeline(long long nblk, Streams* s, Events& ev, cudaStream_t caller, cudaEvent_t ready, Up up, Math math,
+             Down down) {
+  int rc = JX_OK;
+  JX_CUDA(cudaEventRecord(ev.start, caller));
+  for (cudaStream_t x : {s->in, s->comp, s->out}) JX_CUDA(cudaStreamWaitEvent(x, ev.start, 0));
+  if (ready) JX_CUDA(cudaStreamWaitEvent(s->comp, ready, 0));
+  for (long long i = 0; i < nblk && !rc; ++i) {
+    const int b = (int)(i % NBUF);
+    if (i >= NBUF) JX_CUDA(cudaStreamWaitEvent(s->in, ev.done[b], 0));
+    if ((rc = up(i, b, s->in))) break;
+    JX_CUDA(cudaEventRecord(ev.landed[b], s->in));
+    JX_CUDA(cudaStreamWaitEvent(s->comp, ev.landed[b], 0));
+    if (i >= NBUF) JX_CUDA(cudaStreamWaitEvent(s->comp, ev.drained[b], 0));
+    if ((rc = math(i, b, s->comp))) break;
+    JX_CUDA(cudaEventRecord(ev.done[b], s->comp));
+    JX_CUDA(cudaStreamWaitEvent(s->out, ev.done[b], 0));
+    if ((rc = down(i, b, s->out))) break;
+    JX_CUDA(cudaEventRecord(ev.drained[b], s->out));
+  }
+  // the caller's stream waits for all three
+  for (cudaStream_t x : {s->in, s->comp, s->out}) {
+    JX_CUDA(cudaEventRecord(ev.shared, x));
+    JX_CUDA(cudaStreamWaitEvent(caller, ev.shared, 0));
+  }
+  return rc;
+}
+
+int copy_up(void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  JX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
+  return JX_OK;
+}
+int copy_down(void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  JX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st));
+  return JX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -168,36 +210,83 @@ int jx_tape_run_host(const jx_tape* tape, const float* const* ins, float* const*
   const int nio = n_in + n_out;
   void* ws = nullptr;
   if ((rc = jx::scratch_get(sizeof(float) * (size_t)blk * nio * NBUF, &ws, caller))) return rc;
-  JX_CUDA(cudaEventRecord(ev.start, caller));
-  for (cudaStream_t x : {s->in, s->comp, s->out}) JX_CUDA(cudaStreamWaitEvent(x, ev.start, 0));
   auto buf = [&](int slot, int k) { return reinterpret_cast<float*>(ws) + ((size_t)slot * nio + k) * blk; };
-  for (long long i = 0; i < nblk && !rc; ++i) {
-    const int b = (int)(i % NBUF);
-    const long long e0 = i * blk, cnt = std::min(blk, n - e0);
-    if (i >= NBUF) JX_CUDA(cudaStreamWaitEvent(s->in, ev.done[b], 0));
-    for (int k = 0; k < n_in; ++k)
-      JX_CUDA(cudaMemcpyAsync(buf(b, k), ins[k] + e0, sizeof(float) * cnt, cudaMemcpyHostToDevice, s->in));
-    JX_CUDA(cudaEventRecord(ev.landed[b], s->in));
-    JX_CUDA(cudaStreamWaitEvent(s->comp, ev.landed[b], 0));
-    if (i >= NBUF) JX_CUDA(cudaStreamWaitEvent(s->comp, ev.drained[b], 0));
-    const float* tin[JX_TAPE_MAX_IO];
-    float* tout[JX_TAPE_MAX_IO];
-    for (int k = 0; k < n_in; ++k) tin[k] = buf(b, k);
-    for (int k = 0; k < n_out; ++k) tout[k] = buf(b, n_in + k);
-    rc = jx_tape_run(tape, tin, tout, cnt, s->comp);
-    if (rc) break;
-    JX_CUDA(cudaEventRecord(ev.done[b], s->comp));
-    JX_CUDA(cudaStreamWaitEvent(s->out, ev.done[b], 0));
-    for (int k = 0; k < n_out; ++k)
-      JX_CUDA(cudaMemcpyAsync(outs[k] + e0, buf(b, n_in + k), sizeof(float) * cnt, cudaMemcpyDeviceToHost, s->out));
-    JX_CUDA(cudaEventRecord(ev.drained[b], s->out));
-  }
-  for (cudaStream_t x : {s->in, s->comp, s->out}) {
-    JX_CUDA(cudaEventRecord(ev.shared, x));
-    JX_CUDA(cudaStreamWaitEvent(caller, ev.shared, 0));
-  }
+  auto count = [&](long long i) { return std::min(blk, (long long)n - i * blk); };
+  rc = pipeline(
+      nblk, s, ev, caller, nullptr,
+      [&](long long i, int b, cudaStream_t st) {
+        for (int k = 0; k < n_in; ++k) {
+          const int r = copy_up(buf(b, k), ins[k] + i * blk, sizeof(float) * count(i), st);
+          if (r) return r;
+        }
+        return (int)JX_OK;
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        const float* tin[JX_TAPE_MAX_IO];
+        float* tout[JX_TAPE_MAX_IO];
+        for (int k = 0; k < n_in; ++k) tin[k] = buf(b, k);
+        for (int k = 0; k < n_out; ++k) tout[k] = buf(b, n_in + k);
+        return jx_tape_run(tape, tin, tout, count(i), st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        for (int k = 0; k < n_out; ++k) {
+          const int r = copy_down(outs[k] + i * blk, buf(b, n_in + k), sizeof(float) * count(i), st);
+          if (r) return r;
+        }
+        return (int)JX_OK;
+      });
   const int rc2 = jx::scratch_release(ws, caller);
   return rc ? rc : rc2;
+}
+
+// Batched FFTs over host buffers: blocks of whole transforms (1-D rows of n
+// points, or 2-D images of h x w) stream through the device.
+int fft_host(const float* in, float* out, long long elems_per_item, long long items, long long block_items,
+             bool two_d, long long n_or_h, long long w, int inverse, jx_stream_t stream) {
+  cudaStream_t caller = jx::as_stream(stream);
+  Streams* s = nullptr;
+  int rc = streams(&s);
+  if (rc) return rc;
+  Events ev;
+  if ((rc = ev.create())) return rc;
+  const long long per = 2 * elems_per_item;  // floats per item (complex)
+  long long blk = block_items > 0 ? block_items : std::max(1LL, (32LL << 20) / (long long)(per * 4));
+  blk = std::min(blk, items);
+  const long long nblk = (items + blk - 1) / blk;
+  void* ws = nullptr;
+  if ((rc = jx::scratch_get(sizeof(float) * (size_t)(2 * NBUF * blk * per), &ws, caller))) return rc;
+  auto dbuf = [&](int slot, int k) { return reinterpret_cast<float*>(ws) + ((size_t)slot * 2 + k) * blk * per; };
+  auto count = [&](long long i) { return std::min(blk, items - i * blk); };
+  rc = pipeline(
+      nblk, s, ev, caller, nullptr,
+      [&](long long i, int b, cudaStream_t st) {
+        return copy_up(dbuf(b, 0), in + i * blk * per, sizeof(float) * count(i) * per, st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        return two_d ? jx_fft2_c2c_f32(dbuf(b, 0), dbuf(b, 1), n_or_h, w, count(i), inverse, st)
+                     : jx_fft_c2c_f32(dbuf(b, 0), dbuf(b, 1), n_or_h, count(i), inverse, st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        return copy_down(out + i * blk * per, dbuf(b, 1), sizeof(float) * count(i) * per, st);
+      });
+  const int rc2 = jx::scratch_release(ws, caller);
+  return rc ? rc : rc2;
+}
+
+int jx_fft_c2c_f32_host(const float* in, float* out, int64_t n, int64_t batch, int inverse, int64_t block_items,
+                        jx_stream_t stream) {
+  JX_REQUIRE(n >= 1 && batch >= 0, "fft: bad size");
+  if (batch == 0) return JX_OK;
+  JX_REQUIRE(in && out, "fft: NULL pointer");
+  return fft_host(in, out, n, batch, block_items, false, n, 0, inverse, stream);
+}
+
+int jx_fft2_c2c_f32_host(const float* in, float* out, int64_t h, int64_t w, int64_t batch, int inverse,
+                         int64_t block_items, jx_stream_t stream) {
+  JX_REQUIRE(h >= 1 && w >= 1 && batch >= 0, "fft2: bad size");
+  if (batch == 0) return JX_OK;
+  JX_REQUIRE(in && out, "fft2: NULL pointer");
+  return fft_host(in, out, h * w, batch, block_items, true, h, w, inverse, stream);
 }
 
 }  // extern "C"

@@ -48,3 +48,27 @@ def test_tape_run_host_matches_device_run(jx, dev, oracle, n, block):
     jx.call("jx_tape_run_host", tape.handle, ia, oa, n, block, dev.stream)
     dev.sync()
     assert _close(y, oracle.chain_fwd(x, np.float32(1.1), np.float32(0.9)))
+
+
+@pytest.mark.parametrize("n,batch,block", [(4096, 37, 0), (1024, 100, 7), (8, 1000, 64)])
+def test_fft_host_matches_oracle(jx, dev, oracle, n, batch, block):
+    x = np.random.default_rng(n + batch).standard_normal((batch, n, 2)).astype(np.float32)
+    y = np.full_like(x, np.nan)
+    jx.call("jx_fft_c2c_f32_host", x.ctypes.data, y.ctypes.data, n, batch, 0, block, dev.stream)
+    dev.sync()
+    ref = oracle.fft_c2c(x)
+    for b in (0, batch // 2, batch - 1):
+        assert normwise_rel(y[b], ref[b]) <= 1e-5
+
+
+def test_fft2_host_matches_device_call(jx, dev):
+    import torch
+    h, w, batch = 64, 128, 21
+    x = np.random.default_rng(5).standard_normal((batch, h, w, 2)).astype(np.float32)
+    y = np.full_like(x, np.nan)
+    jx.call("jx_fft2_c2c_f32_host", x.ctypes.data, y.ctypes.data, h, w, batch, 1, 4, dev.stream)
+    dev.sync()
+    X = dev.put(x)
+    Y = dev.full(x.shape, np.nan)
+    jx.call("jx_fft2_c2c_f32", X.data_ptr(), Y.data_ptr(), h, w, batch, 1, dev.stream)
+    assert np.array_equal(y, dev.get(Y))  # same kernels, same bits
