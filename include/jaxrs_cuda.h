@@ -70,6 +70,12 @@ JX_API int jx_memcpy_d2d(void *dst, const void *src, size_t nbytes, jx_stream_t 
 JX_API int jx_stream_create(jx_stream_t *stream);
 JX_API int jx_stream_destroy(jx_stream_t stream);
 JX_API int jx_stream_sync(jx_stream_t stream);
+/* Page-lock an existing host range (a Vec<f32>'s storage) so the *_host entry
+ * points and jx_memcpy_* overlap their copies with the math; no reference
+ * counterpart (its readback maps a staging buffer, src/buffer.rs:711-749).
+ * Unregister before the memory is freed. */
+JX_API int jx_host_register(void *ptr, size_t nbytes);
+JX_API int jx_host_unregister(void *ptr);
 
 /* ---- GEMM (gpu_matmul src/backend/ops.rs:460-467; Array::matmul
  *      src/ops/linalg.rs:154-237; einsum "bij,bjk->bik" src/ops/einsum.rs:488-523) */

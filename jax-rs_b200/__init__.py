@@ -61,6 +61,8 @@ _SIGS = {
     "jx_stream_create": [C.POINTER(vp)],
     "jx_stream_destroy": [vp],
     "jx_stream_sync": [vp],
+    "jx_host_register": [vp, C.c_size_t],
+    "jx_host_unregister": [vp],
     "jx_gemm_f32": [vp, vp, vp, i64, i64, i64, ci, ci, i64, i64, i64, i64, i64, i64, i64, ci, vp],
     "jx_gemm_workspace_size": [i64, i64, i64, i64, C.POINTER(C.c_size_t)],
     "jx_gemm_kpad": [i64, C.POINTER(i64)],

@@ -218,4 +218,16 @@ int jx_stream_sync(jx_stream_t stream) {
   return JX_OK;
 }
 
+int jx_host_register(void* ptr, size_t nbytes) {
+  JX_REQUIRE(ptr && nbytes, "jx_host_register: NULL or empty range");
+  JX_CUDA(cudaHostRegister(ptr, nbytes, cudaHostRegisterDefault));
+  return JX_OK;
+}
+
+int jx_host_unregister(void* ptr) {
+  JX_REQUIRE(ptr, "jx_host_unregister: NULL");
+  JX_CUDA(cudaHostUnregister(ptr));
+  return JX_OK;
+}
+
 }  // extern "C"
