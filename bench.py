@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
                    choices=["sgemm", "chain", "chain_grad", "rng", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
-                            "conv", "bgemm"])
+                            "conv", "bgemm", "conv1d", "pool", "batchnorm"])
     p.add_argument("--precision", default=None, choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer (default: exact for mlp, whose one-tile products the "
                         "sequential-k kernel runs faster and bit-identically; 3xtf32 for wide_mlp)")
@@ -265,6 +265,22 @@ def cpu_measure(args, threads, budget_s=8.0):
             O.conv2d_bwd_data(g, w, x.shape, 1, 1, nthreads=threads)
             O.conv2d_bwd_filter(x, g, w.shape, 1, 1, nthreads=threads)
         work, unit, sample = 3 * 2.0 * O_ * C * 9 * 56 * 56 / 1e12, "TFLOP/s", "1 of the 64 images, forward + dX + dW"
+    elif wl == "conv1d":
+        x = rng.standard_normal((1, 256, 4096)).astype(np.float32)
+        w = (rng.standard_normal((256, 256, 3)) * np.sqrt(2.0 / 768)).astype(np.float32)
+        fn = lambda: O.conv1d(x, w, 1, 1, nthreads=threads)
+        work, unit, sample = 2.0 * 256 * 256 * 3 * 4096 / 1e12, "TFLOP/s", "1 of the 64 batch entries"
+    elif wl == "pool":
+        x = rng.standard_normal((2, 256, 112, 112)).astype(np.float32)
+        parts = np.array_split(x.reshape(-1, 112, 112), max(1, threads))
+        fn = lambda: _split_run(lambda p: O.pool2d(p, (3, 3), (2, 2), (1, 1), is_max=True), parts, threads)
+        work, unit, sample = 4.0 * (x.size + x.size // 4) / 1e9, "GB/s", "2 of the 64 batch entries"
+    elif wl == "batchnorm":
+        x = rng.standard_normal((8, 256, 56 * 56)).astype(np.float32)
+        gm = np.ones(256, np.float32)
+        bt = np.zeros(256, np.float32)
+        fn = lambda: O.batchnorm(x, 8, 256, 56 * 56, 1e-5, gm, bt)
+        work, unit, sample = 8.0 * x.size / 1e9, "GB/s", "8 of the 64 batch entries (1 thread: per-channel loop)"
     elif wl == "mlp":
         from oracle import mlp as OM
         Ws, bs = OM.xavier_params([784, 256, 128, 10])
@@ -688,6 +704,101 @@ def run_conv_bgemm(args, dist, jx, torch):
             "clocks": clocks}
 
 
+def run_layers(args, dist, jx, torch):
+    """conv1d: [64,256,4096] x [256,256,3] stride 1 pad 1 (exact f32, the
+    reference's summation order).  pool: 3x3 stride-2 pad-1 max pooling of
+    [64,256,112,112].  batchnorm: batch_norm_2d of [64,256,56,56] with gamma
+    and beta (statistics, then normalisation)."""
+    dev = torch.device("cuda", dist.local)
+    st = torch.cuda.current_stream()
+    s = st.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + dist.rank)
+    B = args.conv_batch or 64
+    if args.workload == "conv1d":
+        C = O = 256
+        L, K = 4096, 3
+        X = torch.randn((B, C, L), device=dev, generator=g)
+        Wt = torch.randn((O, C, K), device=dev, generator=g) * float(np.sqrt(2.0 / (C * K)))
+        Y = torch.empty((B, O, L), device=dev)
+
+        def step():
+            jx.call("jx_conv1d_f32", X.data_ptr(), Wt.data_ptr(), Y.data_ptr(), B, C, O, L, K, 1, 1, s)
+        work = 2.0 * B * O * C * K * L
+        ins, outs, launches = [X, Wt], [Y], 1
+        wl = f"conv1d [{B},256,4096] x [256,256,3] stride 1 pad 1, exact f32 (unfused multiply-add)"
+    elif args.workload == "pool":
+        C, H = 256, 112
+        X = torch.randn((B, C, H, H), device=dev, generator=g)
+        OH = (H + 2 - 3) // 2 + 1
+        Y = torch.empty((B, C, OH, OH), device=dev)
+
+        def step():
+            jx.call("jx_maxpool2d_f32", X.data_ptr(), Y.data_ptr(), B, C, H, H, 3, 3, 2, 1, s)
+        work = 4.0 * (X.numel() + Y.numel())
+        ins, outs, launches = [X], [Y], 1
+        wl = f"maxpool2d 3x3 stride 2 pad 1 over [{B},256,112,112] -> [{B},256,56,56]"
+    else:
+        C, HW = 256, 56 * 56
+        X = torch.randn((B, C, HW), device=dev, generator=g) * 2.0 + 0.5
+        Gm = torch.empty(C, device=dev).uniform_(0.5, 1.5, generator=g)
+        Bt = torch.randn(C, device=dev, generator=g)
+        Y = torch.empty_like(X)
+
+        def step():
+            jx.call("jx_batchnorm_f32", X.data_ptr(), Gm.data_ptr(), Bt.data_ptr(), Y.data_ptr(), B, C, HW, 1e-5,
+                    None, None, s)
+        work = 8.0 * X.numel()
+        ins, outs, launches = [X, Gm, Bt], [Y], 3
+        wl = f"batch_norm_2d [{B},256,56,56] with gamma, beta (statistics + normalisation)"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.stop()
+    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, ins, outs, step, args.e2e_steps)
+    hbm, _, basis = load_peaks()
+    if args.workload == "conv1d":
+        val = work * dist.world / (ms * 1e-3) / 1e12
+        e2e = work * dist.world / (e_ms * 1e-3) / 1e12
+        unit = "TFLOP/s"
+        mhz = clocks.get("sm_max_mhz") or 1965.0
+        peak = 148 * 128 * mhz * 1e6 / 1e12
+        roof = {"bound": "fp32 issue", "kernel": "conv1d_kernel", "achieved": round(val / dist.world, 2),
+                "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(val / dist.world / peak, 4),
+                "peak_basis": f"nominal: 148 SMs x 128 FP32 lanes x {mhz:.0f} MHz, one flop per unfused FMUL or "
+                              "FADD (no measured FP32 peak)", "traffic": None}
+    else:
+        val = work * dist.world / (ms * 1e-3) / 1e9
+        e2e = work * dist.world / (e_ms * 1e-3) / 1e9
+        unit = "GB/s"
+        roof = {"bound": "hbm", "kernel": "pool2d_kernel" if args.workload == "pool" else
+                "norm_stats_wide + norm_finalize + norm_apply (whole call)",
+                "achieved": round(val / dist.world, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(val / dist.world / hbm, 4), "peak_basis": basis, "traffic": None,
+                "note": "algorithmic bytes: one read of x and one write of y" +
+                        ("; the statistics need a second read of x (12 B per element moved at best without L2 "
+                         "reuse), so 8 B per element is a floor no two-pass kernel reaches"
+                         if args.workload == "batchnorm" else "")}
+    return {"metric": METRIC, "value": round(val, 2), "unit": unit, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) (torch generator)",
+            "config": {"workload": wl, "l2": "input > L2", "parallelism": f"batch shards x{dist.world}"},
+            "roofline": roof,
+            "e2e": {"value": round(e2e, 2), "unit": unit, "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out,
+                    "ms_per_step": round(e_ms, 3)},
+            "gpu_launches": args.steps * launches, "clocks": clocks}
+
+
 def run_fft(args, dist, jx, torch):
     """Batched complex FFTs: 1-D n=4096 x 65536, or 2-D 1024x1024 x 256 per rank."""
     dev = torch.device("cuda", dist.local)
@@ -949,6 +1060,8 @@ def main():
         line = run_fft(args, dist, jx, torch)
     elif args.workload in ("conv", "bgemm"):
         line = run_conv_bgemm(args, dist, jx, torch)
+    elif args.workload in ("conv1d", "pool", "batchnorm"):
+        line = run_layers(args, dist, jx, torch)
     else:
         line = run_reduce(args, dist, jx, torch)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:

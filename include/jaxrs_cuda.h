@@ -340,6 +340,51 @@ JX_API int jx_conv2d_bwd_filter_f32(const float *x, const float *dy, float *dw, 
                              int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad,
                              jx_stream_t stream);
 
+/* ---- layers: conv1d, pooling, normalisation ------------------------------- */
+/* gpu_conv1d (src/backend/ops.rs:1014-1025; shader src/backend/shaders.rs:449-519),
+ * nn::conv1d (src/nn.rs:1662-1722: batch = channels = 1, stride 1, padding 0).
+ * x [batch, in_channels, input_len], w [out_channels, in_channels, kernel_len]
+ * -> y [batch, out_channels, (input_len + 2 padding - kernel_len) / stride + 1].
+ * Per output: sum over in-channel, then tap, padded taps skipped, unfused f32:
+ * bit-identical to the reference's loop.  "Kernel size must be <= input size"
+ * (JX_EINVAL) when kernel_len > input_len + 2 padding. */
+JX_API int jx_conv1d_f32(const float *x, const float *w, float *y, int64_t batch, int64_t in_channels,
+                         int64_t out_channels, int64_t input_len, int64_t kernel_len, int64_t stride,
+                         int64_t padding, jx_stream_t stream);
+#define JX_POOL_MAX 0
+#define JX_POOL_AVG 1
+/* Pooling of NCHW planes with a pool_h x pool_w window, per-axis stride and
+ * padding.  Max folds from -inf with f32::max over the in-range taps; average
+ * sums them in row-major order and divides by their count (0 if none):
+ * nn::maxpool2d / avgpool2d (src/nn.rs:2164-2280), and with batch = 1 or
+ * channels = 1 and no padding max_pool2d / avg_pool2d (:1121-1261) and, with
+ * input_h = pool_h = 1, max_pool1d / avg_pool1d (:1002-1100).  Bit-identical. */
+JX_API int jx_pool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,
+                         int64_t input_w, int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w,
+                         int64_t pad_h, int64_t pad_w, int op, jx_stream_t stream);
+/* gpu_maxpool2d / gpu_avgpool2d (src/backend/ops.rs:1204-1215,1359-1370): one
+ * stride and one padding for both axes. */
+JX_API int jx_maxpool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,
+                            int64_t input_w, int64_t pool_h, int64_t pool_w, int64_t stride, int64_t padding,
+                            jx_stream_t stream);
+JX_API int jx_avgpool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,
+                            int64_t input_w, int64_t pool_h, int64_t pool_w, int64_t stride, int64_t padding,
+                            jx_stream_t stream);
+/* global_avg_pool2d / global_max_pool2d (src/nn.rs:2383-2455): [batch,
+ * channels, height, width] -> [batch, channels].  Max is exact; the average
+ * is a tree sum divided by height*width. */
+JX_API int jx_global_pool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t height,
+                                int64_t width, int op, jx_stream_t stream);
+/* gpu_batchnorm (src/backend/ops.rs:1516-1525) / nn::batch_norm_2d (src/nn.rs:
+ * 2303-2360): x [batch, channels, spatial]; per channel, mean and variance
+ * (biased) over batch*spatial, y = (x - mean) / sqrt(var + epsilon) * gamma +
+ * beta.  gamma = beta = NULL drops the affine step: nn::batch_norm [batch,
+ * features] (:656-699) is spatial = 1, nn::layer_norm (:712-725) is batch =
+ * channels = 1.  mean_out / var_out (may be NULL) receive the statistics. */
+JX_API int jx_batchnorm_f32(const float *x, const float *gamma, const float *beta, float *y, int64_t batch,
+                            int64_t channels, int64_t spatial, float epsilon, float *mean_out, float *var_out,
+                            jx_stream_t stream);
+
 /* ---- nn / optim (src/nn.rs:155-221,300-318; src/optim.rs:138-189) -------- */
 /* y[r,:] = softmax(x[r,:]) (src/nn.rs:155-168 applied per row). */
 JX_API int jx_softmax_rows_f32(const float *x, float *y, int64_t rows, int64_t cols, jx_stream_t stream);

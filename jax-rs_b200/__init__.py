@@ -21,6 +21,7 @@ JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, J
 STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "JX_ENCCL", 5: "JX_ETIMEOUT",
                 6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE", 8: "JX_EINTERNAL"}
 PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED = 0, 1, 2
+POOL_MAX, POOL_AVG = 0, 1
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
       "square": 9, "relu": 10, "gelu": 11, "sigmoid": 12, "gelu_grad": 13, "tan": 14, "sign": 15, "sinh": 16,
@@ -63,6 +64,12 @@ _SIGS = {
     "jx_stream_sync": [vp],
     "jx_host_register": [vp, C.c_size_t],
     "jx_host_unregister": [vp],
+    "jx_conv1d_f32": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp],
+    "jx_pool2d_f32": [vp, vp] + [i64] * 10 + [ci, vp],
+    "jx_maxpool2d_f32": [vp, vp] + [i64] * 8 + [vp],
+    "jx_avgpool2d_f32": [vp, vp] + [i64] * 8 + [vp],
+    "jx_global_pool2d_f32": [vp, vp, i64, i64, i64, i64, ci, vp],
+    "jx_batchnorm_f32": [vp, vp, vp, vp, i64, i64, i64, cf, vp, vp, vp],
     "jx_gemm_f32": [vp, vp, vp, i64, i64, i64, ci, ci, i64, i64, i64, i64, i64, i64, i64, ci, vp],
     "jx_gemm_workspace_size": [i64, i64, i64, i64, C.POINTER(C.c_size_t)],
     "jx_gemm_kpad": [i64, C.POINTER(i64)],

@@ -113,6 +113,12 @@ def lib():
         L.jxo_dense_fwd.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64, C.c_int]
         L.jxo_softmax_xent_bwd.argtypes = [f32p, f32p, f32p, i64, i64]
         L.jxo_col_sum.argtypes = [f32p, f32p, i64, i64]
+        L.jxo_conv1d.argtypes = [f32p, f32p, f32p] + [i64] * 7 + [C.c_int]
+        L.jxo_pool2d.argtypes = [f32p, f32p] + [i64] * 9 + [C.c_int]
+        L.jxo_global_pool.argtypes = [f32p, f32p, i64, i64, C.c_int]
+        L.jxo_batchnorm.argtypes = [f32p, C.c_void_p, C.c_void_p, f32p, i64, i64, i64, C.c_float,
+                                    C.c_void_p, C.c_void_p]
+        L.jxo_channel_stats_f64.argtypes = [f32p, i64, i64, i64, f64p, f64p]
         L.jxo_version.restype = C.c_char_p
         _lib = L
     return _lib
@@ -483,3 +489,63 @@ def transpose(x):
     y = np.empty((x.shape[1], x.shape[0]), np.float32)
     lib().jxo_transpose(x, y, x.shape[0], x.shape[1])
     return y
+
+
+# --------------------------------------------------------------------------
+# Layers: conv1d, pooling, normalisation
+# --------------------------------------------------------------------------
+def conv1d(x, w, stride=1, pad=0, nthreads=1):
+    """x [B, C, L], w [O, C, K] -> y [B, O, (L + 2 pad - K) // stride + 1] (conv1d shader order)."""
+    x, w = _c(x), _c(w)
+    B, Ci, L = x.shape
+    O, _, K = w.shape
+    OL = (L + 2 * pad - K) // stride + 1
+    y = np.empty((B, O, OL), np.float32)
+    if lib().jxo_conv1d(x, w, y, B, Ci, L, O, K, stride, pad, nthreads) != 0:
+        raise ValueError("Kernel size must be <= input size")
+    return y
+
+
+def pool2d(x, kernel, stride=None, pad=(0, 0), is_max=True):
+    """x [..., H, W] -> [..., OH, OW]; kernel, stride, pad are (h, w) pairs."""
+    x = _c(x)
+    H, W = x.shape[-2:]
+    kh, kw = kernel
+    sh, sw = stride if stride is not None else kernel
+    ph, pw = pad
+    OH, OW = (H + 2 * ph - kh) // sh + 1, (W + 2 * pw - kw) // sw + 1
+    N = x.size // (H * W) if x.size else 0
+    y = np.empty(x.shape[:-2] + (OH, OW), np.float32)
+    if lib().jxo_pool2d(x, y, N, H, W, kh, kw, sh, sw, ph, pw, 1 if is_max else 0) != 0:
+        raise ValueError("invalid pooling geometry")
+    return y
+
+
+def global_pool(x, is_max=False):
+    """x [B, C, H, W] -> [B, C] (global_avg_pool2d / global_max_pool2d)."""
+    x = _c(x)
+    B, C_, H, W = x.shape
+    y = np.empty((B, C_), np.float32)
+    lib().jxo_global_pool(x, y, B * C_, H * W, 1 if is_max else 0)
+    return y
+
+
+def batchnorm(x, outer, channels, inner, eps, gamma=None, beta=None):
+    """Normalise x viewed as [outer, channels, inner] per channel; returns (y, mean, var)."""
+    x = _c(x)
+    y = np.empty_like(x)
+    mean = np.empty(channels, np.float32)
+    var = np.empty(channels, np.float32)
+    g = _c(gamma) if gamma is not None else None
+    b = _c(beta) if beta is not None else None
+    lib().jxo_batchnorm(x, g.ctypes.data if g is not None else None, b.ctypes.data if b is not None else None,
+                        y, outer, channels, inner, eps, mean.ctypes.data, var.ctypes.data)
+    return y, mean, var
+
+
+def channel_stats_f64(x, outer, channels, inner):
+    x = _c(x)
+    m = np.empty(channels, np.float64)
+    v = np.empty(channels, np.float64)
+    lib().jxo_channel_stats_f64(x, outer, channels, inner, m, v)
+    return m, v

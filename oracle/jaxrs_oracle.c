@@ -886,4 +886,135 @@ void jxo_col_sum(const float *dy, float *db, int64_t B, int64_t N) {
         for (int64_t j = 0; j < N; ++j) db[j] = db[j] + dy[i * N + j];
 }
 
+/* ------------------------------------------------------------------------- */
+/* Layers that the reference runs as WGSL-only kernels or CPU loops:          */
+/* conv1d, 2-D pooling, global pooling, batch / layer normalisation.         */
+/* ------------------------------------------------------------------------- */
+
+/* Batched multi-channel 1-D convolution, the conv1d shader's loop
+ * (src/backend/shaders.rs:449-519, launched by gpu_conv1d
+ * src/backend/ops.rs:1014-1200): y[b,o,p] = sum over ic, then k, of
+ * x[b,ic,p*stride+k-pad] * w[o,ic,k], padded taps skipped, f32 accumulate from
+ * 0.  With batch = channels = 1, stride 1 and pad 0 this is nn::conv1d's CPU
+ * loop (src/nn.rs:1662-1722). */
+typedef struct { const float *x, *w; float *y; int64_t B, C, L, O, K, S, P, OL; } conv1_ctx;
+static void conv1_rows(void *p, int64_t r0, int64_t r1) {
+    conv1_ctx *c = (conv1_ctx *)p;
+    for (int64_t r = r0; r < r1; ++r) {  /* r = b*O + o */
+        int64_t b = r / c->O, o = r % c->O;
+        for (int64_t q = 0; q < c->OL; ++q) {
+            float sum = 0.0f;
+            int64_t start = q * c->S - c->P;
+            for (int64_t ic = 0; ic < c->C; ++ic)
+                for (int64_t k = 0; k < c->K; ++k) {
+                    int64_t ip = start + k;
+                    if (ip < 0 || ip >= c->L) continue;
+                    sum += c->x[(b * c->C + ic) * c->L + ip] * c->w[(o * c->C + ic) * c->K + k];
+                }
+            c->y[r * c->OL + q] = sum;
+        }
+    }
+}
+int jxo_conv1d(const float *x, const float *w, float *y, int64_t B, int64_t C, int64_t L, int64_t O, int64_t K,
+               int64_t stride, int64_t pad, int nthreads) {
+    if (K < 1 || stride < 1 || pad < 0 || L + 2 * pad < K) return -1;
+    conv1_ctx c = {x, w, y, B, C, L, O, K, stride, pad, (L + 2 * pad - K) / stride + 1};
+    parallel_rows(conv1_rows, &c, B * O, nthreads);
+    return 0;
+}
+
+/* 2-D pooling over [N, H, W] planes (N = batch*channels) with separate
+ * window, stride and padding per axis.  Max: init -inf, f32::max over the
+ * in-range taps in (ph, pw) order (nn::maxpool2d src/nn.rs:2164-2211,
+ * max_pool2d :1121-1184, max_pool1d :1002-1047 with h = 1).  Average: the
+ * in-range taps summed in (ph, pw) order from 0 and divided by their count, 0
+ * if none (nn::avgpool2d :2231-2280; avg_pool2d :1199-1261 and avg_pool1d
+ * :1059-1100 divide by the window area, the same count without padding). */
+int jxo_pool2d(const float *x, float *y, int64_t N, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t sh,
+               int64_t sw, int64_t ph_, int64_t pw_, int is_max) {
+    if (kh < 1 || kw < 1 || sh < 1 || sw < 1 || ph_ < 0 || pw_ < 0 || H + 2 * ph_ < kh || W + 2 * pw_ < kw)
+        return -1;
+    int64_t OH = (H + 2 * ph_ - kh) / sh + 1, OW = (W + 2 * pw_ - kw) / sw + 1;
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t oh = 0; oh < OH; ++oh)
+            for (int64_t ow = 0; ow < OW; ++ow) {
+                float acc = is_max ? -INFINITY : 0.0f;
+                int64_t count = 0;
+                for (int64_t a = 0; a < kh; ++a)
+                    for (int64_t b = 0; b < kw; ++b) {
+                        int64_t ih = oh * sh + a - ph_, iw = ow * sw + b - pw_;
+                        if (ih < 0 || ih >= H || iw < 0 || iw >= W) continue;
+                        float v = x[(n * H + ih) * W + iw];
+                        if (is_max) acc = fmaxf(acc, v); else acc += v;
+                        ++count;
+                    }
+                y[(n * OH + oh) * OW + ow] = is_max ? acc : (count > 0 ? acc / (float)count : 0.0f);
+            }
+    return 0;
+}
+
+/* Global pooling of [N, S] rows (N = batch*channels, S = H*W):
+ * global_avg_pool2d (src/nn.rs:2383-2408): sequential sum / S;
+ * global_max_pool2d (:2431-2455): fold from -inf with f32::max. */
+void jxo_global_pool(const float *x, float *y, int64_t N, int64_t S, int is_max) {
+    for (int64_t n = 0; n < N; ++n) {
+        float acc = is_max ? -INFINITY : 0.0f;
+        for (int64_t i = 0; i < S; ++i) acc = is_max ? fmaxf(acc, x[n * S + i]) : acc + x[n * S + i];
+        y[n] = is_max ? acc : acc / (float)S;
+    }
+}
+
+/* Normalisation of x viewed as [outer, C, inner], statistics per channel over
+ * outer*inner elements, in the reference's order: mean = sequential f32 sum /
+ * count, var = sequential f32 sum of (x-mean)^2 / count, std = sqrt(var+eps),
+ * y = (x - mean) / std * gamma + beta (batch_norm_2d src/nn.rs:2303-2360).
+ * gamma == NULL skips the affine step: batch_norm [batch, features]
+ * (:656-699, outer = batch, inner = 1) and layer_norm (:712-725, one
+ * channel over the whole array). */
+void jxo_batchnorm(const float *x, const float *gamma, const float *beta, float *y, int64_t outer, int64_t C,
+                   int64_t inner, float eps, float *mean_out, float *var_out) {
+    float count = (float)(outer * inner);
+    for (int64_t c = 0; c < C; ++c) {
+        float mean = 0.0f;
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) mean += x[(o * C + c) * inner + i];
+        mean /= count;
+        float var = 0.0f;
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) {
+                float d = x[(o * C + c) * inner + i] - mean;
+                var += d * d;
+            }
+        var /= count;
+        float sd = sqrtf(var + eps);
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) {
+                int64_t idx = (o * C + c) * inner + i;
+                float z = (x[idx] - mean) / sd;
+                y[idx] = gamma ? z * gamma[c] + beta[c] : z;
+            }
+        if (mean_out) mean_out[c] = mean;
+        if (var_out) var_out[c] = var;
+    }
+}
+
+/* f64 statistics per channel (two passes in double) for checking device
+ * statistics independently of the f32 summation order. */
+void jxo_channel_stats_f64(const float *x, int64_t outer, int64_t C, int64_t inner, double *mean, double *var) {
+    double cnt = (double)(outer * inner);
+    for (int64_t c = 0; c < C; ++c) {
+        double s = 0.0;
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) s += x[(o * C + c) * inner + i];
+        double m = s / cnt, v = 0.0;
+        for (int64_t o = 0; o < outer; ++o)
+            for (int64_t i = 0; i < inner; ++i) {
+                double d = x[(o * C + c) * inner + i] - m;
+                v += d * d;
+            }
+        mean[c] = m;
+        var[c] = v / cnt;
+    }
+}
+
 const char *jxo_version(void) { return "jaxrs-oracle 1 (restates jax-rs 0.5.1 CPU paths)"; }

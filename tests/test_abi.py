@@ -116,3 +116,23 @@ def test_every_op_compiles(jx):
     code.append((jx.OP_STORE, 1, r, 0))
     t = jx.Tape(code, [0.5], 2, 2)
     t.check()
+
+
+def test_layer_argument_checks(jx):
+    """conv1d, pooling and normalisation reject bad geometry with the
+    reference's assert messages, before touching any memory."""
+    with pytest.raises(jx.JaxRsError, match="Kernel size must be <= input size"):
+        jx.call("jx_conv1d_f32", 1, 1, 1, 1, 1, 1, 4, 5, 1, 0, None)
+    with pytest.raises(jx.JaxRsError, match="Pool size must be positive"):
+        jx.call("jx_pool2d_f32", 1, 1, 1, 1, 4, 4, 0, 2, 1, 1, 0, 0, jx.POOL_MAX, None)
+    with pytest.raises(jx.JaxRsError, match="Stride must be positive"):
+        jx.call("jx_maxpool2d_f32", 1, 1, 1, 1, 4, 4, 2, 2, 0, 0, None)
+    with pytest.raises(jx.JaxRsError, match="larger than the padded input"):
+        jx.call("jx_avgpool2d_f32", 1, 1, 1, 1, 2, 2, 3, 3, 1, 0, None)
+    with pytest.raises(jx.JaxRsError, match="gamma and beta go together"):
+        jx.call("jx_batchnorm_f32", 1, 1, None, 1, 2, 3, 4, 1e-5, None, None, None)
+    with pytest.raises(jx.JaxRsError):
+        jx.call("jx_global_pool2d_f32", 1, 1, 1, 1, 0, 1, 7, None)
+    # empty batches are no-ops
+    jx.call("jx_conv1d_f32", None, None, None, 0, 1, 4, 8, 3, 1, 0, None)
+    jx.call("jx_pool2d_f32", None, None, 0, 3, 4, 4, 2, 2, 2, 2, 0, 0, jx.POOL_AVG, None)

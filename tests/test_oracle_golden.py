@@ -64,6 +64,34 @@ def test_known_answer(oracle, case):
     elif op == "normal_seed":
         got = O.normal(O.key_from_seed(case["seed"]), case["n"])
         np.testing.assert_allclose(got, case["expected"], rtol=case["rtol"], atol=case["atol"])
+    elif op == "conv1d":
+        y = O.conv1d(np.array(case["x"], np.float32), np.array(case["w"], np.float32), case["stride"], case["pad"])
+        if "expected_shape" in case:
+            assert list(y.shape) == case["expected_shape"]
+        else:
+            np.testing.assert_allclose(y, case["expected"], rtol=case["rtol"], atol=case["atol"])
+    elif op == "pool2d":
+        y = O.pool2d(np.array(case["x"], np.float32), tuple(case["kernel"]), tuple(case["stride"]),
+                     tuple(case["pad"]), is_max=case["max"])
+        assert y.tolist() == case["expected"]
+    elif op == "global_pool":
+        y = O.global_pool(np.array(case["x"], np.float32), is_max=case["max"])
+        assert y.tolist() == case["expected"]
+    elif op == "batchnorm":
+        x = np.array(case["x"], np.float32)
+        g = np.array(case["gamma"], np.float32) if "gamma" in case else None
+        b = np.array(case["beta"], np.float32) if "beta" in case else None
+        y, _, _ = O.batchnorm(x, case["outer"], case["channels"], case["inner"], case["eps"], g, b)
+        flat = y.reshape(-1)
+        if "check" in case:
+            for i, v in case["check"].items():
+                assert abs(flat[int(i)] - v) < case["atol"]
+        if "all_within" in case:
+            assert np.all(np.abs(flat) < case["all_within"])
+        if "mean_within" in case:
+            assert abs(float(np.sum(flat, dtype=np.float32)) / flat.size) < case["mean_within"]
+        if "expected_shape" in case:
+            assert list(y.shape) == case["expected_shape"]
     else:
         pytest.fail("unknown case " + op)
 
