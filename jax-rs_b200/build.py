@@ -27,6 +27,9 @@ NVCC_FLAGS = ARCH + [
     "-DJX_BUILD_LIB",
 ]
 LINK_LIBS = ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
+# Per-file flags.  layers.cu computes the reference's unfused f32 arithmetic
+# and wants no contraction anywhere.
+FILE_FLAGS = {"layers.cu": ["--fmad=false"]}
 
 
 def _nccl_flags():
@@ -83,8 +86,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     for src in sources():
         obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
-        if force or _stale(obj, [src] + hdrs):
-            cmd = [NVCC] + NVCC_FLAGS + inc + ["-c", src, "-o", obj]
+        if force or _stale(obj, [src, os.path.abspath(__file__)] + hdrs):
+            cmd = [NVCC] + NVCC_FLAGS + FILE_FLAGS.get(os.path.basename(src), []) + inc + ["-c", src, "-o", obj]
             jobs.append(cmd)
 
     def run(cmd):

@@ -18,7 +18,8 @@
 // bit-identical to the CPU loops.  Global average pooling and the
 // normalisation statistics are tree reductions (tolerance-checked); the
 // normalisation itself, (x - mean) / std * gamma + beta, is evaluated with
-// the reference's operations in its order.
+// the reference's operations in its order, with the mean carried as two f32
+// parts.
 //
 // Layout and bounds.  Everything is NCHW / [outer, channels, inner] row-major
 // f32, as in the reference.  Pooling and global pooling are HBM-bound (one
@@ -35,47 +36,70 @@
 
 namespace {
 
+int grid_for(long long work, int per_block, int cap_per_sm) {
+  const long long want = (work + per_block - 1) / per_block;
+  const long long cap = (long long)jx::num_sms() * cap_per_sm;
+  return (int)std::max(1LL, std::min(want, cap));
+}
+
 // ---------------------------------------------------------------------------
 // conv1d
 // ---------------------------------------------------------------------------
-// Block tile: 64 output channels x 128 output positions, 256 threads.  Warp w
+// Block tile: 64 output channels x 256 output positions, 256 threads.  Warp w
 // owns output channels [8w, 8w+8) of the tile, lane l owns positions
-// l + 32j (j < 4), so each thread keeps 32 accumulators.  Input channels
+// l + 32j (j < 8), so each thread keeps 64 accumulators.  Input channels
 // stream through shared memory in chunks of `icc`:
-//   xs[ic][XW]        the input window of the tile's 128 positions
-//                     (XW = 127*S + K), zero outside [0, L)
+//   xs[ic][XW]        the input window of the tile's 256 positions
+//                     (XW = 255*S + K), zero outside [0, L)
 //   ws[ic][k][64]     the chunk's filter taps, output channel fastest
-// Per output the sum runs over ic, then k, as the shader's loop.  A tap that
-// falls into the padding is skipped, as the shader's bounds check does; a
-// thread whose taps are all in range takes the unchecked loop.
-constexpr int C1_OC = 64, C1_POS = 128, C1_THREADS = 256;
+// Per output the sum runs over ic, then k, as the shader's loop, each step an
+// unfused __fmul_rn then __fadd_rn (the reference's Rust arithmetic), so the
+// result is bit-identical.  A tap that falls into the padding is skipped, as
+// the shader's bounds check does; a warp whose taps are all in range takes
+// the unchecked loop.  The stride and the common tap count 3 are compile-time
+// constants where they can be, so tap addresses are immediate offsets.
+constexpr int C1_OC = 64, C1_NJ = 8, C1_POS = 32 * C1_NJ, C1_THREADS = 256;
 
 struct Conv1dArgs {
   const float* x;
-  const float* w;
+  const float* wt;  // filter as [C*K][Opad], output channel fastest, zero past O
   float* y;
-  long long B, C, L, O, K, S, P, OL;
+  long long B, C, L, O, K, S, P, OL, Opad;
   int icc, xw;
 };
 
-template <bool CHECKED>
+// w [O][C][K] -> wt [C*K][Opad] (Opad = O rounded up to the 64-channel tile).
+__global__ void __launch_bounds__(256) conv1d_filter_kernel(const float* __restrict__ w, float* __restrict__ wt,
+                                                             long long O, long long CK, long long Opad) {
+  const long long total = CK * Opad;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / Opad, o = i - r * Opad;
+    wt[i] = o < O ? __ldg(w + o * CK + r) : 0.0f;
+  }
+}
+
+template <int SS, int KK, bool CHECKED>
 __device__ __forceinline__ void conv1d_chunk(const float* __restrict__ xs, const float* __restrict__ ws,
-                                             float (&acc)[8][4], int nic, int K, int S, int xw, int og, int lane,
-                                             long long in0, long long L) {
+                                             float (&acc)[8][C1_NJ], int nic, int K_rt, int S_rt, int xw, int og,
+                                             int lane, long long in0, long long L) {
+  const int S = SS > 0 ? SS : S_rt;
+  const int K = KK > 0 ? KK : K_rt;
   for (int ic = 0; ic < nic; ++ic) {
-    const float* xr = xs + ic * xw;
+    const float* xr = xs + ic * xw + lane * S;
+    const float* wr = ws + ic * K * C1_OC + og * 8;
+#pragma unroll
     for (int k = 0; k < K; ++k) {
-      const float4* wp = reinterpret_cast<const float4*>(ws + (ic * K + k) * C1_OC + og * 8);
-      const float4 w0 = wp[0], w1 = wp[1];
+      const float4 w0 = *reinterpret_cast<const float4*>(wr + k * C1_OC);
+      const float4 w1 = *reinterpret_cast<const float4*>(wr + k * C1_OC + 4);
       const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int off = (lane + 32 * j) * S + k;
+      for (int j = 0; j < C1_NJ; ++j) {
         if (CHECKED) {
-          const long long ip = in0 + off;
+          const long long ip = in0 + (long long)(lane + 32 * j) * S + k;
           if (ip < 0 || ip >= L) continue;
         }
-        const float xv = xr[off];
+        const float xv = xr[32 * j * S + k];
 #pragma unroll
         for (int r = 0; r < 8; ++r) acc[r][j] = __fadd_rn(acc[r][j], __fmul_rn(xv, wv[r]));
       }
@@ -83,6 +107,7 @@ __device__ __forceinline__ void conv1d_chunk(const float* __restrict__ xs, const
   }
 }
 
+template <int SS, int KK>
 __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
   extern __shared__ __align__(16) float c1_smem[];
   float* ws = c1_smem;                                  // icc * K * 64
@@ -96,40 +121,45 @@ __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
 
   // Whether every tap of this thread's valid outputs is inside [0, L).
   const long long p_first = p0 + lane;
-  long long p_last = p0 + lane + 96;
+  long long p_last = p0 + lane + 32 * (C1_NJ - 1);
   if (p_last >= a.OL) p_last = p0 + lane + 32 * ((a.OL - 1 - p0 - lane) / 32);
   const bool interior = p_first >= a.OL || (p_first * a.S - a.P >= 0 && p_last * a.S - a.P + a.K <= a.L);
   const bool warp_interior = __all_sync(0xffffffffu, interior);
 
-  float acc[8][4];
+  float acc[8][C1_NJ];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[r][j] = 0.0f;
+    for (int j = 0; j < C1_NJ; ++j) acc[r][j] = 0.0f;
 
   for (long long c0 = 0; c0 < a.C; c0 += a.icc) {
     const int nic = (int)min((long long)a.icc, a.C - c0);
     __syncthreads();
-    // filter taps: w[o][c0+ic][k] -> ws[(ic*K + k)*64 + o_local]; reads run
-    // along (ic, k), contiguous in w for a fixed o
-    const int wn = nic * K;
-    for (int i = tid; i < C1_OC * wn; i += C1_THREADS) {
-      const int ol = i / wn, r = i - ol * wn;
-      const long long o = o0 + ol;
-      ws[r * C1_OC + ol] = o < a.O ? __ldg(a.w + (o * a.C + c0) * a.K + r) : 0.0f;
-    }
-    // input window, zero outside [0, L)
+    // filter taps: rows (c0+ic)*K + k of wt, the tile's 64 channels each:
+    // 16 float4 per row, straight copies
+    const int wn4 = nic * K * (C1_OC / 4);
+    const float4* wsrc = reinterpret_cast<const float4*>(a.wt + c0 * a.K * a.Opad + o0);
+    for (int i = tid; i < wn4; i += C1_THREADS)
+      reinterpret_cast<float4*>(ws)[i] = __ldg(wsrc + (long long)(i >> 4) * (a.Opad / 4) + (i & 15));
+    // input window, zero outside [0, L); (ic, off) advanced without division
     const float* xb = a.x + (b * a.C + c0) * a.L;
-    for (int i = tid; i < nic * a.xw; i += C1_THREADS) {
-      const int ic = i / a.xw, off = i - ic * a.xw;
-      const long long ip = in0 + off;
-      xs[i] = (ip >= 0 && ip < a.L) ? __ldg(xb + ic * a.L + ip) : 0.0f;
+    {
+      int ic = tid / a.xw, off = tid - ic * a.xw;
+      for (int i = tid; i < nic * a.xw; i += C1_THREADS) {
+        const long long ip = in0 + off;
+        xs[i] = (ip >= 0 && ip < a.L) ? __ldg(xb + (long long)ic * a.L + ip) : 0.0f;
+        off += C1_THREADS;
+        while (off >= a.xw) {
+          off -= a.xw;
+          ++ic;
+        }
+      }
     }
     __syncthreads();
     if (warp_interior)
-      conv1d_chunk<false>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
+      conv1d_chunk<SS, KK, false>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
     else
-      conv1d_chunk<true>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
+      conv1d_chunk<SS, KK, true>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
   }
 
 #pragma unroll
@@ -138,7 +168,7 @@ __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
     if (o >= a.O) break;
     float* yr = a.y + (b * a.O + o) * a.OL;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < C1_NJ; ++j) {
       const long long p = p0 + lane + 32 * j;
       if (p < a.OL) yr[p] = acc[r][j];
     }
@@ -156,10 +186,23 @@ struct PoolArgs {
 };
 
 // IDX is the index type: 32-bit when every index fits (cheaper division).
-template <bool MAX, typename IDX>
+// KH, KW > 0 fix the window at compile time (fully unrolled); 0 reads it from
+// the arguments.  Out-of-range taps load the fold's neutral value (-inf for
+// max, +0 for the sum) instead of being skipped: the sum starts at +0 and so
+// never holds -0, which makes adding +0 an identity, and max(acc, -inf) = acc,
+// so the result is the reference's bit for bit while every tap's load is
+// issued at once.
+template <bool MAX>
+__device__ __forceinline__ float pool_fold(float acc, float v) {
+  return MAX ? fmaxf(acc, v) : __fadd_rn(acc, v);
+}
+
+template <bool MAX, typename IDX, int KH, int KW>
 __global__ void __launch_bounds__(256) pool2d_kernel(PoolArgs a) {
   const IDX total = (IDX)(a.N * a.OH * a.OW), OW = (IDX)a.OW, OH = (IDX)a.OH;
   const IDX stride = (IDX)gridDim.x * blockDim.x;
+  const float neutral = MAX ? -INFINITY : 0.0f;
+  const int kh = KH > 0 ? KH : a.kh, kw = KW > 0 ? KW : a.kw;
   for (IDX idx = (IDX)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
     const IDX t = idx / OW;
     const IDX ow = idx - t * OW;
@@ -167,22 +210,52 @@ __global__ void __launch_bounds__(256) pool2d_kernel(PoolArgs a) {
     const IDX oh = t - n * OH;
     const float* plane = a.x + (long long)n * a.H * a.W;
     const long long ih0 = (long long)oh * a.sh - a.ph, iw0 = (long long)ow * a.sw - a.pw;
-    float acc = MAX ? -INFINITY : 0.0f;
+    float acc = neutral;
     int count = 0;
-    for (int r = 0; r < a.kh; ++r) {
-      const long long ih = ih0 + r;
-      if (ih < 0 || ih >= a.H) continue;
-      const float* row = plane + ih * a.W;
-      for (int c = 0; c < a.kw; ++c) {
-        const long long iw = iw0 + c;
-        if (iw < 0 || iw >= a.W) continue;
-        const float v = __ldg(row + iw);
-        acc = MAX ? fmaxf(acc, v) : __fadd_rn(acc, v);
-        ++count;
+    if (KH > 0) {
+      float v[KH > 0 ? KH : 1][KW > 0 ? KW : 1];
+#pragma unroll
+      for (int r = 0; r < kh; ++r) {
+        const long long ih = ih0 + r;
+        const bool rok = ih >= 0 && ih < a.H;
+#pragma unroll
+        for (int c = 0; c < kw; ++c) {
+          const long long iw = iw0 + c;
+          const bool ok = rok && iw >= 0 && iw < a.W;
+          v[r][c] = ok ? __ldg(plane + ih * a.W + iw) : neutral;
+          count += ok;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kh; ++r)
+#pragma unroll
+        for (int c = 0; c < kw; ++c) acc = pool_fold<MAX>(acc, v[r][c]);
+    } else {
+      for (int r = 0; r < kh; ++r) {
+        const long long ih = ih0 + r;
+        const bool rok = ih >= 0 && ih < a.H;
+#pragma unroll 4
+        for (int c = 0; c < kw; ++c) {
+          const long long iw = iw0 + c;
+          const bool ok = rok && iw >= 0 && iw < a.W;
+          acc = pool_fold<MAX>(acc, ok ? __ldg(plane + ih * a.W + iw) : neutral);
+          count += ok;
+        }
       }
     }
     a.y[idx] = MAX ? acc : (count ? __fdiv_rn(acc, (float)count) : 0.0f);
   }
+}
+
+template <bool MAX, typename IDX>
+void launch_pool(const PoolArgs& a, cudaStream_t st) {
+  const int grid = grid_for(a.N * a.OH * a.OW, 256, 16);
+  if (a.kh == 2 && a.kw == 2)
+    pool2d_kernel<MAX, IDX, 2, 2><<<grid, 256, 0, st>>>(a);
+  else if (a.kh == 3 && a.kw == 3)
+    pool2d_kernel<MAX, IDX, 3, 3><<<grid, 256, 0, st>>>(a);
+  else
+    pool2d_kernel<MAX, IDX, 0, 0><<<grid, 256, 0, st>>>(a);
 }
 
 // ---------------------------------------------------------------------------
@@ -264,38 +337,61 @@ __device__ __forceinline__ double2 block_sum2(double2 v, double2* red) {
   return v;
 }
 
-__global__ void __launch_bounds__(256) norm_stats_wide(NormArgs a, double2* __restrict__ part) {
-  __shared__ double2 red[8];
-  const long long c = blockIdx.x;
-  const int g = blockIdx.y;
-  const float p = __ldg(a.x + c * a.inner);
-  const bool vec = (a.inner & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
-  const long long per = a.outer * a.inner;
-  long long t = (long long)g * a.chunk;
-  const long long t_end = min(per, t + a.chunk);
-  double2 s = make_double2(0.0, 0.0);
-  while (t < t_end) {
-    const long long o = t / a.inner, i0 = t - o * a.inner, i1 = min(a.inner, i0 + (t_end - t));
-    const float* row = a.x + (o * a.C + c) * a.inner;
-    if (vec) {  // i0 and i1 are multiples of 4 here
-      const float4* r4 = reinterpret_cast<const float4*>(row);
-      for (long long i = i0 / 4 + threadIdx.x; i < i1 / 4; i += blockDim.x) {
-        const float4 v = __ldg(r4 + i);
-        const double d0 = (double)v.x - p, d1 = (double)v.y - p, d2 = (double)v.z - p, d3 = (double)v.w - p;
-        s.x += (d0 + d1) + (d2 + d3);
-        s.y += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+// Wide rows: work items (chunk g, channel c), one warp each, in (g, c) order
+// so the pass reads memory front to back.  A lane issues all U of its loads
+// (float4 when rows are 16-byte aligned) before it sums; chunk is a multiple
+// of the warp's sub-step of 32*U*E elements.
+template <bool VEC>
+__global__ void __launch_bounds__(256) norm_stats_items(NormArgs a, double2* __restrict__ part) {
+  constexpr int U = 8, E = VEC ? 4 : 1, STEP = 32 * U * E;
+  const int lane = threadIdx.x & 31;
+  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+  const long long items = a.C * a.G, per = a.outer * a.inner;
+  for (long long it = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; it < items; it += nw) {
+    const long long g = it / a.C, c = it - g * a.C;
+    const float p = __ldg(a.x + c * a.inner);
+    const long long t0 = g * a.chunk, t1 = min(per, t0 + a.chunk);
+    double sx = 0.0, sy = 0.0;
+    for (long long ts = t0; ts < t1; ts += STEP) {
+      long long t = ts + (long long)lane * E;
+      long long o = t / a.inner, i = t - o * a.inner;
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float* ptr = a.x + (o * a.C + c) * a.inner + i;
+        if (VEC)
+          v[u] = t < t1 ? __ldg(reinterpret_cast<const float4*>(ptr)) : make_float4(p, p, p, p);
+        else
+          v[u].x = t < t1 ? __ldg(ptr) : p;
+        t += 32 * E;
+        i += 32 * E;
+        while (i >= a.inner) {
+          i -= a.inner;
+          ++o;
+        }
       }
-    } else {
-      for (long long i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        const double d = (double)__ldg(row + i) - p;
-        s.x += d;
-        s.y += d * d;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        // shifted values summed in f32 (x - p is exact while x is within a
+        // factor 2 of p), then carried in f64
+        if (VEC) {
+          const float d0 = v[u].x - p, d1 = v[u].y - p, d2 = v[u].z - p, d3 = v[u].w - p;
+          sx += (double)((d0 + d1) + (d2 + d3));
+          sy += (double)((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3));
+        } else {
+          const float d = v[u].x - p;
+          sx += (double)d;
+          sy += (double)(d * d);
+        }
       }
     }
-    t += i1 - i0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      sx += __shfl_xor_sync(0xffffffffu, sx, off);
+      sy += __shfl_xor_sync(0xffffffffu, sy, off);
+    }
+    if (lane == 0) part[it] = make_double2(sx, sy);
   }
-  s = block_sum2(s, red);
-  if (threadIdx.x == 0) part[(long long)g * a.C + c] = s;
 }
 
 __global__ void __launch_bounds__(256) norm_stats_narrow(NormArgs a, double2* __restrict__ part) {
@@ -306,91 +402,109 @@ __global__ void __launch_bounds__(256) norm_stats_narrow(NormArgs a, double2* __
   const long long c = col / a.inner;
   const float p = __ldg(a.x + c * a.inner);
   double2 s = make_double2(0.0, 0.0);
-  for (long long o = g; o < a.outer; o += a.G) {
-    const double d = (double)__ldg(a.x + o * cols + col) - p;
-    s.x += d;
-    s.y += d * d;
+  for (long long o = g; o < a.outer; o += 4LL * a.G) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long r = o + (long long)u * a.G;
+      v[u] = r < a.outer ? __ldg(a.x + r * cols + col) : p;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const double d = (double)v[u] - p;
+      s.x += d;
+      s.y += d * d;
+    }
   }
   part[(long long)g * cols + col] = s;
 }
 
-// One warp per channel: combine the partials, then mean, var and
-// std = sqrt(var + eps) in f32 as the reference computes std.
+// One block per channel: combine the partials in a fixed order, then mean,
+// var and std = sqrt(var + eps) in f32 as the reference computes std.  The
+// mean is kept as hi + lo (two f32 values) so that x - mean loses nothing to
+// the mean's own rounding when the mean is large against the spread.
 __global__ void __launch_bounds__(256) norm_finalize(NormArgs a, const double2* __restrict__ part, bool wide,
-                                                     float eps, float2* __restrict__ ms, float* __restrict__ mean_out,
+                                                     float eps, float4* __restrict__ ms, float* __restrict__ mean_out,
                                                      float* __restrict__ var_out) {
-  const int lane = threadIdx.x & 31;
-  const long long c = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (c >= a.C) return;
+  __shared__ double2 red[8];
+  const long long c = blockIdx.x;
   double2 s = make_double2(0.0, 0.0);
   if (wide) {
-    for (int g = lane; g < a.G; g += 32) s = add2(s, part[(long long)g * a.C + c]);
+    for (long long g = threadIdx.x; g < a.G; g += blockDim.x) s = add2(s, part[g * a.C + c]);
   } else {
     const long long cols = a.C * a.inner, m = (long long)a.G * a.inner;
-    for (long long t = lane; t < m; t += 32) {
+    for (long long t = threadIdx.x; t < m; t += blockDim.x) {
       const long long g = t / a.inner, i = t - g * a.inner;
       s = add2(s, part[g * cols + c * a.inner + i]);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
-    s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
-  }
-  if (lane == 0) {
+  s = block_sum2(s, red);
+  if (threadIdx.x == 0) {
     const double n = (double)a.outer * (double)a.inner;
     const double p = (double)__ldg(a.x + c * a.inner);
     const double d = s.x / n;
     const double var = fmax(s.y / n - d * d, 0.0);
-    const float mean_f = (float)(p + d), var_f = (float)var;
-    ms[c] = make_float2(mean_f, sqrtf(var_f + eps));
+    const double mean = p + d;
+    const float mean_f = (float)mean, var_f = (float)var;
+    ms[c] = make_float4(mean_f, (float)(mean - (double)mean_f), sqrtf(var_f + eps), 0.0f);
     if (mean_out) mean_out[c] = mean_f;
     if (var_out) var_out[c] = var_f;
   }
 }
 
-// y = (x - mean) / std * gamma + beta, unfused, in the reference's order.
-// The grid sweeps the tensor from its end to its start, so the statistics
-// pass's most recent reads (still in L2) are read first.
+// y = (x - mean) / std * gamma + beta, unfused, in the reference's order
+// (x - mean taken as (x - hi) - lo).  Each thread handles four units one grid
+// apart per pass, loads first; the passes walk the tensor from its end to its
+// start, so the statistics pass's most recent reads (still in L2) come first.
 template <bool AFFINE>
-__device__ __forceinline__ float norm1(float v, float2 m, float g, float b) {
-  const float z = __fdiv_rn(__fsub_rn(v, m.x), m.y);
+__device__ __forceinline__ float norm1(float v, float4 m, float g, float b) {
+  const float z = __fdiv_rn(__fsub_rn(__fsub_rn(v, m.x), m.y), m.z);
   return AFFINE ? __fadd_rn(__fmul_rn(z, g), b) : z;
 }
 
 template <bool AFFINE, bool VEC, typename IDX>
 __global__ void __launch_bounds__(256) norm_apply(const float* __restrict__ x, float* __restrict__ y,
-                                                  const float2* __restrict__ ms, const float* __restrict__ gamma,
+                                                  const float4* __restrict__ ms, const float* __restrict__ gamma,
                                                   const float* __restrict__ beta, long long n, long long C_,
                                                   long long inner_) {
+  constexpr int U = 4;
   const IDX units = (IDX)(VEC ? n / 4 : n), C = (IDX)C_, inner = (IDX)inner_;
   const IDX nthreads = (IDX)gridDim.x * blockDim.x;
   const IDX tid = (IDX)blockIdx.x * blockDim.x + threadIdx.x;
-  for (IDX sweep = (units + nthreads - 1) / nthreads; sweep-- > 0;) {
-    const IDX u = sweep * nthreads + tid;
-    if (u >= units) continue;
-    const IDX e = VEC ? u * 4 : u;
-    const IDX c = (e / inner) % C;
-    const float2 m = ms[c];
-    const float g = AFFINE ? __ldg(gamma + c) : 1.0f, b = AFFINE ? __ldg(beta + c) : 0.0f;
-    if (VEC) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(x) + u);
-      float4 r;
-      r.x = norm1<AFFINE>(v.x, m, g, b);
-      r.y = norm1<AFFINE>(v.y, m, g, b);
-      r.z = norm1<AFFINE>(v.z, m, g, b);
-      r.w = norm1<AFFINE>(v.w, m, g, b);
-      reinterpret_cast<float4*>(y)[u] = r;
-    } else {
-      y[u] = norm1<AFFINE>(__ldg(x + u), m, g, b);
+  const IDX per = nthreads * U;
+  for (IDX pass = (units + per - 1) / per; pass-- > 0;) {
+    const IDX base = pass * per + tid;
+    float4 v[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const IDX u = base + (IDX)k * nthreads;
+      if (u < units) {
+        if (VEC)
+          v[k] = __ldg(reinterpret_cast<const float4*>(x) + u);
+        else
+          v[k].x = __ldg(x + u);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const IDX u = base + (IDX)k * nthreads;
+      if (u >= units) continue;
+      const IDX e = VEC ? u * 4 : u;
+      const IDX c = (e / inner) % C;
+      const float4 m = ms[c];
+      const float g = AFFINE ? __ldg(gamma + c) : 1.0f, b = AFFINE ? __ldg(beta + c) : 0.0f;
+      if (VEC) {
+        float4 r;
+        r.x = norm1<AFFINE>(v[k].x, m, g, b);
+        r.y = norm1<AFFINE>(v[k].y, m, g, b);
+        r.z = norm1<AFFINE>(v[k].z, m, g, b);
+        r.w = norm1<AFFINE>(v[k].w, m, g, b);
+        reinterpret_cast<float4*>(y)[u] = r;
+      } else {
+        y[u] = norm1<AFFINE>(v[k].x, m, g, b);
+      }
     }
   }
-}
-
-int grid_for(long long work, int per_block, int cap_per_sm) {
-  const long long want = (work + per_block - 1) / per_block;
-  const long long cap = (long long)jx::num_sms() * cap_per_sm;
-  return (int)std::max(1LL, std::min(want, cap));
 }
 
 }  // namespace
@@ -415,7 +529,6 @@ int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64
              "jx_conv1d_f32: batch <= 65535 and out_channels <= %d", 65535 * C1_OC);
   Conv1dArgs a;
   a.x = x;
-  a.w = w;
   a.y = y;
   a.B = batch;
   a.C = in_channels;
@@ -431,13 +544,28 @@ int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64
   a.icc = (int)std::max(1LL, std::min({16LL, (long long)in_channels, budget / per_ic}));
   const size_t smem = (size_t)a.icc * per_ic * 4;
   JX_REQUIRE(smem <= 200 * 1024, "jx_conv1d_f32: window too large for shared memory");
-  if (smem > 48 * 1024) JX_CUDA(cudaFuncSetAttribute(conv1d_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     (int)smem));
+  void (*kern)(Conv1dArgs) = stride == 1 ? (kernel_len == 3 ? conv1d_kernel<1, 3> : conv1d_kernel<1, 0>)
+                            : stride == 2 ? conv1d_kernel<2, 0> : conv1d_kernel<0, 0>;
+  if (smem > 48 * 1024)
+    JX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const dim3 grid((unsigned)((OL + C1_POS - 1) / C1_POS), (unsigned)((out_channels + C1_OC - 1) / C1_OC),
                   (unsigned)batch);
-  conv1d_kernel<<<grid, C1_THREADS, smem, jx::as_stream(stream)>>>(a);
-  JX_LAUNCH_CHECK("conv1d_kernel");
-  return JX_OK;
+  cudaStream_t st = jx::as_stream(stream);
+  a.Opad = (out_channels + C1_OC - 1) / C1_OC * C1_OC;
+  const long long ck = in_channels * kernel_len;
+  void* ws = nullptr;
+  if (int rc = jx::scratch_get((size_t)(ck * a.Opad) * sizeof(float), &ws, st)) return rc;
+  a.wt = static_cast<const float*>(ws);
+  conv1d_filter_kernel<<<grid_for(ck * a.Opad, 256, 8), 256, 0, st>>>(w, static_cast<float*>(ws), out_channels, ck,
+                                                                       a.Opad);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    kern<<<grid, C1_THREADS, smem, st>>>(a);
+    e = cudaGetLastError();
+  }
+  const int rc = e == cudaSuccess ? JX_OK : jx::check_cuda(e, "conv1d kernels");
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
 }
 
 int jx_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
@@ -471,19 +599,18 @@ int jx_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int
   const long long total = a.N * a.OH * a.OW;
   if (total == 0) return JX_OK;
   JX_REQUIRE(x && y, "jx_pool2d_f32: NULL buffer");
-  const int grid = grid_for(total, 256, 16);
-  const bool small = total + 256LL * grid < (1LL << 31) && a.N * a.H * a.W < (1LL << 31);
+  const bool small = total + 256LL * 16 * jx::num_sms() < (1LL << 31) && a.N * a.H * a.W < (1LL << 31);
   cudaStream_t st = jx::as_stream(stream);
   if (op == JX_POOL_MAX) {
     if (small)
-      pool2d_kernel<true, unsigned><<<grid, 256, 0, st>>>(a);
+      launch_pool<true, unsigned>(a, st);
     else
-      pool2d_kernel<true, long long><<<grid, 256, 0, st>>>(a);
+      launch_pool<true, long long>(a, st);
   } else {
     if (small)
-      pool2d_kernel<false, unsigned><<<grid, 256, 0, st>>>(a);
+      launch_pool<false, unsigned>(a, st);
     else
-      pool2d_kernel<false, long long><<<grid, 256, 0, st>>>(a);
+      launch_pool<false, long long>(a, st);
   }
   JX_LAUNCH_CHECK("pool2d_kernel");
   return JX_OK;
@@ -531,17 +658,22 @@ int jx_batchnorm_f32(const float* x, const float* gamma, const float* beta, floa
   a.C = channels;
   a.inner = spatial;
   const bool wide = spatial >= 128;
-  const long long target = 4LL * jx::num_sms();  // blocks for the statistics pass
+  const bool vec_rows = (spatial & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   long long parts;
   a.chunk = 0;
+  int stats_grid = 0;
   if (wide) {
-    const long long per = batch * spatial;
-    const long long g = std::max(1LL, std::min({(target + channels - 1) / channels, (per + 4095) / 4096, 4096LL}));
-    a.chunk = ((per + g - 1) / g + 3) / 4 * 4;
-    a.G = (int)((per + a.chunk - 1) / a.chunk);
-    JX_REQUIRE(channels <= 0x7fffffffLL, "jx_batchnorm_f32: too many channels");
-    parts = (long long)a.G * channels;
+    const long long per = batch * spatial, step = vec_rows ? 1024 : 256;
+    const long long target_items = 256LL * jx::num_sms();  // about 4 per resident warp
+    const long long m = std::max(1LL, (channels * ((per + step - 1) / step) + target_items - 1) / target_items);
+    a.chunk = m * step;
+    const long long G = (per + a.chunk - 1) / a.chunk;
+    JX_REQUIRE(G <= 0x7fffffffLL && channels <= 0x7fffffffLL, "jx_batchnorm_f32: too many items");
+    a.G = (int)G;
+    parts = G * channels;
+    stats_grid = grid_for(parts * 32, 256, 8);
   } else {
+    const long long target = 8LL * jx::num_sms();
     const long long cols = channels * spatial, col_blocks = (cols + 255) / 256;
     JX_REQUIRE(col_blocks <= 0x7fffffffLL, "jx_batchnorm_f32: too many columns");
     a.G = (int)std::max(1LL, std::min({(long long)batch, (target + col_blocks - 1) / col_blocks, 1024LL}));
@@ -549,17 +681,19 @@ int jx_batchnorm_f32(const float* x, const float* gamma, const float* beta, floa
   }
   void* ws = nullptr;
   const size_t part_bytes = (size_t)parts * sizeof(double2);
-  if (int rc = jx::scratch_get(part_bytes + (size_t)channels * sizeof(float2), &ws, st)) return rc;
+  if (int rc = jx::scratch_get(part_bytes + (size_t)channels * sizeof(float4), &ws, st)) return rc;
   double2* part = static_cast<double2*>(ws);
-  float2* ms = reinterpret_cast<float2*>(static_cast<char*>(ws) + part_bytes);
+  float4* ms = reinterpret_cast<float4*>(static_cast<char*>(ws) + part_bytes);
   int rc = JX_OK;
-  if (wide)
-    norm_stats_wide<<<dim3((unsigned)channels, (unsigned)a.G), 256, 0, st>>>(a, part);
+  if (wide && vec_rows)
+    norm_stats_items<true><<<stats_grid, 256, 0, st>>>(a, part);
+  else if (wide)
+    norm_stats_items<false><<<stats_grid, 256, 0, st>>>(a, part);
   else
     norm_stats_narrow<<<dim3((unsigned)((channels * spatial + 255) / 256), (unsigned)a.G), 256, 0, st>>>(a, part);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) {
-    norm_finalize<<<(unsigned)((channels + 7) / 8), 256, 0, st>>>(a, part, wide, epsilon, ms, mean_out, var_out);
+    norm_finalize<<<(unsigned)channels, 256, 0, st>>>(a, part, wide, epsilon, ms, mean_out, var_out);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
@@ -567,7 +701,7 @@ int jx_batchnorm_f32(const float* x, const float* gamma, const float* beta, floa
     const bool vec = (spatial & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(y) & 15) == 0;
     const int grid = grid_for(vec ? n / 4 : n, 256, 8);
-    const bool small = n + 256LL * grid < (1LL << 31);
+    const bool small = n + 4LL * 256 * grid < (1LL << 31);
 #define JX_NORM_APPLY(AFF, VEC)                                                                   \
   do {                                                                                            \
     if (small)                                                                                    \
