@@ -294,6 +294,103 @@ int twiddles(int logn, const float2** out) {
   return JX_OK;
 }
 
+// ---- 1024-point transforms as 32 x 32 in registers ------------------------
+// n = n2 + 32 n1, k = k1 + 32 k2:
+//   X[k1 + 32 k2] = sum_n2 W1024^(n2 k1) [sum_n1 x[n2 + 32 n1] W32^(n1 k1)] W32^(n2 k2).
+// A thread owns one n2 (then one k1) of one transform: it loads 32 points,
+// does the inner 32-point DFT in registers, applies W1024^(n2 k1) from the
+// table, passes the values through shared memory once (a transpose), and
+// does the outer 32-point DFT in registers.  Used for the column pass of 2-D
+// transforms (rows measured faster on fft_kernel): C = 8 adjacent columns per
+// CTA of 256 threads, a warp spanning the 8 columns x 4 consecutive points,
+// so every global access is a 64-byte row segment (4 columns per CTA, 32-byte
+// segments, measured slower).  With a row stride of 33 and a column region of
+// 1060 eight-byte slots the transpose's writes and reads each touch every
+// bank pair exactly twice per warp.
+constexpr int F32_C = 8, F32_KS = 33, F32_RS = 1060;
+
+// 32-point DFT, natural order in and out: two 16-point DFTs of the even and
+// odd points, then X[k] = E[k] + W32^k O[k], X[k+16] = E[k] - W32^k O[k].
+template <bool INV>
+__device__ __forceinline__ void dft32(cf2* v) {
+  cf2 e[16], o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    e[i] = v[2 * i];
+    o[i] = v[2 * i + 1];
+  }
+  dft16<INV>(e);
+  dft16<INV>(o);
+  // cos(2 pi k / 32), k = 0..8
+  constexpr float C32[9] = {1.0f, 0.98078528040323044913f, 0.92387953251128675613f, 0.83146961230254523708f,
+                            0.70710678118654752440f, 0.55557023301960222474f, 0.38268343236508977173f,
+                            0.19509032201612826785f, 0.0f};
+  const float sg = INV ? 1.0f : -1.0f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    // W32^k = (cos(2 pi k/32), sg sin(2 pi k/32)); sin(2 pi k/32) = cos(2 pi (8-k)/32)
+    const float c = k <= 8 ? C32[k] : -C32[16 - k];
+    const float sn = k <= 8 ? C32[8 - k] : C32[k - 8];
+    const cf2 t = k == 0 ? o[0] : cmul(o[k], cf2{c, sg * sn});
+    v[k] = cadd(e[k], t);
+    v[k + 16] = csub(e[k], t);
+  }
+}
+
+template <bool COLS, bool INV>
+__global__ void __launch_bounds__(32 * F32_C, 16 / F32_C)
+    fft1024_kernel(const float2* __restrict__ in, float2* __restrict__ out, long long ntrans, Addr<COLS> ad,
+                   const float2* __restrict__ tw, float scale) {
+  extern __shared__ float2 f32_raw[];
+  cf2* S = reinterpret_cast<cf2*>(f32_raw);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  static_assert(COLS, "rows use fft_kernel");
+  const int c = lane % F32_C;                           // column within the CTA
+  const int q = w * (32 / F32_C) + lane / F32_C;        // n2, then k1
+  const long long t = (long long)blockIdx.x * F32_C + c;
+  const bool active = t < ntrans;
+  const long long gb = ad.base(active ? t : 0), ob = ad.obase(active ? t : 0), es = ad.estride();
+  cf2 v[32];
+#pragma unroll
+  for (int n1 = 0; n1 < 32; ++n1) {
+    const float2 x = active ? __ldcs(in + gb + (long long)(q + 32 * n1) * es) : make_float2(0.f, 0.f);
+    v[n1] = {x.x, x.y};
+  }
+  dft32<INV>(v);  // v[k1] = Y[n2 = q][k1]
+#pragma unroll
+  for (int k1 = 1; k1 < 32; ++k1) {
+    const float2 wv = __ldg(tw + ((q * k1) & 1023));
+    v[k1] = cmul(v[k1], cf2{wv.x, INV ? -wv.y : wv.y});
+  }
+  cf2* Sc = S + c * F32_RS;
+#pragma unroll
+  for (int k1 = 0; k1 < 32; ++k1) Sc[k1 * F32_KS + q] = v[k1];
+  __syncthreads();
+#pragma unroll
+  for (int n2 = 0; n2 < 32; ++n2) v[n2] = Sc[q * F32_KS + n2];  // now q = k1
+  dft32<INV>(v);  // v[k2] = X[q + 32 k2]
+  if (active) {
+#pragma unroll
+    for (int k2 = 0; k2 < 32; ++k2)
+      __stcs(out + ob + (long long)(q + 32 * k2) * es, make_float2(v[k2].x * scale, v[k2].y * scale));
+  }
+}
+
+template <bool COLS>
+int launch_fft1024(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, bool inv, float scale,
+                   cudaStream_t st) {
+  const size_t smem = sizeof(float2) * (size_t)F32_C * F32_RS;
+  const float2* tw = nullptr;
+  if (int rc = twiddles(10, &tw)) return rc;
+  const long long blocks = (ntrans + F32_C - 1) / F32_C;
+  JX_REQUIRE(blocks < (1LL << 31), "fft: batch too large");
+  auto k = inv ? fft1024_kernel<COLS, true> : fft1024_kernel<COLS, false>;
+  JX_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<(unsigned)blocks, 32 * F32_C, smem, st>>>(in, out, ntrans, ad, tw, scale);
+  JX_LAUNCH_CHECK("fft1024_kernel");
+  return JX_OK;
+}
+
 template <int LOGN, int TPC, bool COLS>
 int launch_fft(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, bool inv, float scale,
                cudaStream_t st) {
@@ -331,6 +428,9 @@ int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, lo
     return launch_fft<LOGN, TPC, false>(in, out, ntrans, ad, inv, scale, st);
   }
   Addr<true> ad{N, w, hw, 0};
+  if constexpr (LOGN == 10) {
+    if (w % F32_C == 0) return launch_fft1024<true>(in, out, ntrans, ad, inv, scale, st);
+  }
   if constexpr (N <= 1024) {
     // 8 adjacent columns (64-byte row segments) per CTA: small enough that
     // several CTAs share an SM, so one CTA's loads overlap another's math.

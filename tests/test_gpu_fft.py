@@ -108,7 +108,7 @@ def test_full_config_1d_properties(jx, dev, oracle):
 
 
 # ---- real input / real output (fft, rfft, irfft, rfftn, irfftn) --------------
-@pytest.mark.parametrize("n,batch", [(2, 3), (4, 1), (8, 5), (16, 7), (64, 3), (1024, 9), (4096, 4), (16384, 2)])
+@pytest.mark.parametrize("n,batch", [(2, 3), (4, 1), (8, 5), (16, 7), (64, 3), (1024, 9), (2048, 5), (4096, 4), (16384, 2)])
 @pytest.mark.parametrize("full", [True, False])
 def test_real_input_fft_vs_oracle(jx, dev, oracle, n, batch, full):
     rng = np.random.default_rng(n + batch)
@@ -124,7 +124,7 @@ def test_real_input_fft_vs_oracle(jx, dev, oracle, n, batch, full):
     assert normwise_rel(y, np.stack([y64.real, y64.imag], axis=-1)) <= 1e-5
 
 
-@pytest.mark.parametrize("n,batch", [(2, 3), (4, 2), (8, 5), (64, 3), (1024, 9), (4096, 4), (16384, 2)])
+@pytest.mark.parametrize("n,batch", [(2, 3), (4, 2), (8, 5), (64, 3), (1024, 9), (2048, 5), (4096, 4), (16384, 2)])
 def test_irfft_vs_oracle_and_round_trip(jx, dev, oracle, n, batch):
     rng = np.random.default_rng(7 * n + batch)
     x = rng.standard_normal((batch, n)).astype(np.float32)
