@@ -160,11 +160,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // row-major, straight from the caller's f32 buffers (no split pass, no
 // workspace).  TMA streams the raw tiles -- A K-major with 128-byte swizzle,
 // B MN-major as eight 32 x 32 boxes in the SWIZZLE_128B_ATOM_32B layout --
-// into the hi slots of the stage; the eight epilogue warps then split every
-// value in place (hi over the raw value, lo into the lo slot, same offset, so
-// the layout is kept), publish the stage to the tensor core and, as in the
-// pre-split kernel, drain the TMEM span partials and store C.  K beyond the
-// matrix reads TMA's zero fill.  Warpgroup 0 (TMA, MMA, two idle warps) gives
+// into the hi slots of the stage, where they stay: the tf32 MMA reads a raw
+// f32 value as hi = trunc(x) (its low 13 bits ignored), so the hi.hi products
+// start as soon as the tiles land.  Meanwhile the eight epilogue warps write
+// lo = tf32_rn(x - trunc(x)) into the lo slot (same offset, so the layout is
+// kept) and publish it for the two cross products; as in the pre-split kernel
+// they then drain the TMEM span partials and store C.  The operand error per
+// element is at most 2^-21 relative (2^-22 for the pre-split kernel's
+// round-to-nearest hi).  K beyond the matrix reads TMA's zero fill.  Warpgroup 0 (TMA, MMA, two idle warps) gives
 // registers to the two epilogue warpgroups: 128 x 40 + 256 x 232 = 384 x 168.
 // ---------------------------------------------------------------------------
 constexpr int FS_THREADS = 384;
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1)
     }
     // ---------------- MMA issuer ----------------
     if (warp == 1 && jxd::elect_one())
-      mma_issuer<true>(smem, full, empty, sfull, sempty, tmem_base, num_tiles, num_kb, abort_flag, err);
+      mma_issuer<true>(smem, full, empty, sfull, sempty, tmem_base, num_tiles, num_kb, abort_flag, err, raw_full);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FS_HIGH_REGS));
     // ---------------- split the stage in place, drain spans, store C ----------------
@@ -280,12 +283,11 @@ __global__ void __launch_bounds__(FS_THREADS, 1)
           uint8_t* hp = f < A_TILE / 16 ? st + f * 16 : st + 2 * A_TILE + (f - A_TILE / 16) * 16;
           const int lo_off = f < A_TILE / 16 ? A_TILE : B_TILE;
           const float4 x = *reinterpret_cast<const float4*>(hp);
-          float4 h, l;
-          jxd::split_tf32(x.x, h.x, l.x);
-          jxd::split_tf32(x.y, h.y, l.y);
-          jxd::split_tf32(x.z, h.z, l.z);
-          jxd::split_tf32(x.w, h.w, l.w);
-          *reinterpret_cast<float4*>(hp) = h;
+          float4 l;
+          l.x = jxd::tf32_lo_of_trunc(x.x);
+          l.y = jxd::tf32_lo_of_trunc(x.y);
+          l.z = jxd::tf32_lo_of_trunc(x.z);
+          l.w = jxd::tf32_lo_of_trunc(x.w);
           *reinterpret_cast<float4*>(hp + lo_off) = l;
         }
         jxd::fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads

@@ -243,6 +243,16 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   lo = __uint_as_float(l);
 }
 
+// lo part for a hi taken as the truncation of x to tf32 (what the tf32 MMA
+// reads from a raw f32 value): x - trunc(x) is exact in f32, then rounded to
+// the nearest tf32.
+__device__ __forceinline__ float tf32_lo_of_trunc(float x) {
+  const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  uint32_t l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(__fsub_rn(x, hi)));
+  return __uint_as_float(l);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

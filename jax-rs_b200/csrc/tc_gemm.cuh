@@ -78,10 +78,15 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, uns
 // bounds that bias (over a full K it would grow linearly with K).
 // B_MN: the B tiles are MN-major (row-major B streamed as 32 x 32 boxes, 4 KB
 // apart, in the SWIZZLE_128B_ATOM_32B layout) instead of K-major.
+// raw_full (fused split only): the hi slots hold the raw f32 tiles as TMA
+// landed them, which the tf32 MMA reads as trunc(x) (low 13 bits ignored);
+// the hi.hi products are issued as soon as raw_full completes, overlapping
+// the lo computation, and the two cross products once full completes.
 template <bool B_MN = false>
 __device__ __forceinline__ void mma_issuer(uint8_t* smem, uint64_t* full, uint64_t* empty, uint64_t* sfull,
                                            uint64_t* sempty, uint32_t tmem_base, int num_tiles, int num_kb,
-                                           volatile int* abort_flag, unsigned int* err) {
+                                           volatile int* abort_flag, unsigned int* err,
+                                           uint64_t* raw_full = nullptr) {
   constexpr uint32_t idesc = jxd::idesc_tf32(BM, BN) | (B_MN ? (1u << 16) : 0u);
   int stage = 0;
   uint32_t phase = 0;
@@ -95,12 +100,43 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, uint64_t* full, uint64
       const uint32_t d_tmem = tmem_base + p * (uint32_t)BN;
       const int kb_end = min(kb0 + SPAN_KB, num_kb);
       for (int kb = kb0; kb < kb_end; ++kb) {
-        if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
-        jxd::tc_fence_after();
         const uint32_t sa_h = smem_base + stage * STAGE_BYTES;
         const uint32_t sa_l = sa_h + A_TILE;
         const uint32_t sb_h = sa_h + 2 * A_TILE;
         const uint32_t sb_l = sb_h + B_TILE;
+        if (raw_full) {
+          if (!wait_bounded(&raw_full[stage], phase, err)) { *abort_flag = 1; break; }
+          jxd::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + k * 32);
+            const uint64_t bh = B_MN ? jxd::smem_desc_mn_sw128_32b(sb_h + k * 1024, 32 * BK * 4)
+                                     : jxd::smem_desc_k_sw128(sb_h + k * 32);
+            jxd::mma_tf32(d_tmem, ah, bh, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
+          jxd::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t ah = jxd::smem_desc_k_sw128(sa_h + k * 32);
+            const uint64_t al = jxd::smem_desc_k_sw128(sa_l + k * 32);
+            uint64_t bh, bl;
+            if constexpr (B_MN) {
+              bh = jxd::smem_desc_mn_sw128_32b(sb_h + k * 1024, 32 * BK * 4);
+              bl = jxd::smem_desc_mn_sw128_32b(sb_l + k * 1024, 32 * BK * 4);
+            } else {
+              bh = jxd::smem_desc_k_sw128(sb_h + k * 32);
+              bl = jxd::smem_desc_k_sw128(sb_l + k * 32);
+            }
+            jxd::mma_tf32(d_tmem, al, bh, idesc, 1u);
+            jxd::mma_tf32(d_tmem, ah, bl, idesc, 1u);
+          }
+          jxd::mma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          continue;
+        }
+        if (!wait_bounded(&full[stage], phase, err)) { *abort_flag = 1; break; }
+        jxd::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < BK / 8; ++k) {
           const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
