@@ -686,7 +686,14 @@ def run_conv_bgemm(args, dist, jx, torch):
     if args.workload == "conv":
         e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X, Wt, G], [Y, DX, DW], step, args.e2e_steps)
     else:
-        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [A, Bm], [Cm], step, args.e2e_steps)
+        # through the host-buffer entry point: batch blocks stream up, multiply and down overlapped
+        hA, hB = A.cpu().pin_memory(), Bm.cpu().pin_memory()
+        hC = torch.empty(Cm.shape).pin_memory()
+
+        def host_step():
+            jx.call("jx_gemm_batched_f32_host", hA.data_ptr(), hB.data_ptr(), hC.data_ptr(), n, n, n, nb, 0, s)
+        e_ms = time_host_steps(torch, dist, st, host_step, args.e2e_steps)
+        e_in, e_out = 2 * hA.numel() * 4, hC.numel() * 4
     return {"metric": METRIC, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": wl,
@@ -765,7 +772,17 @@ def run_layers(args, dist, jx, torch):
     torch.cuda.synchronize()
     ms = dist.max(e0.elapsed_time(e1) / args.steps)
     clocks = clk.stop()
-    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, ins, outs, step, args.e2e_steps)
+    if args.workload == "pool":
+        hX = X.cpu().pin_memory()
+        hY = torch.empty(Y.shape).pin_memory()
+
+        def host_step():
+            jx.call("jx_pool2d_f32_host", hX.data_ptr(), hY.data_ptr(), B, C, H, H, 3, 3, 2, 2, 1, 1,
+                    jx.POOL_MAX, 0, s)
+        e_ms = time_host_steps(torch, dist, st, host_step, args.e2e_steps)
+        e_in, e_out = hX.numel() * 4, hY.numel() * 4
+    else:
+        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, ins, outs, step, args.e2e_steps)
     hbm, _, basis = load_peaks()
     if args.workload == "conv1d":
         val = work * dist.world / (ms * 1e-3) / 1e12
@@ -797,6 +814,22 @@ def run_layers(args, dist, jx, torch):
             "e2e": {"value": round(e2e, 2), "unit": unit, "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out,
                     "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps * launches, "clocks": clocks}
+
+
+def time_host_steps(torch, dist, st, host_step, steps):
+    """ms per call of a host-buffer entry point (copies inside), CUDA events on
+    the caller's stream (which waits for the call's last download), max over
+    ranks."""
+    host_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        host_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return dist.max(e0.elapsed_time(e1) / steps)
 
 
 def run_fft(args, dist, jx, torch):

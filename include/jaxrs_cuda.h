@@ -108,6 +108,22 @@ JX_API int jx_gemm_split_f32(const float *src, float *hi, float *lo, int64_t row
 JX_API int jx_gemm_presplit_f32(const float *Ah, const float *Al, const float *Bh, const float *Bl, float *C,
                                 int64_t M, int64_t N, int64_t Kp, int64_t ldc, int64_t batch, int64_t strideC,
                                 jx_stream_t stream);
+/* No counterpart in the reference (its readback is one blocking copy,
+ * src/buffer.rs:711-749).  C = A . B (3xTF32) with A, B and C in host memory
+ * (pinned for overlap), untransposed: B is uploaded and split once, then row
+ * blocks of block_rows rows (0: about M/8) of A stream through the device
+ * while the product of the previous block runs and the block before that
+ * downloads, on three streams.  The caller's stream waits for the last
+ * download. */
+JX_API int jx_gemm_f32_host(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int64_t ldc, int64_t block_rows, jx_stream_t stream);
+/* Batched counterpart over host buffers (einsum "bij,bjk->bik" on host
+ * arrays, src/ops/einsum.rs:488-523): A [batch][M][K], B [batch][K][N],
+ * C [batch][M][N], contiguous; blocks of block_items entries (0: about 96 MiB
+ * of operands) stream through the device, uploads, the batched 3xTF32
+ * product and downloads overlapping on three streams. */
+JX_API int jx_gemm_batched_f32_host(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
+                                    int64_t batch, int64_t block_items, jx_stream_t stream);
 /* No counterpart in the reference.  jx_gemm_f32 (JX_PREC_3XTF32) for callers
  * that cannot let a library allocate device memory: a process whose own arena
  * or caching allocator already owns the device's memory, a latency-critical
@@ -119,15 +135,6 @@ JX_API int jx_gemm_presplit_f32(const float *Ah, const float *Al, const float *B
  * call on each device looks up the array's address (cudaGetSymbolAddress), so
  * make that first call before any stream capture.  All calls share the array:
  * calls that overlap on the GPU race and must be serialised by the caller. */
-/* No counterpart in the reference (its readback is one blocking copy,
- * src/buffer.rs:711-749).  C = A . B (3xTF32) with A, B and C in host memory
- * (pinned for overlap), untransposed: B is uploaded and split once, then row
- * blocks of block_rows rows (0: about M/8) of A stream through the device
- * while the product of the previous block runs and the block before that
- * downloads, on three streams.  The caller's stream waits for the last
- * download. */
-JX_API int jx_gemm_f32_host(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                            int64_t ldb, int64_t ldc, int64_t block_rows, jx_stream_t stream);
 JX_API int jx_gemm_f32_noalloc(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
                                int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                                int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream);
@@ -362,6 +369,13 @@ JX_API int jx_conv1d_f32(const float *x, const float *w, float *y, int64_t batch
 JX_API int jx_pool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,
                          int64_t input_w, int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w,
                          int64_t pad_h, int64_t pad_w, int op, jx_stream_t stream);
+/* jx_pool2d_f32 over host buffers: blocks of block_items images (0: about
+ * 32 MiB of input) stream through the device, uploads, pooling and downloads
+ * overlapping on three streams; the caller's stream waits for the last
+ * download. */
+JX_API int jx_pool2d_f32_host(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,
+                              int64_t input_w, int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w,
+                              int64_t pad_h, int64_t pad_w, int op, int64_t block_items, jx_stream_t stream);
 /* gpu_maxpool2d / gpu_avgpool2d (src/backend/ops.rs:1204-1215,1359-1370): one
  * stride and one padding for both axes. */
 JX_API int jx_maxpool2d_f32(const float *x, float *y, int64_t batch, int64_t channels, int64_t input_h,

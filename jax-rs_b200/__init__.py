@@ -66,6 +66,8 @@ _SIGS = {
     "jx_host_unregister": [vp],
     "jx_conv1d_f32": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, vp],
     "jx_pool2d_f32": [vp, vp] + [i64] * 10 + [ci, vp],
+    "jx_pool2d_f32_host": [vp, vp] + [i64] * 10 + [ci, i64, vp],
+    "jx_gemm_batched_f32_host": [vp, vp, vp, i64, i64, i64, i64, i64, vp],
     "jx_maxpool2d_f32": [vp, vp] + [i64] * 8 + [vp],
     "jx_avgpool2d_f32": [vp, vp] + [i64] * 8 + [vp],
     "jx_global_pool2d_f32": [vp, vp, i64, i64, i64, i64, ci, vp],

@@ -289,4 +289,85 @@ int jx_fft2_c2c_f32_host(const float* in, float* out, int64_t h, int64_t w, int6
   return fft_host(in, out, h * w, batch, block_items, true, h, w, inverse, stream);
 }
 
+int jx_gemm_batched_f32_host(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                             int64_t batch, int64_t block_items, jx_stream_t stream) {
+  JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
+  if (M == 0 || N == 0 || batch == 0) return JX_OK;
+  JX_REQUIRE(K > 0, "gemm host: K must be positive");
+  JX_REQUIRE(A && B && C, "matmul: NULL operand");
+  cudaStream_t caller = jx::as_stream(stream);
+  Streams* s = nullptr;
+  int rc = streams(&s);
+  if (rc) return rc;
+  Events ev;
+  if ((rc = ev.create())) return rc;
+  const long long fa = M * K, fb = K * N, fc = M * N, per = fa + fb + fc;  // floats per batch entry
+  long long blk = block_items > 0 ? block_items : std::max(1LL, (96LL << 20) / (per * 4));
+  blk = std::min(blk, (long long)batch);
+  const long long nblk = (batch + blk - 1) / blk;
+  void* ws = nullptr;
+  if ((rc = jx::scratch_get(sizeof(float) * (size_t)(NBUF * blk * per), &ws, caller))) return rc;
+  auto slot = [&](int b) { return reinterpret_cast<float*>(ws) + (size_t)b * blk * per; };
+  auto count = [&](long long i) { return std::min(blk, (long long)batch - i * blk); };
+  rc = pipeline(
+      nblk, s, ev, caller, nullptr,
+      [&](long long i, int b, cudaStream_t st) {
+        int r = copy_up(slot(b), A + i * blk * fa, sizeof(float) * count(i) * fa, st);
+        if (!r) r = copy_up(slot(b) + blk * fa, B + i * blk * fb, sizeof(float) * count(i) * fb, st);
+        return r;
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        float* a = slot(b);
+        float* bb = a + blk * fa;
+        float* c = bb + blk * fb;
+        return jx_gemm_f32(a, bb, c, M, N, K, 0, 0, K, N, N, count(i), fa, fb, fc, JX_PREC_3XTF32, st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        return copy_down(C + i * blk * fc, slot(b) + blk * (fa + fb), sizeof(float) * count(i) * fc, st);
+      });
+  const int rc2 = jx::scratch_release(ws, caller);
+  return rc ? rc : rc2;
+}
+
+int jx_pool2d_f32_host(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
+                       int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                       int64_t pad_w, int op, int64_t block_items, jx_stream_t stream) {
+  // geometry checks (and their messages) are jx_pool2d_f32's: run them once on an empty batch
+  if (int rc = jx_pool2d_f32(nullptr, nullptr, 0, channels, input_h, input_w, pool_h, pool_w, stride_h, stride_w,
+                             pad_h, pad_w, op, stream))
+    return rc;
+  JX_REQUIRE(batch >= 0, "jx_pool2d_f32_host: negative batch");
+  if (batch == 0 || channels == 0) return JX_OK;
+  JX_REQUIRE(x && y, "jx_pool2d_f32_host: NULL buffer");
+  cudaStream_t caller = jx::as_stream(stream);
+  Streams* s = nullptr;
+  int rc = streams(&s);
+  if (rc) return rc;
+  Events ev;
+  if ((rc = ev.create())) return rc;
+  const long long oh = (input_h + 2 * pad_h - pool_h) / stride_h + 1, ow = (input_w + 2 * pad_w - pool_w) / stride_w + 1;
+  const long long fi = channels * input_h * input_w, fo = channels * oh * ow;  // floats per image
+  long long blk = block_items > 0 ? block_items : std::max(1LL, (32LL << 20) / (fi * 4));
+  blk = std::min(blk, (long long)batch);
+  const long long nblk = (batch + blk - 1) / blk;
+  void* ws = nullptr;
+  if ((rc = jx::scratch_get(sizeof(float) * (size_t)(NBUF * blk * (fi + fo)), &ws, caller))) return rc;
+  auto slot = [&](int b) { return reinterpret_cast<float*>(ws) + (size_t)b * blk * (fi + fo); };
+  auto count = [&](long long i) { return std::min(blk, (long long)batch - i * blk); };
+  rc = pipeline(
+      nblk, s, ev, caller, nullptr,
+      [&](long long i, int b, cudaStream_t st) {
+        return copy_up(slot(b), x + i * blk * fi, sizeof(float) * count(i) * fi, st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        return jx_pool2d_f32(slot(b), slot(b) + blk * fi, count(i), channels, input_h, input_w, pool_h, pool_w,
+                             stride_h, stride_w, pad_h, pad_w, op, st);
+      },
+      [&](long long i, int b, cudaStream_t st) {
+        return copy_down(y + i * blk * fo, slot(b) + blk * fi, sizeof(float) * count(i) * fo, st);
+      });
+  const int rc2 = jx::scratch_release(ws, caller);
+  return rc ? rc : rc2;
+}
+
 }  // extern "C"

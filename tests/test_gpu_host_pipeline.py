@@ -94,3 +94,30 @@ def test_registered_host_memory(jx, dev, oracle):
         jx.call("jx_host_unregister", x.ctypes.data)
         jx.call("jx_host_unregister", y.ctypes.data)
     assert _close(y, oracle.chain_fwd(x, np.float32(1.1), np.float32(0.9)))
+
+
+@pytest.mark.parametrize("M,N,K,batch,block", [(64, 96, 40, 5, 2), (256, 256, 300, 3, 0), (33, 17, 9, 7, 3)])
+def test_batched_gemm_host_matches_oracle(jx, dev, oracle, M, N, K, batch, block):
+    rng = np.random.default_rng(M + batch)
+    a = rng.uniform(-1, 1, (batch, M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (batch, K, N)).astype(np.float32)
+    c = np.full((batch, M, N), np.nan, np.float32)
+    jx.call("jx_gemm_batched_f32_host", a.ctypes.data, b.ctypes.data, c.ctypes.data, M, N, K, batch, block,
+            dev.stream)
+    dev.sync()
+    for i in range(batch):
+        assert normwise_rel(c[i], oracle.matmul(a[i], b[i])) <= 1e-5
+
+
+@pytest.mark.parametrize("is_max", [True, False])
+def test_pool_host_matches_device_call(jx, dev, is_max):
+    x = np.random.default_rng(4).standard_normal((7, 3, 21, 19)).astype(np.float32)
+    geo = (7, 3, 21, 19, 3, 3, 2, 2, 1, 1)
+    op = jx.POOL_MAX if is_max else jx.POOL_AVG
+    y = np.full((7, 3, 11, 10), np.nan, np.float32)
+    jx.call("jx_pool2d_f32_host", x.ctypes.data, y.ctypes.data, *geo, op, 2, dev.stream)
+    dev.sync()
+    X = dev.put(x)
+    Y = dev.full(y.shape, np.nan)
+    jx.call("jx_pool2d_f32", X.data_ptr(), Y.data_ptr(), *geo, op, dev.stream)
+    assert np.array_equal(y, dev.get(Y))  # same kernel, same bits
