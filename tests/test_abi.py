@@ -136,3 +136,25 @@ def test_layer_argument_checks(jx):
     # empty batches are no-ops
     jx.call("jx_conv1d_f32", None, None, None, 0, 1, 4, 8, 3, 1, 0, None)
     jx.call("jx_pool2d_f32", None, None, 0, 3, 4, 4, 2, 2, 2, 2, 0, 0, jx.POOL_AVG, None)
+
+
+def test_rust_ffi_block_matches_header():
+    """INTEGRATION.md's Rust extern block is the generator's output for the
+    current header, and it declares every JX_API function exactly once."""
+    import importlib.util
+    import os
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("rust_ffi", os.path.join(root, "jax-rs_b200", "rust_ffi.py"))
+    rf = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rf)
+    block = rf.rust_block()
+    with open(os.path.join(root, "INTEGRATION.md")) as f:
+        doc = f.read()
+    m = re.search(r"<!-- rust-ffi:begin -->\n```rust\n(.*?)```\n<!-- rust-ffi:end -->", doc, flags=re.S)
+    assert m, "INTEGRATION.md lacks the generated Rust block"
+    assert m.group(1) == block, "regenerate with: python jax-rs_b200/rust_ffi.py"
+    with open(os.path.join(root, "include", "jaxrs_cuda.h")) as f:
+        header_names = set(re.findall(r"JX_API[^;(]*\b(jx_\w+)\s*\(", f.read()))
+    rust_names = re.findall(r"pub fn (jx_\w+)\(", block)
+    assert len(rust_names) == len(set(rust_names)) and set(rust_names) == header_names
