@@ -414,36 +414,73 @@ __global__ void split_transpose_kernel(const float* __restrict__ src, float* __r
 // Exact path: the reference loop's rounding sequence (src/ops/linalg.rs:220-228):
 // sum = 0; for p in 0..k { sum = sum + a*b } with each product and sum rounded.
 // ---------------------------------------------------------------------------
-__global__ void gemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                  float* __restrict__ C, int M, int N, int K, int transA, int transB,
-                                  long long lda, long long ldb, long long ldc, long long sA, long long sB,
-                                  long long sC) {
-  __shared__ float As[16][17];
-  __shared__ float Bs[16][17];
+// One thread per output of a 16 x 16 tile.  K streams through shared memory
+// in chunks of EX_KC: the next chunk is loaded into registers while the
+// current one is summed, so each chunk costs one barrier and its loads are in
+// flight behind EX_KC dependent additions (K = 784 takes 7 round trips to L2,
+// not 49).  Every output still sums its products in ascending k from 0.
+constexpr int EX_T = 16, EX_KC = 128, EX_PER = EX_T * EX_KC / (EX_T * EX_T);  // 8 loads per operand
+
+__global__ void __launch_bounds__(EX_T* EX_T)
+    gemm_exact_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
+                      int K, int transA, int transB, long long lda, long long ldb, long long ldc, long long sA,
+                      long long sB, long long sC) {
+  __shared__ float As[2][EX_T][EX_KC + 1];  // [row][k]
+  __shared__ float Bs[2][EX_KC][EX_T + 1];  // [k][col]
   const int b = blockIdx.z;
   const float* a = A + (long long)b * sA;
   const float* bb = B + (long long)b * sB;
-  const int row = blockIdx.y * 16 + threadIdx.y;
-  const int col = blockIdx.x * 16 + threadIdx.x;
+  const int tid = threadIdx.y * EX_T + threadIdx.x;
+  const int r0 = blockIdx.y * EX_T, c0 = blockIdx.x * EX_T;
+  // Element e of this thread's share of a chunk: (tile row or column, k within
+  // the chunk), arranged so that consecutive threads read consecutive
+  // addresses of the operand as stored.
+  auto a_at = [&](int e, int& r, int& k) {
+    if (transA) { r = tid & (EX_T - 1); k = (tid >> 4) + 16 * e; }    // a[k][r]: r fastest
+    else { k = tid & (EX_KC - 1); r = (tid >> 7) + 2 * e; }           // a[r][k]: k fastest
+  };
+  auto b_at = [&](int e, int& k, int& c) {
+    if (transB) { k = tid & (EX_KC - 1); c = (tid >> 7) + 2 * e; }    // b[c][k]: k fastest
+    else { c = tid & (EX_T - 1); k = (tid >> 4) + 16 * e; }           // b[k][c]: c fastest
+  };
+  float ra[EX_PER], rb[EX_PER];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int e = 0; e < EX_PER; ++e) {
+      int r, k, c, kb;
+      a_at(e, r, k);
+      const int gr = r0 + r, gk = k0 + k;
+      ra[e] = (gr < M && gk < K) ? (transA ? a[(long long)gk * lda + gr] : a[(long long)gr * lda + gk]) : 0.0f;
+      b_at(e, kb, c);
+      const int gkb = k0 + kb, gc = c0 + c;
+      rb[e] = (gkb < K && gc < N) ? (transB ? bb[(long long)gc * ldb + gkb] : bb[(long long)gkb * ldb + gc]) : 0.0f;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int e = 0; e < EX_PER; ++e) {
+      int r, k, c, kb;
+      a_at(e, r, k);
+      As[buf][r][k] = ra[e];
+      b_at(e, kb, c);
+      Bs[buf][kb][c] = rb[e];
+    }
+  };
+  const int nchunk = (K + EX_KC - 1) / EX_KC;
+  load(0);
+  store(0);
+  __syncthreads();
   float sum = 0.0f;
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    {
-      const int r = blockIdx.y * 16 + threadIdx.y, k = k0 + threadIdx.x;
-      float v = 0.0f;
-      if (r < M && k < K) v = transA ? a[(long long)k * lda + r] : a[(long long)r * lda + k];
-      As[threadIdx.y][threadIdx.x] = v;
-    }
-    {
-      const int k = k0 + threadIdx.y, c = blockIdx.x * 16 + threadIdx.x;
-      float v = 0.0f;
-      if (k < K && c < N) v = transB ? bb[(long long)c * ldb + k] : bb[(long long)k * ldb + c];
-      Bs[threadIdx.y][threadIdx.x] = v;
-    }
-    __syncthreads();
-    const int kmax = min(16, K - k0);
-    for (int kk = 0; kk < kmax; ++kk) sum = __fadd_rn(sum, __fmul_rn(As[threadIdx.y][kk], Bs[kk][threadIdx.x]));
+  for (int ch = 0; ch < nchunk; ++ch) {
+    const int buf = ch & 1;
+    if (ch + 1 < nchunk) load((ch + 1) * EX_KC);
+    const int kmax = min(EX_KC, K - ch * EX_KC);
+    for (int kk = 0; kk < kmax; ++kk)
+      sum = __fadd_rn(sum, __fmul_rn(As[buf][threadIdx.y][kk], Bs[buf][kk][threadIdx.x]));
+    if (ch + 1 < nchunk) store(buf ^ 1);
     __syncthreads();
   }
+  const int row = r0 + threadIdx.y, col = c0 + threadIdx.x;
   if (row < M && col < N) C[(long long)b * sC + (long long)row * ldc + col] = sum;
 }
 
