@@ -1056,13 +1056,15 @@ def run_mlp(args, dist, jx, torch):
                      "achieved": round(flops / (ms * 1e-3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)", "traffic": None,
-                     "note": ("one-tile products on the sequential-k f32 kernel; the step is bound by its "
-                              f"{mlp_launches(widths, batch, True)} launches, the tensor peak is quoted for scale")
+                     "note": ("exact f32 (sequential-k, unfused): the whole step is one cooperative kernel "
+                              "with grid barriers between its phases; the tensor peak is quoted for scale")
                      if prec == jx.PREC_EXACT else ""},
         "e2e": {"value": round(samples / (e2e_ms * 1e-3), 1), "unit": "samples/s",
                 "h2d_bytes_per_step": (hx.numel() + hy.numel()) * 4, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps * mlp_launches(widths, batch, prec == jx.PREC_EXACT),
+        # exact precision on one GPU: the whole step is one cooperative kernel
+        "gpu_launches": args.steps * (1 if prec == jx.PREC_EXACT and comm is None
+                                      else mlp_launches(widths, batch, prec == jx.PREC_EXACT)),
         "clocks": clocks,
     }
     if comm is not None:

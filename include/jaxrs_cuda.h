@@ -451,6 +451,11 @@ JX_API int jx_mlp_attach_comm(jx_mlp *mlp, void *comm, int world, int64_t global
  * labels [batch] are device pointers; loss_out (device scalar) may be NULL. */
 JX_API int jx_mlp_train_step(jx_mlp *mlp, const float *x, const float *labels, float *loss_out,
                              jx_stream_t stream);
+/* With JX_PREC_EXACT and no communicator, a step runs as one cooperative
+ * kernel (forward, loss, backward, Adam, grid barriers between phases; the
+ * same arithmetic as the separate kernels, bit-identical).  enable = 0 selects
+ * the captured graph of separate kernels instead.  On by default. */
+JX_API int jx_mlp_set_fused(jx_mlp *mlp, int enable);
 JX_API int jx_mlp_destroy(jx_mlp *mlp);
 
 /* ---- data-parallel collectives (no reference counterpart: the reference has

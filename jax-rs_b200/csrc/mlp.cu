@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "jx_common.cuh"
+#include "nn_common.cuh"
 
 namespace jx {
 int col_sum(const float* dy, float* db, long long rows, int cols, cudaStream_t st);
@@ -55,6 +56,338 @@ __global__ void adam_flat_kernel(float* __restrict__ p, const float* __restrict_
 
 __global__ void step_inc_kernel(int* step) { *step += 1; }
 
+// ---------------------------------------------------------------------------
+// Fused step (JX_PREC_EXACT, one GPU): forward, softmax cross-entropy,
+// backward and Adam in one cooperative launch instead of ~23 kernels.  Phases
+// are separated by a grid barrier (2L+1 of them); inside a phase every block
+// takes work items in a grid-stride loop.  The arithmetic is the separate
+// kernels' own: the exact GEMM's ascending-k unfused sums (one thread per
+// output of a 16 x 16 tile, K through a cp.async ring of 128-wide chunks),
+// bias + activation, jxn::softmax_xent_row, the column sums' sequential row
+// order, the activation derivative and Adam, so the results are bit-identical
+// to the captured-graph path.  Data written inside the launch is read back
+// through L2 (ld.global.cg): an SM's L1 may still hold the previous contents
+// of a buffer that another SM rewrote.
+// ---------------------------------------------------------------------------
+constexpr int FS_MAXL = 8, FS_THREADS = 256, FS_T = 16, FS_KC = 128;
+
+struct FusedStep {
+  int L, B;
+  int w[FS_MAXL + 1];
+  int act[FS_MAXL];
+  long long woff[FS_MAXL], boff[FS_MAXL];
+  const float* x;
+  const float* labels;
+  float *params, *grads, *m, *v;
+  float* h[FS_MAXL + 1];
+  float* pre[FS_MAXL + 1];
+  float *dzA, *dzB, *row_loss, *loss, *loss_out;
+  int* step;
+  const float2* tab;
+  float lr, b1, b2, eps, omb1, omb2, count;
+  long long nparams;
+  unsigned* bar;   // two launch slots of barrier arrivals
+  int slot;        // this launch's slot; it zeroes the other one for the next launch
+  unsigned* err;
+};
+
+__device__ __forceinline__ unsigned long long fs_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Grid barrier number `index` (0-based) of this launch: every block adds one
+// arrival and waits until all gridDim.x * (index + 1) have arrived.  The wait
+// gives up after 2 s, records JX_DEVERR_TIMEOUT and returns false.
+__device__ bool fs_grid_sync(unsigned* cnt, unsigned index, unsigned* err, int* ok_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned target = gridDim.x * (index + 1);
+    __threadfence();
+    atomicAdd(cnt, 1u);
+    bool ok = true;
+    const unsigned long long t0 = fs_ns();
+    while (*reinterpret_cast<volatile unsigned*>(cnt) < target) {
+      if (fs_ns() - t0 > 2000000000ull) {
+        atomicOr(err, JX_DEVERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+    __threadfence();
+    *ok_flag = ok;
+  }
+  __syncthreads();
+  return *ok_flag;
+}
+
+constexpr int FS_NS = 4;  // cp.async stages of FS_KC k-values in flight per tile
+
+// Shared-memory stage of one operand, kept in the orientation it has in
+// global memory so that cp.async can move 16 bytes at a time: k-major rows
+// [16][FS_KC + 4] when k is contiguous, else [FS_KC][16 + 4].
+constexpr int FS_KP = FS_KC + 4, FS_MP = FS_T + 4;
+constexpr int FS_OPF = FS_KC * FS_MP;  // floats per operand stage (the larger layout)
+static_assert(FS_T * FS_KP <= FS_OPF, "stage size");
+struct FsSmem {
+  float A[FS_NS][FS_OPF];
+  float B[FS_NS][FS_OPF];
+  float red[32];
+  int ok;
+};
+
+__device__ __forceinline__ void fs_cp4(float* dst, const float* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(jxd::smem_u32(dst)), "l"(src),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void fs_cp16(float* dst, const float* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(jxd::smem_u32(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void fs_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void fs_cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Copies one operand's chunk (FS_T rows/cols of the tile x FS_KC k-values
+// starting at k0) into a stage.  KMAJ: k contiguous in global memory (the
+// stage is [FS_T][FS_KP]); else the tile's 16 rows/cols are contiguous (the
+// stage is [FS_KC][FS_MP]).  x0: the tile's first row/col, X: rows/cols in the
+// matrix, ld: its row stride.  vec: 16-byte copies allowed (ld and the base
+// 16-byte aligned); zero-filled outside the matrix either way.
+template <bool KMAJ>
+__device__ __forceinline__ void fs_load_op(float* stage, const float* __restrict__ g, int x0, int X, int k0, int K,
+                                           int ld, bool vec) {
+  const int tid = threadIdx.x;
+  if (vec) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {  // 512 16-byte pieces per chunk
+      const int idx = tid + 256 * e;
+      if (KMAJ) {
+        const int x = idx >> 5, kk = (idx & 31) * 4;
+        const int gx = x0 + x, gk = k0 + kk;
+        const int bytes = gx < X ? max(0, min(16, (K - gk) * 4)) : 0;
+        fs_cp16(stage + x * FS_KP + kk, bytes ? g + (long long)gx * ld + gk : g, bytes);
+      } else {
+        const int kk = idx >> 2, x = (idx & 3) * 4;
+        const int gx = x0 + x, gk = k0 + kk;
+        const int bytes = gk < K ? max(0, min(16, (X - gx) * 4)) : 0;
+        fs_cp16(stage + kk * FS_MP + x, bytes ? g + (long long)gk * ld + gx : g, bytes);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {  // 2048 single floats, consecutive threads on consecutive addresses
+      const int idx = tid + 256 * e;
+      if (KMAJ) {
+        const int x = idx >> 7, kk = idx & 127;
+        const int gx = x0 + x, gk = k0 + kk;
+        const bool v = gx < X && gk < K;
+        fs_cp4(stage + x * FS_KP + kk, v ? g + (long long)gx * ld + gk : g, v);
+      } else {
+        const int kk = idx >> 4, x = idx & 15;
+        const int gx = x0 + x, gk = k0 + kk;
+        const bool v = gk < K && gx < X;
+        fs_cp4(stage + kk * FS_MP + x, v ? g + (long long)gk * ld + gx : g, v);
+      }
+    }
+  }
+}
+
+// Four consecutive k-values of row/col x of a stage.
+template <bool KMAJ>
+__device__ __forceinline__ float4 fs_get4(const float* stage, int x, int kk) {
+  if (KMAJ) return *reinterpret_cast<const float4*>(stage + x * FS_KP + kk);
+  return make_float4(stage[kk * FS_MP + x], stage[(kk + 1) * FS_MP + x], stage[(kk + 2) * FS_MP + x],
+                     stage[(kk + 3) * FS_MP + x]);
+}
+template <bool KMAJ>
+__device__ __forceinline__ float fs_get1(const float* stage, int x, int kk) {
+  return KMAJ ? stage[x * FS_KP + kk] : stage[kk * FS_MP + x];
+}
+
+__device__ __forceinline__ bool fs_vec_ok(const float* p, int ld) {
+  return (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+// One 16 x 16 tile of C = op(A) . op(B) (M x N, K deep); epi(row, col, sum)
+// for the in-range outputs.  TA / TB: A / B transposed in memory (A is then
+// [K][M], B [N][K]).  K streams through a ring of FS_NS shared-memory stages
+// filled by cp.async, FS_NS - 1 chunks ahead of the sums.  colsum (or null):
+// the tile's first row of threads also sums B's columns over k in order --
+// the column sums of the separate kernels (256-row chunk sums added in chunk
+// order) -- for the tiles of the first row of C.
+template <bool TA, bool TB, class Epi>
+__device__ void fs_tile(FsSmem& sm, int tile, const float* __restrict__ a, const float* __restrict__ b, int M, int N,
+                        int K, int lda, int ldb, Epi epi, float* colsum = nullptr) {
+  constexpr bool AK = !TA, BK = TB;  // k contiguous in the stage
+  const int tiles_n = (N + FS_T - 1) / FS_T;
+  const int r0 = (tile / tiles_n) * FS_T, c0 = (tile % tiles_n) * FS_T;
+  const int tid = threadIdx.x, tx = tid & (FS_T - 1), ty = tid >> 4;
+  const bool va = fs_vec_ok(a, lda), vb = fs_vec_ok(b, ldb);
+  auto issue = [&](int ch) {
+    const int st = ch % FS_NS, k0 = ch * FS_KC;
+    fs_load_op<AK>(sm.A[st], a, r0, M, k0, K, lda, va);
+    fs_load_op<BK>(sm.B[st], b, c0, N, k0, K, ldb, vb);
+  };
+  const int nchunk = (K + FS_KC - 1) / FS_KC;
+#pragma unroll
+  for (int c = 0; c < FS_NS - 1; ++c) {
+    if (c < nchunk) issue(c);
+    fs_cp_commit();
+  }
+  const bool do_cs = colsum && r0 == 0 && ty == 0;
+  float sum = 0.0f, cs_acc = 0.0f, cs_tot = 0.0f;
+  for (int ch = 0; ch < nchunk; ++ch) {
+    fs_cp_wait<FS_NS - 2>();  // this thread's copies of chunk ch have landed
+    __syncthreads();          // everyone's; stage (ch - 1) % FS_NS is free again
+    if (ch + FS_NS - 1 < nchunk) issue(ch + FS_NS - 1);
+    fs_cp_commit();
+    const float* As = sm.A[ch % FS_NS];
+    const float* Bs = sm.B[ch % FS_NS];
+    const int kmax = min(FS_KC, K - ch * FS_KC);
+    const int k4 = kmax & ~3;
+    // several 4-value reads in flight ahead of the dependent adds; the
+    // products are still added one by one in ascending k
+#pragma unroll 4
+    for (int kk = 0; kk < k4; kk += 4) {
+      const float4 av = fs_get4<AK>(As, ty, kk);
+      const float4 bv = fs_get4<BK>(Bs, tx, kk);
+      sum = __fadd_rn(sum, __fmul_rn(av.x, bv.x));
+      sum = __fadd_rn(sum, __fmul_rn(av.y, bv.y));
+      sum = __fadd_rn(sum, __fmul_rn(av.z, bv.z));
+      sum = __fadd_rn(sum, __fmul_rn(av.w, bv.w));
+    }
+    for (int kk = k4; kk < kmax; ++kk) sum = __fadd_rn(sum, __fmul_rn(fs_get1<AK>(As, ty, kk), fs_get1<BK>(Bs, tx, kk)));
+    if (do_cs) {
+      if (ch > 0 && (ch * FS_KC) % 256 == 0) {
+        cs_tot += cs_acc;
+        cs_acc = 0.0f;
+      }
+      for (int kk = 0; kk < kmax; ++kk) cs_acc += fs_get1<BK>(Bs, tx, kk);
+    }
+  }
+  fs_cp_wait<0>();
+  __syncthreads();  // the ring is free for the next tile
+  if (do_cs && c0 + tx < N) {
+    cs_tot += cs_acc;
+    colsum[c0 + tx] = cs_tot;
+  }
+  const int row = r0 + ty, col = c0 + tx;
+  if (row < M && col < N) epi(row, col, sum);
+}
+
+__global__ void __launch_bounds__(FS_THREADS, 2) mlp_fused_step_kernel(FusedStep a) {
+  extern __shared__ __align__(16) unsigned char fs_raw[];
+  FsSmem& sm = *reinterpret_cast<FsSmem*>(fs_raw);
+  const int t = *a.step;  // read before the first barrier; block 0 writes t + 1 at the end
+  unsigned* cnt = a.bar + a.slot;
+  if (blockIdx.x == 0 && threadIdx.x == 0) a.bar[a.slot ^ 1] = 0u;
+  unsigned nbar = 0;
+  const int lane = threadIdx.x & 31;
+  const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x, gthreads = (long long)gridDim.x * blockDim.x;
+  const int B = a.B;
+
+  // ---- forward: h_l = act(h_{l-1} W_l + b_l) ----
+  for (int l = 1; l <= a.L; ++l) {
+    const int K = a.w[l - 1], N = a.w[l];
+    const float* in = l == 1 ? a.x : a.h[l - 1];
+    const float* W = a.params + a.woff[l - 1];
+    const float* bias = a.params + a.boff[l - 1];
+    float* out = a.h[l];
+    float* pre = l < a.L ? a.pre[l] : nullptr;
+    const int act = l < a.L ? a.act[l - 1] : 0;
+    const int tiles = ((B + FS_T - 1) / FS_T) * ((N + FS_T - 1) / FS_T);
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x)
+      fs_tile<false, false>(sm, tile, in, W, B, N, K, K, N, [&](int r, int c, float sum) {
+        const float v = __fadd_rn(sum, __ldcg(bias + c));
+        if (pre) pre[(long long)r * N + c] = v;
+        out[(long long)r * N + c] = jxn::act_apply(act, v);
+      });
+    if (!fs_grid_sync(cnt, nbar++, a.err, &sm.ok)) return;
+  }
+
+  // ---- softmax cross-entropy: dz = dL/dlogits, per-row losses ----
+  const int C = a.w[a.L];
+  for (long long r = gtid >> 5; r < B; r += gthreads >> 5) {
+    const float lr = jxn::softmax_xent_row(a.h[a.L] + r * C, __ldcg(a.labels + r), C, a.count, nullptr,
+                                           a.dzA + r * C, lane);
+    if (lane == 0) a.row_loss[r] = lr;
+  }
+  if (!fs_grid_sync(cnt, nbar++, a.err, &sm.ok)) return;
+
+  // loss = sum of row losses / count, in the order of the 1024-thread
+  // reduction the separate kernels use (block 0, overlapping the backward)
+  if (blockIdx.x == 0) {
+    const int wid = threadIdx.x >> 5;
+    for (int w = wid; w < 32; w += FS_THREADS / 32) {
+      float acc = 0.0f;
+      for (long long i = w * 32 + lane; i < B; i += 1024) acc += __ldcg(a.row_loss + i);
+      acc = jxn::warp_sum(acc);
+      if (lane == 0) sm.red[w] = acc;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      float acc = sm.red[lane];
+      acc = jxn::warp_sum(acc);
+      if (lane == 0) {
+        const float loss = __fdiv_rn(acc, a.count);
+        *a.loss = loss;
+        if (a.loss_out) *a.loss_out = loss;
+      }
+    }
+  }
+
+  // ---- backward: dW_l = h_{l-1}^T dz, db_l = column sums of dz,
+  //      dz_{l-1} = (dz W_l^T) * act'(pre_{l-1}) ----
+  float* dz = a.dzA;
+  float* dzn = a.dzB;
+  for (int l = a.L; l >= 1; --l) {
+    const int K = a.w[l - 1], N = a.w[l];
+    const float* hin = l == 1 ? a.x : a.h[l - 1];
+    const float* W = a.params + a.woff[l - 1];
+    float* gW = a.grads + a.woff[l - 1];
+    float* gb = a.grads + a.boff[l - 1];
+    const int tiles_w = ((K + FS_T - 1) / FS_T) * ((N + FS_T - 1) / FS_T);
+    const int tiles_h = l > 1 ? ((B + FS_T - 1) / FS_T) * ((K + FS_T - 1) / FS_T) : 0;
+    for (int tile = blockIdx.x; tile < tiles_w + tiles_h; tile += gridDim.x) {
+      if (tile < tiles_w) {
+        fs_tile<true, false>(
+            sm, tile, hin, dz, K, N, B, K, N, [&](int r, int c, float sum) { gW[(long long)r * N + c] = sum; }, gb);
+      } else {
+        const float* pre = a.pre[l - 1];
+        const int act = a.act[l - 2];
+        fs_tile<false, true>(sm, tile - tiles_w, dz, W, B, K, N, N, N, [&](int r, int c, float sum) {
+          dzn[(long long)r * K + c] = __fmul_rn(sum, jxn::act_grad_rt(act, __ldcg(pre + (long long)r * K + c)));
+        });
+      }
+    }
+    if (!fs_grid_sync(cnt, nbar++, a.err, &sm.ok)) return;
+    float* tmp = dz;
+    dz = dzn;
+    dzn = tmp;
+  }
+
+  // ---- Adam over every parameter ----
+  const float2 rr = a.tab[t - 1];
+  const bool first = t == 1;
+  for (long long i = gtid; i < a.nparams; i += gthreads) {
+    const float gi = __ldcg(a.grads + i);
+    const float mi = first ? __fmul_rn(gi, a.omb1) : __fadd_rn(__fmul_rn(a.m[i], a.b1), __fmul_rn(gi, a.omb1));
+    const float g2 = __fmul_rn(gi, gi);
+    const float vi = first ? __fmul_rn(g2, a.omb2) : __fadd_rn(__fmul_rn(a.v[i], a.b2), __fmul_rn(g2, a.omb2));
+    const float mh = __fmul_rn(mi, rr.x);
+    const float vh = __fmul_rn(vi, rr.y);
+    a.params[i] = __fsub_rn(a.params[i], __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), a.eps)), a.lr));
+    a.m[i] = mi;
+    a.v[i] = vi;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *a.step = t + 1;
+}
+
 }  // namespace
 
 struct jx_mlp {
@@ -78,6 +411,12 @@ struct jx_mlp {
   std::vector<cudaEvent_t> ev;
   cudaGraphExec_t gexec = nullptr;
   long long steps = 0;
+  // fused step (exact precision, one GPU)
+  bool fused = true;
+  unsigned* bar = nullptr;     // two slots of grid-barrier arrivals
+  float* row_loss = nullptr;   // B per-row losses
+  int fused_grid = 0;
+  long long fused_launches = 0;  // alternates the barrier slot, whatever else runs between
 };
 
 namespace {
@@ -98,6 +437,8 @@ void free_all(jx_mlp* n) {
   cudaFree(n->loss);
   cudaFree(n->step);
   cudaFree(n->tab);
+  cudaFree(n->bar);
+  cudaFree(n->row_loss);
 }
 
 int fill_adam_table(jx_mlp* n) {
@@ -163,6 +504,73 @@ int run_step(jx_mlp* n, cudaStream_t st) {
                                                            1.0f - n->b2);
   step_inc_kernel<<<1, 1, 0, st>>>(n->step);
   JX_LAUNCH_CHECK("adam_flat_kernel");
+  return JX_OK;
+}
+
+bool fused_eligible(const jx_mlp* n) {
+  if (!n->fused || n->comm || n->prec != JX_PREC_EXACT || n->L > FS_MAXL || n->B > (1 << 24)) return false;
+  for (long long x : n->w)
+    if (x > (1 << 24)) return false;
+  return true;
+}
+
+int run_fused_step(jx_mlp* n, const float* x, const float* labels, float* loss_out, cudaStream_t st) {
+  if (!n->bar) {
+    JX_CUDA(cudaMalloc(&n->bar, 2 * sizeof(unsigned)));
+    JX_CUDA(cudaMemset(n->bar, 0, 2 * sizeof(unsigned)));
+    JX_CUDA(cudaMalloc(&n->row_loss, sizeof(float) * n->B));
+  }
+  if (!n->fused_grid) {
+    int per_sm = 0;
+    JX_CUDA(cudaFuncSetAttribute(mlp_fused_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(FsSmem)));
+    JX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mlp_fused_step_kernel, FS_THREADS,
+                                                          sizeof(FsSmem)));
+    JX_REQUIRE(per_sm >= 1, "jx_mlp_train_step: fused step does not fit on an SM");
+    // two CTAs per SM: enough for the largest phase, few arrivals per barrier
+    n->fused_grid = jx::num_sms() * (per_sm < 2 ? per_sm : 2);
+  }
+  FusedStep a;
+  a.L = n->L;
+  a.B = (int)n->B;
+  for (int l = 0; l <= n->L; ++l) a.w[l] = (int)n->w[l];
+  for (int l = 0; l < n->L; ++l) {
+    a.act[l] = n->act[l];
+    a.woff[l] = n->woff[l];
+    a.boff[l] = n->boff[l];
+    a.h[l + 1] = n->h[l + 1];
+    a.pre[l + 1] = n->pre[l + 1];
+  }
+  a.h[0] = nullptr;
+  a.pre[0] = nullptr;
+  a.x = x;
+  a.labels = labels;
+  a.params = n->params;
+  a.grads = n->grads;
+  a.m = n->m;
+  a.v = n->v;
+  a.dzA = n->dz;
+  a.dzB = n->dh;
+  a.row_loss = n->row_loss;
+  a.loss = n->loss;
+  a.loss_out = loss_out;
+  a.step = n->step;
+  a.tab = n->tab;
+  a.lr = n->lr;
+  a.b1 = n->b1;
+  a.b2 = n->b2;
+  a.eps = n->eps;
+  a.omb1 = 1.0f - n->b1;
+  a.omb2 = 1.0f - n->b2;
+  a.count = (float)(n->global_B * n->w[n->L]);
+  a.nparams = n->nparams;
+  a.bar = n->bar;
+  a.slot = (int)(n->fused_launches & 1);
+  a.err = jx::device_error_word();
+  void* args[] = {&a};
+  JX_CUDA(cudaLaunchCooperativeKernel((const void*)mlp_fused_step_kernel, dim3(n->fused_grid), dim3(FS_THREADS), args,
+                                      sizeof(FsSmem), st));
+  ++n->fused_launches;
   return JX_OK;
 }
 
@@ -302,6 +710,11 @@ int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* los
   JX_REQUIRE(n && x && labels, "jx_mlp_train_step: NULL argument");
   JX_REQUIRE(n->steps < ADAM_TABLE_STEPS, "jx_mlp_train_step: more than %lld steps", ADAM_TABLE_STEPS);
   cudaStream_t st = jx::as_stream(stream);
+  if (fused_eligible(n)) {
+    if (int rc = run_fused_step(n, x, labels, loss_out, st)) return rc;
+    ++n->steps;
+    return JX_OK;
+  }
   JX_CUDA(cudaMemcpyAsync(n->h[0], x, sizeof(float) * n->B * n->w[0], cudaMemcpyDeviceToDevice, st));
   JX_CUDA(cudaMemcpyAsync(n->labels, labels, sizeof(float) * n->B, cudaMemcpyDeviceToDevice, st));
   int rc;
@@ -334,6 +747,12 @@ int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* los
   if (rc) return rc;
   if (loss_out) JX_CUDA(cudaMemcpyAsync(loss_out, n->loss, sizeof(float), cudaMemcpyDeviceToDevice, st));
   ++n->steps;
+  return JX_OK;
+}
+
+int jx_mlp_set_fused(jx_mlp* n, int enable) {
+  JX_REQUIRE(n, "jx_mlp_set_fused: NULL");
+  n->fused = enable != 0;
   return JX_OK;
 }
 

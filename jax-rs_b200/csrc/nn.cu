@@ -19,29 +19,16 @@
 
 #include "jx_common.cuh"
 #include "jx_math.cuh"
+#include "nn_common.cuh"
 
 namespace {
 
-constexpr float XENT_EPS = 1e-7f;
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// one_hot's class of a label (src/nn.rs:214-218): `idx as usize` saturates
-// negatives and NaN to 0 and truncates toward zero; out-of-range classes mark nothing.
-__device__ __forceinline__ long long label_class(float v) {
-  if (!(v > 0.0f)) return 0;  // negative, zero, NaN
-  if (v >= 9.2e18f) return 0x7fffffffffffffffLL;
-  return (long long)v;
-}
+using jxn::act_f;
+using jxn::act_grad;
+using jxn::label_class;
+using jxn::warp_max;
+using jxn::warp_sum;
+using jxn::XENT_EPS;
 
 // One warp per row.  Softmax: m = max (fold with max, order-free), e_c =
 // exp(x_c - m), s = sum e_c, p_c = e_c / s.
@@ -61,39 +48,17 @@ __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restri
   }
 }
 
-// Fused softmax + cross-entropy with one-hot labels.  Per row: probabilities
-// (optional output), the row's loss contribution -ln(p_y + eps) (the other
-// classes contribute -0 * ln(p + eps) = 0), and dL/dlogits with the reference's
-// normaliser `count` (rows*cols for one call; the global element count when
-// the batch is split across data-parallel ranks).
+// Fused softmax + cross-entropy with one-hot labels, one warp per row
+// (jxn::softmax_xent_row).
 __global__ void softmax_xent_kernel(const float* __restrict__ logits, const float* __restrict__ labels,
                                     float* __restrict__ probs, float* __restrict__ dlogits,
                                     float* __restrict__ row_loss, long long rows, int cols, float count) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const float* in = logits + r * cols;
-    const long long y = label_class(labels[r]);
-    float m = -INFINITY;
-    for (int c = lane; c < cols; c += 32) m = fmaxf(m, in[c]);
-    m = warp_max(m);
-    float s = 0.0f;
-    for (int c = lane; c < cols; c += 32) s += jxm::jx_exp(in[c] - m);
-    s = warp_sum(s);
-    const bool has = y < cols;
-    const float py = has ? __fdiv_rn(jxm::jx_exp(in[y] - m), s) : 0.0f;
-    // dL/dp_y and sum_k p_k dL/dp_k (only the label term is non-zero)
-    const float dpy = has ? -__fdiv_rn(1.0f, __fmul_rn(__fadd_rn(py, XENT_EPS), count)) : 0.0f;
-    const float sdot = __fmul_rn(py, dpy);
-    for (int c = lane; c < cols; c += 32) {
-      const float p = __fdiv_rn(jxm::jx_exp(in[c] - m), s);
-      if (probs) probs[r * cols + c] = p;
-      if (dlogits) {
-        const float dp = (has && c == y) ? dpy : 0.0f;
-        dlogits[r * cols + c] = __fmul_rn(p, __fsub_rn(dp, sdot));
-      }
-    }
-    if (lane == 0) row_loss[r] = has ? -logf(__fadd_rn(py, XENT_EPS)) : 0.0f;
+    const float l = jxn::softmax_xent_row(logits + r * cols, labels[r], cols, count, probs ? probs + r * cols : nullptr,
+                                          dlogits ? dlogits + r * cols : nullptr, lane);
+    if (lane == 0) row_loss[r] = l;
   }
 }
 
@@ -110,19 +75,6 @@ __global__ void sum_div_kernel(const float* __restrict__ v, long long n, float c
     acc = warp_sum(acc);
     if (threadIdx.x == 0) out[0] = __fdiv_rn(acc, count);
   }
-}
-
-template <int ACT>
-__device__ __forceinline__ float act_f(float x) {
-  if constexpr (ACT == 1) return fmaxf(x, 0.0f);
-  else if constexpr (ACT == 2) return jxm::gelu_f(x);
-  else return x;
-}
-template <int ACT>
-__device__ __forceinline__ float act_grad(float x) {
-  if constexpr (ACT == 1) return x > 0.0f ? 1.0f : 0.0f;  // relu'(0) taken as 0
-  else if constexpr (ACT == 2) return jxm::gelu_grad_f(x);
-  else return 1.0f;
 }
 
 // y = act(y + bias[c]) over [rows, cols]; pre (optional) keeps y + bias.
@@ -172,7 +124,14 @@ __global__ void col_partial_kernel(const float* __restrict__ dy, float* __restri
   if (c >= cols) return;
   const long long r1 = r0 + CS < rows ? r0 + CS : rows;
   float acc = 0.0f;
-  for (long long r = r0; r < r1; ++r) acc += dy[r * cols + c];
+  for (long long r = r0; r < r1; r += 16) {  // 16 loads in flight, added in row order
+    float vals[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) vals[j] = r + j < r1 ? dy[(r + j) * cols + c] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (r + j < r1) acc += vals[j];
+  }
   part[(long long)blockIdx.y * cols + c] = acc;
 }
 __global__ void col_final_kernel(const float* __restrict__ part, float* __restrict__ db, int chunks, int cols) {

@@ -7,6 +7,8 @@ The C types map one to one: `int` -> `c_int`, `int64_t` -> `i64`,
 `size_t` -> `usize`, `float` -> `f32`, pointers keep their constness level by
 level, `jx_stream_t` -> `JxStream`, and the opaque handles (`jx_tape`,
 `jx_graph`, `jx_program`, `jx_mlp`) become zero-sized `#[repr(C)]` structs.
+`python jax-rs_b200/rust_ffi.py --update INTEGRATION.md` rewrites the block
+between that file's rust-ffi markers.
 """
 from __future__ import annotations
 
@@ -104,5 +106,18 @@ def rust_block(header: str = HEADER) -> str:
     return "\n".join(lines) + "\n"
 
 
+def update_doc(path: str) -> None:
+    """Rewrite the block between the rust-ffi markers of a Markdown file."""
+    with open(path) as f:
+        doc = f.read()
+    begin, end = "<!-- rust-ffi:begin -->\n```rust\n", "```\n<!-- rust-ffi:end -->"
+    i, j = doc.index(begin) + len(begin), doc.index(end)
+    with open(path, "w") as f:
+        f.write(doc[:i] + rust_block() + doc[j:])
+
+
 if __name__ == "__main__":
-    sys.stdout.write(rust_block())
+    if len(sys.argv) == 3 and sys.argv[1] == "--update":
+        update_doc(sys.argv[2])
+    else:
+        sys.stdout.write(rust_block())

@@ -160,3 +160,34 @@ def test_mlp_3xtf32_tracks_oracle(jx, dev, oracle):
     ol, _, _ = OM.train(Ws, bs, data)
     dl, _ = _train_device(jx, dev, Ws, bs, data, widths, jx.PREC_3XTF32)
     assert max(abs(a - b) for a, b in zip(dl, ol)) <= 1e-4
+
+
+def _train_mode(jx, dev, Ws, bs, data, widths, acts, fused):
+    net = jx.MLP(widths, acts, data[0][0].shape[0], jx.PREC_EXACT)
+    jx.call("jx_mlp_set_fused", net.handle, 1 if fused else 0)
+    net.set_params(net.pack(Ws, bs))
+    net.set_adam(1e-3, 0.9, 0.999, 1e-8)
+    losses = []
+    Lo = dev.full((1,), np.nan)
+    for x, y in data:
+        X, Y = dev.put(x), dev.put(y)
+        net.step(X.data_ptr(), Y.data_ptr(), Lo.data_ptr(), dev.stream)
+        losses.append(dev.get(Lo)[0])
+    return np.array(losses), net.get_params()
+
+
+@pytest.mark.parametrize("widths,acts,batch", [([784, 256, 128, 10], ["relu", "relu"], 128),
+                                               ([33, 70, 5], ["gelu"], 300),
+                                               ([20, 17, 9, 13, 3], ["relu", "none", "gelu"], 37),
+                                               ([64, 10], [], 16)])
+def test_fused_step_bit_identical_to_graph(jx, dev, oracle, widths, acts, batch):
+    """One cooperative kernel per step gives the captured graph's bits:
+    losses and every parameter after 12 Adam steps."""
+    import oracle.mlp as OM
+    Ws, bs = OM.xavier_params(widths, seed=3)
+    data = OM.batches(12, batch, widths[0], widths[-1], seed=4)
+    lf, pf = _train_mode(jx, dev, Ws, bs, data, widths, acts, True)
+    lg, pg = _train_mode(jx, dev, Ws, bs, data, widths, acts, False)
+    assert np.array_equal(lf, lg)
+    assert np.array_equal(pf, pg)
+    assert jx.device_status() == 0
