@@ -275,10 +275,18 @@ __global__ void __launch_bounds__(RNG_THREADS) rng_kernel(uint64_t s0, uint64_t 
     }
     __syncwarp();
     const int c = lane >> 4, col = lane & 15;
+    // row r of the tile goes to (2 * (warp_first + r) + c) * RNG_CHUNK + j0 + col
+    const long long idx0 = (2 * warp_first + c) * RNG_CHUNK + j0 + col;
+    if ((2 * warp_first + 63) * RNG_CHUNK + j0 + 15 < n) {  // the whole tile is in range (warp-uniform)
+      float* p = out + idx0;
+#pragma unroll 8
+      for (int r = 0; r < 32; ++r, p += 2 * RNG_CHUNK) __stcs(p, T[r][lane]);
+    } else {
 #pragma unroll 4
-    for (int r = 0; r < 32; ++r) {
-      const long long idx = (2 * (warp_first + r) + c) * RNG_CHUNK + j0 + col;
-      if (idx < n) __stcs(out + idx, T[r][lane]);
+      for (int r = 0; r < 32; ++r) {
+        const long long idx = idx0 + (long long)r * 2 * RNG_CHUNK;
+        if (idx < n) __stcs(out + idx, T[r][lane]);
+      }
     }
     __syncwarp();
   }

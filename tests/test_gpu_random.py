@@ -56,3 +56,18 @@ def test_zero_size_and_bad_range(jx, dev, oracle):
     with pytest.raises(jx.JaxRsError) as e:
         jx.call("jx_random_randint_f32", k.s0, k.s1, None, 10, 5, 5, dev.stream)
     assert "minval must be less than maxval" in e.value.message
+
+
+@pytest.mark.parametrize("n", [5000, 262145])
+def test_unaligned_output_stream(jx, dev, oracle, n):
+    """An output that is not 16-byte aligned gives the same stream."""
+    k = _key(oracle, 9)
+    Y = dev.full((n + 1,), np.nan)
+    jx.call("jx_random_uniform_f32", k.s0, k.s1, Y.data_ptr() + 4, n, -2.0, 3.0, dev.stream)
+    y = dev.get(Y)
+    assert np.isnan(y[0])
+    assert np.array_equal(y[1:], oracle.uniform_range(k, n, -2.0, 3.0))
+    jx.call("jx_random_normal_f32", k.s0, k.s1, Y.data_ptr() + 4, n, dev.stream)
+    z = dev.get(Y)[1:]
+    ref = oracle.normal(k, n)
+    assert np.all(np.abs(z - ref) <= 2e-6 * np.abs(ref) + 5e-7)
