@@ -183,7 +183,20 @@ struct PoolArgs {
   float* y;
   long long N, H, W, OH, OW;
   int kh, kw, sh, sw, ph, pw;
+  unsigned ow_m, oh_m;  // division by OW and OH as multiply-high (fast_div), 32-bit index path
+  int ow_l, oh_l;
 };
+
+// n / d for n < 2^31 by the multiply-high method of Granlund and Montgomery
+// ("Division by invariant integers using multiplication", 1994): with
+// l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> l (the sum stays below 2^32 for n < 2^31).
+void fast_div_params(unsigned d, unsigned& m, int& l) {
+  l = 0;
+  while ((1ull << l) < d) ++l;
+  m = (unsigned)((((1ull << l) - d) << 32) / d + 1);
+}
+__device__ __forceinline__ unsigned fast_div(unsigned n, unsigned m, int l) { return (__umulhi(n, m) + n) >> l; }
 
 // IDX is the index type: 32-bit when every index fits (cheaper division).
 // KH, KW > 0 fix the window at compile time (fully unrolled); 0 reads it from
@@ -203,16 +216,30 @@ __global__ void __launch_bounds__(256) pool2d_kernel(PoolArgs a) {
   const IDX stride = (IDX)gridDim.x * blockDim.x;
   const float neutral = MAX ? -INFINITY : 0.0f;
   const int kh = KH > 0 ? KH : a.kh, kw = KW > 0 ? KW : a.kw;
+  constexpr bool SMALL = sizeof(IDX) == 4;
   for (IDX idx = (IDX)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
-    const IDX t = idx / OW;
+    const IDX t = SMALL ? (IDX)fast_div((unsigned)idx, a.ow_m, a.ow_l) : idx / OW;
     const IDX ow = idx - t * OW;
-    const IDX n = t / OH;
+    const IDX n = SMALL ? (IDX)fast_div((unsigned)t, a.oh_m, a.oh_l) : t / OH;
     const IDX oh = t - n * OH;
     const float* plane = a.x + (long long)n * a.H * a.W;
     const long long ih0 = (long long)oh * a.sh - a.ph, iw0 = (long long)ow * a.sw - a.pw;
     float acc = neutral;
     int count = 0;
-    if (KH > 0) {
+    if (KH > 0 && ih0 >= 0 && iw0 >= 0 && ih0 + kh <= a.H && iw0 + kw <= a.W) {
+      // the whole window inside the plane: no tests
+      const float* p0 = plane + ih0 * a.W + iw0;
+      float v[KH > 0 ? KH : 1][KW > 0 ? KW : 1];
+#pragma unroll
+      for (int r = 0; r < kh; ++r)
+#pragma unroll
+        for (int c = 0; c < kw; ++c) v[r][c] = __ldg(p0 + r * a.W + c);
+#pragma unroll
+      for (int r = 0; r < kh; ++r)
+#pragma unroll
+        for (int c = 0; c < kw; ++c) acc = pool_fold<MAX>(acc, v[r][c]);
+      count = kh * kw;
+    } else if (KH > 0) {
       float v[KH > 0 ? KH : 1][KW > 0 ? KW : 1];
 #pragma unroll
       for (int r = 0; r < kh; ++r) {
@@ -223,7 +250,7 @@ __global__ void __launch_bounds__(256) pool2d_kernel(PoolArgs a) {
           const long long iw = iw0 + c;
           const bool ok = rok && iw >= 0 && iw < a.W;
           v[r][c] = ok ? __ldg(plane + ih * a.W + iw) : neutral;
-          count += ok;
+          if (!MAX) count += ok;
         }
       }
 #pragma unroll
@@ -239,7 +266,7 @@ __global__ void __launch_bounds__(256) pool2d_kernel(PoolArgs a) {
           const long long iw = iw0 + c;
           const bool ok = rok && iw >= 0 && iw < a.W;
           acc = pool_fold<MAX>(acc, ok ? __ldg(plane + ih * a.W + iw) : neutral);
-          count += ok;
+          if (!MAX) count += ok;
         }
       }
     }
@@ -600,6 +627,10 @@ int jx_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int
   if (total == 0) return JX_OK;
   JX_REQUIRE(x && y, "jx_pool2d_f32: NULL buffer");
   const bool small = total + 256LL * 16 * jx::num_sms() < (1LL << 31) && a.N * a.H * a.W < (1LL << 31);
+  if (small) {
+    fast_div_params((unsigned)a.OW, a.ow_m, a.ow_l);
+    fast_div_params((unsigned)a.OH, a.oh_m, a.oh_l);
+  }
   cudaStream_t st = jx::as_stream(stream);
   if (op == JX_POOL_MAX) {
     if (small)
