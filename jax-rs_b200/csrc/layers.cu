@@ -66,6 +66,7 @@ struct Conv1dArgs {
   float* y;
   long long B, C, L, O, K, S, P, OL, Opad;
   int icc, xw;
+  int buf_floats;  // one of the two shared-memory buffers: icc*K*64 taps + icc*xw inputs, padded to 4
 };
 
 // w [O][C][K] -> wt [C*K][Opad] (Opad = O rounded up to the 64-channel tile).
@@ -107,11 +108,20 @@ __device__ __forceinline__ void conv1d_chunk(const float* __restrict__ xs, const
   }
 }
 
+__device__ __forceinline__ void c1_cp4(float* dst, const float* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(jxd::smem_u32(dst)), "l"(src),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void c1_cp16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(jxd::smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Input channels stream through two shared-memory buffers filled by
+// cp.async: chunk i+1 lands while chunk i is summed.
 template <int SS, int KK>
 __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
   extern __shared__ __align__(16) float c1_smem[];
-  float* ws = c1_smem;                                  // icc * K * 64
-  float* xs = c1_smem + (size_t)a.icc * a.K * C1_OC;    // icc * xw
   const int tid = threadIdx.x, lane = tid & 31, og = tid >> 5;
   const long long p0 = (long long)blockIdx.x * C1_POS;
   const long long o0 = (long long)blockIdx.y * C1_OC;
@@ -126,40 +136,55 @@ __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
   const bool interior = p_first >= a.OL || (p_first * a.S - a.P >= 0 && p_last * a.S - a.P + a.K <= a.L);
   const bool warp_interior = __all_sync(0xffffffffu, interior);
 
+  // fill(buf, c0): taps of input channels [c0, c0 + nic) (rows (c0+ic)*K + k
+  // of wt, the tile's 64 channels each, 16-byte copies) and their input
+  // windows (zero outside [0, L))
+  auto fill = [&](int buf, long long c0) {
+    float* ws = c1_smem + (size_t)buf * a.buf_floats;
+    float* xs = ws + (size_t)a.icc * a.K * C1_OC;
+    const int nic = (int)min((long long)a.icc, a.C - c0);
+    const int wn4 = nic * K * (C1_OC / 4);
+    const float* wsrc = a.wt + c0 * a.K * a.Opad + o0;
+    for (int i = tid; i < wn4; i += C1_THREADS) c1_cp16(ws + 4 * i, wsrc + (long long)(i >> 4) * a.Opad + 4 * (i & 15));
+    const float* xb = a.x + (b * a.C + c0) * a.L;
+    int ic = tid / a.xw, off = tid - ic * a.xw;
+    for (int i = tid; i < nic * a.xw; i += C1_THREADS) {
+      const long long ip = in0 + off;
+      const bool v = ip >= 0 && ip < a.L;
+      c1_cp4(xs + i, v ? xb + (long long)ic * a.L + ip : a.x, v);
+      off += C1_THREADS;
+      while (off >= a.xw) {
+        off -= a.xw;
+        ++ic;
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
   float acc[8][C1_NJ];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
     for (int j = 0; j < C1_NJ; ++j) acc[r][j] = 0.0f;
 
-  for (long long c0 = 0; c0 < a.C; c0 += a.icc) {
+  fill(0, 0);
+  int buf = 0;
+  for (long long c0 = 0; c0 < a.C; c0 += a.icc, buf ^= 1) {
     const int nic = (int)min((long long)a.icc, a.C - c0);
-    __syncthreads();
-    // filter taps: rows (c0+ic)*K + k of wt, the tile's 64 channels each:
-    // 16 float4 per row, straight copies
-    const int wn4 = nic * K * (C1_OC / 4);
-    const float4* wsrc = reinterpret_cast<const float4*>(a.wt + c0 * a.K * a.Opad + o0);
-    for (int i = tid; i < wn4; i += C1_THREADS)
-      reinterpret_cast<float4*>(ws)[i] = __ldg(wsrc + (long long)(i >> 4) * (a.Opad / 4) + (i & 15));
-    // input window, zero outside [0, L); (ic, off) advanced without division
-    const float* xb = a.x + (b * a.C + c0) * a.L;
-    {
-      int ic = tid / a.xw, off = tid - ic * a.xw;
-      for (int i = tid; i < nic * a.xw; i += C1_THREADS) {
-        const long long ip = in0 + off;
-        xs[i] = (ip >= 0 && ip < a.L) ? __ldg(xb + (long long)ic * a.L + ip) : 0.0f;
-        off += C1_THREADS;
-        while (off >= a.xw) {
-          off -= a.xw;
-          ++ic;
-        }
-      }
+    if (c0 + a.icc < a.C) {
+      fill(buf ^ 1, c0 + a.icc);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    __syncthreads();
+    __syncthreads();  // chunk c0 has landed for every thread
+    const float* ws = c1_smem + (size_t)buf * a.buf_floats;
+    const float* xs = ws + (size_t)a.icc * a.K * C1_OC;
     if (warp_interior)
       conv1d_chunk<SS, KK, false>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
     else
       conv1d_chunk<SS, KK, true>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
+    __syncthreads();  // done with this buffer before it is refilled
   }
 
 #pragma unroll
@@ -567,10 +592,11 @@ int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64
   a.OL = OL;
   a.xw = (int)((C1_POS - 1) * stride + kernel_len);
   const long long per_ic = (long long)kernel_len * C1_OC + a.xw;  // floats per input channel of a chunk
-  const long long budget = 48 * 1024 / 4;
+  const long long budget = 48 * 1024 / 4;                          // floats per buffer
   a.icc = (int)std::max(1LL, std::min({16LL, (long long)in_channels, budget / per_ic}));
-  const size_t smem = (size_t)a.icc * per_ic * 4;
-  JX_REQUIRE(smem <= 200 * 1024, "jx_conv1d_f32: window too large for shared memory");
+  a.buf_floats = (int)((a.icc * per_ic + 3) / 4 * 4);
+  const size_t smem = (size_t)2 * a.buf_floats * 4;
+  JX_REQUIRE(smem <= 220 * 1024, "jx_conv1d_f32: window too large for shared memory");
   void (*kern)(Conv1dArgs) = stride == 1 ? (kernel_len == 3 ? conv1d_kernel<1, 3> : conv1d_kernel<1, 0>)
                             : stride == 2 ? conv1d_kernel<2, 0> : conv1d_kernel<0, 0>;
   if (smem > 48 * 1024)
