@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
                    choices=["sgemm", "chain", "chain_grad", "rng", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
-                            "conv", "bgemm", "conv1d", "pool", "batchnorm"])
+                            "conv", "bgemm", "conv1d", "pool", "batchnorm", "sum_vjp", "max_vjp"])
     p.add_argument("--precision", default=None, choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer (default: exact for mlp, whose one-tile products the "
                         "sequential-k kernel runs faster and bit-identically; 3xtf32 for wide_mlp)")
@@ -240,6 +240,16 @@ def cpu_measure(args, threads, budget_s=8.0):
         else:
             fn = lambda: O.arg_rows(x, True, nthreads=threads)
         work, unit, sample = (4.0 * x.size + 4.0 * 4096) / 1e9, "GB/s", "4096 of the 65536 rows"
+    elif wl in ("sum_vjp", "max_vjp"):
+        x = rng.standard_normal((4096, 4096)).astype(np.float32)
+        ct = rng.standard_normal(4096).astype(np.float32)
+        if wl == "sum_vjp":
+            fn = lambda: O.sum_rows_vjp(ct, 4096)
+            work = (4.0 * 4096 + 4.0 * x.size) / 1e9
+        else:
+            fn = lambda: O.max_rows_vjp(x, ct)
+            work = (8.0 * x.size + 4.0 * 4096) / 1e9
+        unit, sample = "GB/s", "4096 of the 65536 rows (1 thread)"
     elif wl == "fullsum":
         n = 1 << 24
         x = rng.standard_normal(n).astype(np.float32)
@@ -599,6 +609,22 @@ def run_reduce(args, dist, jx, torch):
         def step():
             jx.argreduce_rows(X.data_ptr(), idx.data_ptr(), None, rows, cols, True, s)
         kern, bytes_step = "argreduce_rows_kernel", 4.0 * rows * cols + 4.0 * rows
+    elif args.workload == "sum_vjp":
+        # cotangent of sum over axis 1 broadcast back: read ct [rows], write dx [rows, cols]
+        CT = torch.randn(rows, device=dev, generator=g)
+        DX = torch.empty_like(X)
+
+        def step():
+            jx.sum_rows_vjp(CT.data_ptr(), DX.data_ptr(), rows, cols, s)
+        kern, bytes_step = "sum_rows_vjp", 4.0 * rows + 4.0 * rows * cols
+    elif args.workload == "max_vjp":
+        # max over axis 1: the cotangent split over the tied maxima of each row
+        CT = torch.randn(rows, device=dev, generator=g)
+        DX = torch.empty_like(X)
+
+        def step():
+            jx.max_rows_vjp(X.data_ptr(), CT.data_ptr(), DX.data_ptr(), rows, cols, s)
+        kern, bytes_step = "max_rows_vjp", 4.0 * rows * cols + 4.0 * rows + 4.0 * rows * cols
     else:
         def step():
             jx.reduce_all(X.data_ptr(), out.data_ptr(), rows * cols, "sum", s)
@@ -619,12 +645,17 @@ def run_reduce(args, dist, jx, torch):
     clocks = clk.stop()
     gbs = bytes_step * dist.world / (ms * 1e-3) / 1e9
     hbm, _, basis = load_peaks()
-    res = [idx] if args.workload == "argmax" else ([out] if args.workload == "rowsum" else [out[:1]])
-    e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], res, step, args.e2e_steps)
+    if args.workload in ("sum_vjp", "max_vjp"):
+        ins = [CT] if args.workload == "sum_vjp" else [X, CT]
+        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, ins, [DX], step, args.e2e_steps)
+    else:
+        res = [idx] if args.workload == "argmax" else ([out] if args.workload == "rowsum" else [out[:1]])
+        e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X], res, step, args.e2e_steps)
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
-            "config": {"workload": f"{args.workload} over [{rows}, {cols}] f32 per rank", "l2": "1 GiB input > L2"},
+            "config": {"workload": f"{args.workload} over [{rows}, {cols}] f32 per rank",
+                       "l2": "1 GiB input or output > L2"},
             "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,

@@ -257,6 +257,64 @@ __global__ void __launch_bounds__(256) max_rows_vjp_kernel(const float* __restri
   }
 }
 
+// Rows of up to 8192 floats (a multiple of 4, 16-byte aligned): one block
+// per row, the row held in registers (V4 float4 per thread), so it is read
+// once: block max, block count of the maxima, then the write.
+template <int V4>
+__global__ void __launch_bounds__(256) max_rows_vjp_reg_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ ct, float* __restrict__ dx,
+                                                               long long rows, int cols) {
+  __shared__ float sm_max[8];
+  __shared__ int sm_cnt[8];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c4 = cols >> 2;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4* row = reinterpret_cast<const float4*>(x + r * cols);
+    float4 v[V4];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+      const int i = threadIdx.x + 256 * k;
+      v[k] = i < c4 ? __ldcs(row + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+    }
+    m = warp_red(JX_RED_MAX, m);
+    if (lane == 0) sm_max[w] = m;
+    __syncthreads();
+    m = sm_max[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, sm_max[i]);
+    int cnt = 0;
+#pragma unroll
+    for (int k = 0; k < V4; ++k)
+      if (threadIdx.x + 256 * k < c4) cnt += (v[k].x == m) + (v[k].y == m) + (v[k].z == m) + (v[k].w == m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) sm_cnt[w] = cnt;
+    __syncthreads();
+    cnt = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cnt += sm_cnt[i];
+    const float count = (float)cnt;  // exact: counts < 2^24
+    const float g = ct[r];
+    const float hit = count > 1.0f ? __fdiv_rn(1.0f, count) : 1.0f;
+    float4* drow = reinterpret_cast<float4*>(dx + r * cols);
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+      const int i = threadIdx.x + 256 * k;
+      if (i < c4) {
+        float4 o;
+        o.x = __fmul_rn(v[k].x == m ? hit : 0.0f, g);
+        o.y = __fmul_rn(v[k].y == m ? hit : 0.0f, g);
+        o.z = __fmul_rn(v[k].z == m ? hit : 0.0f, g);
+        o.w = __fmul_rn(v[k].w == m ? hit : 0.0f, g);
+        __stcs(drow + i, o);
+      }
+    }
+    __syncthreads();  // sm_max / sm_cnt are reused by the next row
+  }
+}
+
 int grid_rows(long long rows, int warps_per_block) {
   long long blocks = (rows + warps_per_block - 1) / warps_per_block;
   long long cap = (long long)jx::num_sms() * 16;
@@ -354,7 +412,20 @@ int jx_max_rows_vjp_f32(const float* x, const float* ct, float* dx, int64_t rows
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "max vjp: bad size");
   if (rows == 0) return JX_OK;
   JX_REQUIRE(x && ct && dx, "max vjp: NULL pointer");
-  max_rows_vjp_kernel<<<grid_rows(rows, 8), 256, 0, jx::as_stream(stream)>>>(x, ct, dx, rows, (int)cols);
+  cudaStream_t st = jx::as_stream(stream);
+  const bool vec = (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dx) & 15) == 0;
+  const int blocks = (int)std::min<long long>(rows, (long long)jx::num_sms() * 8);
+  if (vec && cols <= 1024)
+    max_rows_vjp_reg_kernel<1><<<blocks, 256, 0, st>>>(x, ct, dx, rows, (int)cols);
+  else if (vec && cols <= 2048)
+    max_rows_vjp_reg_kernel<2><<<blocks, 256, 0, st>>>(x, ct, dx, rows, (int)cols);
+  else if (vec && cols <= 4096)
+    max_rows_vjp_reg_kernel<4><<<blocks, 256, 0, st>>>(x, ct, dx, rows, (int)cols);
+  else if (vec && cols <= 8192)
+    max_rows_vjp_reg_kernel<8><<<blocks, 256, 0, st>>>(x, ct, dx, rows, (int)cols);
+  else
+    max_rows_vjp_kernel<<<grid_rows(rows, 8), 256, 0, st>>>(x, ct, dx, rows, (int)cols);
   JX_LAUNCH_CHECK("max_rows_vjp_kernel");
   return JX_OK;
 }

@@ -116,3 +116,19 @@ def test_sum_and_max_vjp(jx, dev, oracle):
     assert np.array_equal(dev.get(DX), oracle.sum_rows_vjp(ct, cols))
     jx.max_rows_vjp(X.data_ptr(), CT.data_ptr(), DX.data_ptr(), rows, cols, dev.stream)
     assert np.array_equal(dev.get(DX), oracle.max_rows_vjp(x, ct))
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 4), (300, 128), (64, 1024), (64, 1028), (40, 2048), (33, 4096),
+                                       (17, 8192), (9, 8196)])
+def test_max_vjp_widths(jx, dev, oracle, rows, cols):
+    """Every width class of the register-resident kernel and the fallback:
+    ties (small integers), a row of -inf and a NaN, bit-identical."""
+    rng = np.random.default_rng(rows + cols)
+    x = rng.integers(-3, 4, (rows, cols)).astype(np.float32)
+    x[0, :] = -np.inf
+    x[1, 2] = np.nan
+    ct = rng.standard_normal(rows).astype(np.float32)
+    X, CT = dev.put(x), dev.put(ct)
+    DX = dev.full((rows, cols), np.nan)
+    jx.max_rows_vjp(X.data_ptr(), CT.data_ptr(), DX.data_ptr(), rows, cols, dev.stream)
+    assert np.array_equal(dev.get(DX), oracle.max_rows_vjp(x, ct))
