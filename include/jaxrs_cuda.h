@@ -101,7 +101,9 @@ JX_API int jx_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t batch
  * jx_gemm_split_f32 writes hi = tf32(x), lo = tf32(x - hi) K-major:
  * hi/lo are [batch][rows][Kp]; element (r,k) is src[b*stride + r*ld + k], or
  * src[b*stride + k*ld + r] when trans != 0.  jx_gemm_presplit_f32 computes
- * C[b] = Ah.Bh^T + Ah.Bl^T + Al.Bh^T from such buffers (A rows = M, B rows = N). */
+ * C[b] = Ah.Bh^T + Ah.Bl^T + Al.Bh^T from such buffers (A rows = M, B rows = N);
+ * a single product with fewer 128x256 tiles than SMs is cut along K and its
+ * partial products added in order (split-K, library scratch). */
 JX_API int jx_gemm_kpad(int64_t K, int64_t *Kp);
 JX_API int jx_gemm_split_f32(const float *src, float *hi, float *lo, int64_t rows, int64_t K, int64_t ld,
                              int trans, int64_t batch, int64_t stride, jx_stream_t stream);

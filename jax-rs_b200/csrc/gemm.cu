@@ -587,6 +587,31 @@ int launch_fused_split(const float* A, const float* B, float* C, long long M, lo
   return JX_OK;
 }
 
+// Split-K for products with too few output tiles to fill the GPU: the
+// k-blocks are cut into S equal slices (S divides their number, so no slice
+// reads past a padded row), each slice a batch entry of the same pre-split
+// operands (a 3-D tensor map whose batch stride is the slice's offset along
+// K), its partial product written to scratch; the partials are then added in
+// slice order.
+int splitk_slices(long long tiles, long long num_kb) {
+  const long long want = std::min<long long>(16, jx::num_sms() / std::max<long long>(1, tiles));
+  for (long long S = want; S >= 2; --S)
+    if (num_kb % S == 0 && num_kb / S >= SPAN_KB) return (int)S;
+  return 1;
+}
+
+__global__ void splitk_sum_kernel(const float* __restrict__ part, float* __restrict__ C, int M, int N, int S,
+                                  long long ldc) {
+  const long long total = (long long)M * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int sl = 1; sl < S; ++sl) acc += part[(long long)sl * total + i];
+    const long long m = i / N, n = i - m * N;
+    C[m * ldc + n] = acc;
+  }
+}
+
 int launch_split(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
                  int batch, bool transposed, cudaStream_t st) {
   if (!transposed) {
@@ -640,6 +665,38 @@ int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float
   return gemm_presplit_err(Ah, Al, Bh, Bl, C, M, N, Kp, ldc, strideC, batch, st, device_error_word(), false, false);
 }
 
+// One product (batch 1) on pre-split operands, cut into S k-slices.
+int gemm_presplit_splitk(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
+                         int Kp, long long ldc, int S, cudaStream_t st) {
+  int rc = get_encode();
+  if (rc) return rc;
+  const int Ks = Kp / S;  // a multiple of BK
+  CUtensorMap mAh, mAl, mBh, mBl;
+  const uint64_t row = (uint64_t)Kp * 4, slice = (uint64_t)Ks * 4;
+  if ((rc = make_map_3d(&mAh, Ah, Ks, M, S, row, slice, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = make_map_3d(&mAl, Al, Ks, M, S, row, slice, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = make_map_3d(&mBh, Bh, Ks, N, S, row, slice, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = make_map_3d(&mBl, Bl, Ks, N, S, row, slice, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  void* part = nullptr;
+  if ((rc = scratch_get(sizeof(float) * (size_t)S * M * N, &part, st))) return rc;
+  JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+  const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  const int nt = tiles_m * tiles_n * S;
+  float* pp = static_cast<float*>(part);
+  gemm_3xtf32_kernel<<<std::min(nt, num_sms()), GEMM_THREADS, GEMM_SMEM, st>>>(
+      mAh, mAl, mBh, mBl, pp, M, N, Ks, N, (long long)M * N, tiles_m, tiles_n, nt, 0, 0, device_error_word());
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    const long long total = (long long)M * N;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, (long long)num_sms() * 8);
+    splitk_sum_kernel<<<blocks, 256, 0, st>>>(pp, C, M, N, S, ldc);
+    e = cudaGetLastError();
+  }
+  rc = e == cudaSuccess ? JX_OK : check_cuda(e, "split-K kernels");
+  const int rc2 = scratch_release(part, st);
+  return rc ? rc : rc2;
+}
+
 // Sets the main kernel's shared-memory limit on the current device once, up
 // front (jx_init), so no later call -- e.g. one inside a stream capture -- has to.
 int gemm_prepare() {
@@ -690,6 +747,9 @@ int jx_gemm_presplit_f32(const float* Ah, const float* Al, const float* Bh, cons
   JX_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && Kp < (1LL << 31) && batch < 65536, "gemm presplit: too large");
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   JX_REQUIRE(a16(Ah) && a16(Al) && a16(Bh) && a16(Bl), "gemm presplit: operands must be 16-byte aligned");
+  const long long tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int S = batch == 1 ? splitk_slices(tiles, Kp / BK) : 1;
+  if (S > 1) return jx::gemm_presplit_splitk(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, S, jx::as_stream(stream));
   return jx::gemm_presplit(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch,
                            jx::as_stream(stream));
 }
@@ -732,10 +792,10 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
   JX_REQUIRE(precision == JX_PREC_3XTF32, "matmul: unknown precision %d", precision);
   // The split pass costs about 250 * (1/M + 1/N) of the main kernel's time
   // (12 bytes of HBM traffic per operand element against 2*M*N*K flop);
-  // the fused kernel runs about 20% slower than the main kernel (its in-place
-  // split sits on every k-block's critical path with two stages), so it wins
-  // below that crossover, given enough tiles to fill the GPU (a product of a
-  // few tiles is latency-bound, and the longer per-k-block path then costs more).
+  // the fused kernel runs slower than the main kernel (its lo split sits on
+  // the cross products' path with two stages), so it wins below that
+  // crossover, given enough tiles to fill the GPU.  Products with fewer tiles
+  // than SMs take the split pass and are cut along K (split-K).
   const long long tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   if (fused_split_ok(A, B, transA, transB, lda, ldb, batch, strideA, strideB) &&
       250.0 * (1.0 / (double)M + 1.0 / (double)N) > 0.2 && tiles >= jx::num_sms())
@@ -752,7 +812,11 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
   float* Bl = Bh + (size_t)batch * N * Kp;
   rc = launch_split(A, Ah, Al, (int)M, (int)K, (int)Kp, lda, strideA, (int)batch, transA != 0, st);
   if (!rc) rc = launch_split(B, Bh, Bl, (int)N, (int)K, (int)Kp, ldb, strideB, (int)batch, transB == 0, st);
-  if (!rc) rc = jx::gemm_presplit(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st);
+  const int S = batch == 1 ? splitk_slices(tiles, Kp / BK) : 1;
+  if (!rc && S > 1)
+    rc = jx::gemm_presplit_splitk(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, S, st);
+  else if (!rc)
+    rc = jx::gemm_presplit(Ah, Al, Bh, Bl, C, (int)M, (int)N, (int)Kp, ldc, strideC, (int)batch, st);
   int rc2 = jx::scratch_release(scratch, st);
   return rc ? rc : rc2;
 }
