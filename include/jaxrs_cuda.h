@@ -458,6 +458,12 @@ JX_API int jx_mlp_train_step(jx_mlp *mlp, const float *x, const float *labels, f
  * same arithmetic as the separate kernels, bit-identical).  enable = 0 selects
  * the captured graph of separate kernels instead.  On by default. */
 JX_API int jx_mlp_set_fused(jx_mlp *mlp, int enable);
+/* Self-test of the bounded waits (no reference counterpart): a two-block
+ * grid barrier waiting for one arrival more than the grid has.  Each block's
+ * wait gives up after timeout_ms (1..5000), records JX_DEVERR_TIMEOUT in the
+ * device error word and returns; *timed_out = 1 if the kernel reported it.
+ * The context stays usable. */
+JX_API int jx_selftest_barrier_timeout(int timeout_ms, int *timed_out);
 JX_API int jx_mlp_destroy(jx_mlp *mlp);
 
 /* ---- data-parallel collectives (no reference counterpart: the reference has

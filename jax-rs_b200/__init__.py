@@ -142,6 +142,7 @@ _SIGS = {
     "jx_mlp_attach_comm": [vp, vp, ci, i64],
     "jx_mlp_train_step": [vp, vp, vp, vp, vp],
     "jx_mlp_set_fused": [vp, ci],
+    "jx_selftest_barrier_timeout": [ci, C.POINTER(ci)],
     "jx_mlp_destroy": [vp],
     "jx_nccl_unique_id_size": [],
     "jx_nccl_get_unique_id": [vp],

@@ -100,16 +100,17 @@ __device__ __forceinline__ unsigned long long fs_ns() {
 // Grid barrier number `index` (0-based) of this launch: every block adds one
 // arrival and waits until all gridDim.x * (index + 1) have arrived.  The wait
 // gives up after 2 s, records JX_DEVERR_TIMEOUT and returns false.
-__device__ bool fs_grid_sync(unsigned* cnt, unsigned index, unsigned* err, int* ok_flag) {
+__device__ bool fs_grid_sync(unsigned* cnt, unsigned index, unsigned* err, int* ok_flag,
+                             unsigned long long limit_ns = 2000000000ull, unsigned extra = 0) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned target = gridDim.x * (index + 1);
+    const unsigned target = gridDim.x * (index + 1) + extra;
     __threadfence();
     atomicAdd(cnt, 1u);
     bool ok = true;
     const unsigned long long t0 = fs_ns();
     while (*reinterpret_cast<volatile unsigned*>(cnt) < target) {
-      if (fs_ns() - t0 > 2000000000ull) {
+      if (fs_ns() - t0 > limit_ns) {
         atomicOr(err, JX_DEVERR_TIMEOUT);
         ok = false;
         break;
@@ -507,6 +508,15 @@ int run_step(jx_mlp* n, cudaStream_t st) {
   return JX_OK;
 }
 
+// A grid barrier that waits for one arrival more than the grid has: every
+// block's bounded wait runs out after limit_ns, records JX_DEVERR_TIMEOUT and
+// returns; status[0] = 1 if the block saw the timeout.
+__global__ void fs_barrier_selftest_kernel(unsigned* cnt, unsigned* err, unsigned long long limit_ns, int* status) {
+  __shared__ int ok;
+  const bool passed = fs_grid_sync(cnt, 0, err, &ok, limit_ns, 1u);
+  if (threadIdx.x == 0 && !passed) atomicOr(status, 1);
+}
+
 bool fused_eligible(const jx_mlp* n) {
   if (!n->fused || n->comm || n->prec != JX_PREC_EXACT || n->L > FS_MAXL || n->B > (1 << 24)) return false;
   for (long long x : n->w)
@@ -747,6 +757,27 @@ int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* los
   if (rc) return rc;
   if (loss_out) JX_CUDA(cudaMemcpyAsync(loss_out, n->loss, sizeof(float), cudaMemcpyDeviceToDevice, st));
   ++n->steps;
+  return JX_OK;
+}
+
+int jx_selftest_barrier_timeout(int timeout_ms, int* timed_out) {
+  JX_REQUIRE(timed_out && timeout_ms >= 1 && timeout_ms <= 5000, "jx_selftest_barrier_timeout: 1..5000 ms");
+  void* buf = nullptr;
+  JX_CUDA(cudaMalloc(&buf, 64));
+  JX_CUDA(cudaMemset(buf, 0, 64));
+  unsigned* cnt = static_cast<unsigned*>(buf);
+  int* status = reinterpret_cast<int*>(static_cast<char*>(buf) + 32);
+  unsigned* err = jx::device_error_word();
+  unsigned long long limit = (unsigned long long)timeout_ms * 1000000ull;
+  void* args[] = {&cnt, &err, &limit, &status};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)fs_barrier_selftest_kernel, dim3(2), dim3(64), args, 0,
+                                              nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  int h = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h, status, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(buf);
+  if (e != cudaSuccess) return jx::check_cuda(e, "barrier self-test");
+  *timed_out = h;
   return JX_OK;
 }
 

@@ -191,3 +191,20 @@ def test_fused_step_bit_identical_to_graph(jx, dev, oracle, widths, acts, batch)
     assert np.array_equal(lf, lg)
     assert np.array_equal(pf, pg)
     assert jx.device_status() == 0
+
+
+def test_bounded_barrier_wait_reports_timeout(jx, dev, oracle):
+    """A grid barrier that can never complete gives up after its limit,
+    reports JX_DEVERR_TIMEOUT, and the device keeps working."""
+    import ctypes as C
+    jx.device_status()  # clear the error word
+    flag = C.c_int(0)
+    jx.call("jx_selftest_barrier_timeout", 200, C.byref(flag))
+    assert flag.value == 1
+    assert jx.device_status() & 0x2
+    assert jx.device_status() == 0  # read and cleared
+    a = np.arange(6, dtype=np.float32).reshape(2, 3)
+    A, B = dev.put(a), dev.put(np.eye(3, dtype=np.float32))
+    Cm = dev.full((2, 3), np.nan)
+    jx.gemm(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), 2, 3, 3, precision=jx.PREC_EXACT, stream=dev.stream)
+    assert np.array_equal(dev.get(Cm), a)
