@@ -222,6 +222,8 @@ struct ImplicitArgs {
   // cols mode (weight gradient): B columns are output pixels q of all images
   int Q, Ks;                         // contraction length, per-slice length
   int OW, NPo;
+  unsigned npo_m, ow_m;              // q / NPo and p / OW as multiply-high (Granlund-Montgomery)
+  int npo_l, ow_l;
   long long ldc, strideC;            // row-major partial outputs per slice
 };
 
@@ -402,9 +404,10 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           gmask = 0;
           if (jq < a.Ks && q < a.Q) {
             const int qi = (int)q;
-            const int b = qi / a.NPo;
+            // qi < 2^31: n / d = (umulhi(n, m) + n) >> l with the host's (m, l)
+            const int b = (int)((__umulhi((unsigned)qi, a.npo_m) + (unsigned)qi) >> a.npo_l);
             const int p = qi - b * a.NPo;
-            const int oh = p / a.OW, ow = p - (p / a.OW) * a.OW;
+            const int oh = (int)((__umulhi((unsigned)p, a.ow_m) + (unsigned)p) >> a.ow_l), ow = p - oh * a.OW;
             const int qh = oh * a.S - a.P, qw = ow * a.S - a.P;
             gmask = tap_mask(qh, qw, 0, 0, a, false);
             gbase = src + ((long long)b * a.img_stride + (long long)qh * a.LW + qw);
@@ -565,6 +568,15 @@ __global__ void split_filter_ocswap(const float* __restrict__ w, float* __restri
     hi[i] = h;
     lo[i] = l;
   }
+}
+
+// Constants for n / d by multiply-high (Granlund and Montgomery, "Division
+// by invariant integers using multiplication", 1994), valid for n < 2^31:
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1.
+void magic_div(unsigned d, unsigned& m, int& l) {
+  l = 0;
+  while ((1ull << l) < d) ++l;
+  m = (unsigned)((((1ull << l) - d) << 32) / d + 1);
 }
 
 int blocks_for(long long work, int cap_per_sm) {
@@ -775,6 +787,8 @@ int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long lo
     a.Ks = (int)Ks;
     a.OW = g.OW;
     a.NPo = (int)NP;
+    magic_div((unsigned)a.NPo, a.npo_m, a.npo_l);
+    magic_div((unsigned)a.OW, a.ow_m, a.ow_l);
     a.ldc = K;
     a.strideC = (long long)g.O * K;
     rc = launch_conv_gemm<true>(Ah, Al, (int)S, (int)Ksp, x, tab, a, part, st);
