@@ -62,7 +62,8 @@ def parse():
 # the default size, from one ncu capture of dram__bytes_read.sum +
 # dram__bytes_write.sum (commands and figures: profiles/dram_traffic_by_kernel.md).
 # FFT and conv were captured on a smaller batch and scaled by the batch; their
-# traffic is proportional to it.  None for any other size.
+# traffic is proportional to it.  batchnorm sums its three kernels (the
+# roofline covers the whole call).  None for any other size.
 TRAFFIC = {
     "sgemm": 4.5905e9 + 0.2583e9,            # gemm_3xtf32_kernel, 8192^3
     "chain": 1.0738e9 + 1.0275e9,            # jx_tape_kernel, 2^28
@@ -70,13 +71,23 @@ TRAFFIC = {
     "argmax": 1.0738e9 + 0.0033e9,           # argreduce_rows_kernel<max>
     "fullsum": 1.0738e9 + 0.0049e9,          # reduce_all_pass1<sum>
     "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
-    "fft2d": 8 * (0.2685e9 + 0.2121e9),      # column pass fft_kernel<10,8,cols>, batch 32 x 8
+    "fft2d": 8 * (0.2685e9 + 0.2162e9),      # column pass fft1024_kernel, batch 32 x 8
     "conv": 2 * (0.1082e9 + 0.0551e9 + 0.1079e9 + 0.0530e9 + 0.3201e9 + 0.0709e9),  # 3 conv_gemm_kernel, B 32 x 2
+    "bgemm": 2.2020e9 + 1.0442e9,            # gemm_fused_split_kernel, [64,2048,2048]^2
+    "pool": 0.8228e9 + 0.1918e9,             # pool2d_kernel<max,3,3>, [64,256,112,112]
+    "batchnorm": (0.2055e9 + 0.0036e9) + 0.0005e9 + (0.2056e9 + 0.1571e9),  # stats + finalize + apply
+    "conv1d": 0.2704e9 + 0.2296e9,           # conv1d_kernel<1,3>, [64,256,4096]
+    "sum_vjp": 0.0003e9 + 1.0131e9,          # sum_rows_vjp_kernel, [65536,4096]
+    "max_vjp": 1.0742e9 + 1.0265e9,          # max_rows_vjp_reg_kernel<4>, [65536,4096]
+    "rng": 0.0043e9 + 1.0194e9,              # rng_kernel, 2^28 draws
+    "mlp": 0.0033e9 + 0.0,                   # mlp_fused_step_kernel, batch 128 (weights stay in L2)
 }
 
 
 def traffic_for(args):
     default = (args.size == 8192 and not args.fft_batch and not args.conv_batch)
+    if args.workload == "mlp" and args.precision not in (None, "exact"):
+        return None  # the figure is the fused exact step's
     return TRAFFIC.get(args.workload) if default else None
 
 
@@ -831,7 +842,7 @@ def run_layers(args, dist, jx, torch):
         roof = {"bound": "fp32 issue", "kernel": "conv1d_kernel", "achieved": round(val / dist.world, 2),
                 "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(val / dist.world / peak, 4),
                 "peak_basis": f"nominal: 148 SMs x 128 FP32 lanes x {mhz:.0f} MHz, one flop per unfused FMUL or "
-                              "FADD (no measured FP32 peak)", "traffic": None}
+                              "FADD (no measured FP32 peak)", "traffic": traffic_for(args)}
     else:
         val = work * dist.world / (ms * 1e-3) / 1e9
         e2e = work * dist.world / (e_ms * 1e-3) / 1e9
@@ -839,7 +850,7 @@ def run_layers(args, dist, jx, torch):
         roof = {"bound": "hbm", "kernel": "pool2d_kernel" if args.workload == "pool" else
                 "norm_stats_wide + norm_finalize + norm_apply (whole call)",
                 "achieved": round(val / dist.world, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(val / dist.world / hbm, 4), "peak_basis": basis, "traffic": None,
+                "frac": round(val / dist.world / hbm, 4), "peak_basis": basis, "traffic": traffic_for(args),
                 "note": "algorithmic bytes: one read of x and one write of y" +
                         ("; the statistics need a second read of x (12 B per element moved at best without L2 "
                          "reuse), so 8 B per element is a floor no two-pass kernel reaches"
@@ -923,7 +934,7 @@ def run_fft(args, dist, jx, torch):
         torch.cuda.synchronize()
         row_ms = e0.elapsed_time(e1) / args.steps
         kern_ms = max(ms - row_ms, 1e-6)
-        kern, kern_note = "fft_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
+        kern, kern_note = "fft1024_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
     hbm, _, basis = load_peaks()
     kgbs = nbytes / (kern_ms * 1e-3) / 1e9
     # e2e through the host-buffer FFT entry points: blocks of transforms go up,
@@ -1093,7 +1104,8 @@ def run_mlp(args, dist, jx, torch):
         "roofline": {"bound": "tensor" if wide else "launch", "kernel": "whole training step",
                      "achieved": round(flops / (ms * 1e-3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
-                     "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)", "traffic": None,
+                     "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)",
+                     "traffic": None if wide else traffic_for(args),
                      "note": ("exact f32 (sequential-k, unfused): the whole step is one cooperative kernel "
                               "with grid barriers between its phases; the tensor peak is quoted for scale")
                      if prec == jx.PREC_EXACT else ""},
