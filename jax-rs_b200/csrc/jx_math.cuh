@@ -18,7 +18,6 @@
 namespace jxm {
 
 constexpr float PI_F = 3.14159265358979323846f;
-constexpr float GELU_C1 = 0.044715f;
 
 // --- exp / tanh on the multi-function unit ------------------------------------
 // exp(x) = 2^(x*log2(e)).  hi = fl(x*L2E) goes to ex2.approx, which covers the
@@ -68,10 +67,24 @@ __device__ __forceinline__ float jx_tanh(float x) {
 //   sigmoid(x) = (x >= 0 ? 1 : E) / (1 + E),   tanh(|x|) = (1 - E^2) / (1 + E^2),
 // and both quotients share r = 1 / ((1 + E)(1 + E^2)).  For |x| < 0.05 tanh
 // takes the odd series (1 - E^2 cancels there).  Used by op-tapes that apply
-// both functions to one value.
+// both functions to one value.  E is jx_exp's compensated exponential of
+// -min(|x|, 104): exp(-104) is below 2^-149 and flushes to zero, so the
+// clamp changes no result, keeps the exponent finite (infinite x would make
+// the correction term NaN), and min.NaN lets a NaN argument through.
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float y;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+  return y;
+}
 __device__ __forceinline__ void sigmoid_tanh(float x, float& s, float& t) {
+  const float L2E = 1.44269502162933349609375f;  // log2(e) rounded to f32
+  const float LN2 = 0.693147180559945309417f;
   const float ax = fabsf(x);
-  const float E = jx_exp(-ax);
+  const float a_c = min_nan(ax, 104.0f);
+  const float hi = a_c * -L2E;
+  const float lo = fmaf(a_c, -L2E, -hi);
+  const float e = ex2_approx(hi);
+  const float E = fmaf(e, lo * LN2, e);
   const float E2 = E * E;
   const float a = 1.0f + E, b = 1.0f + E2;
   const float r = rcp_approx(a * b);
@@ -109,40 +122,48 @@ static __device__ __noinline__ float jx_unary_more(int op, float x) {
 __device__ __forceinline__ float sign_f(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f); }
 
 // nn::gelu (src/nn.rs:111-122): coeff = sqrt(2/pi); inner = coeff*(v + 0.044715*v^3);
-// 0.5*v*(1 + tanh(inner)); v.powi(3) = v*(v*v).  coeff is the f32 value of
-// sqrtf(2.0f / PI) (0x3f4c4229), as the reference computes it per element.
-// inner is formed in the reference's order; the identity
-// 0.5*(1 + tanh(z)) = 1/(1 + e^{-2z}) then takes one exponential and one
-// reciprocal instead of tanh's two paths.  The difference from the
-// reference's own evaluation is its rounding of 1 + tanh(z) near tanh = -1
-// (at most 0.5*|v|*2^-24 for |v| <= 5, below 3e-7 in absolute terms); large
-// negative v gives -0 or a tiny negative value there as in the reference.
-// e = 2^(-2z*log2 e) skips jx_exp's product correction: its relative error
-// (|2z|*6e-8) matters only while 1/(1 + e) is not negligible, |2z| <= 16.
+// 0.5*v*(1 + tanh(inner)).  coeff is the f32 value of sqrtf(2.0f / PI)
+// (0x3f4c4229), as the reference computes it per element.  The identity
+// 0.5*(1 + tanh(z)) = 1/(1 + e^{-2z}) takes one exponential and one
+// reciprocal instead of tanh's two paths, and the exponent -2*inner*log2(e)
+// is formed as v*(K + KC1*v^2) with K = fl(-2*log2(e)*coeff) and
+// KC1 = fl(K*0.044715) (one multiply, one FMA, one multiply).  That argument
+// is within a few ulp of the reference's rounded inner times -2*log2(e); the
+// relative error it puts on e, |arg|*ln2*2.4e-7, matters only while
+// 1/(1 + e) is not negligible, and the result stays within 2e-6 relative
+// (3e-7 absolute near zero) of the reference's evaluation.  Large negative v
+// gives -0 or a tiny negative value as in the reference.
 __device__ __forceinline__ float gelu_coeff() { return __int_as_float(0x3f4c4229); }
-__device__ __forceinline__ float gelu_inner(float v) {
-  const float v3 = __fmul_rn(v, __fmul_rn(v, v));
-  return __fmul_rn(gelu_coeff(), __fadd_rn(v, __fmul_rn(GELU_C1, v3)));
-}
-constexpr float NEG2_L2E = -2.0f * 1.44269502162933349609375f;  // exact: -2 * fl(log2 e)
+__device__ __forceinline__ float gelu_k() { return __int_as_float(0xc0135760); }    // fl(-2*fl(log2 e)*coeff)
+__device__ __forceinline__ float gelu_kc1() { return __int_as_float(0xbdd2d3e6); }  // fl(K*0.044715)
+__device__ __forceinline__ float gelu_c3() { return __int_as_float(0x3ddb33b5); }   // fl(3*0.044715*coeff)
+// log2 of e^{-2 inner(v)}
+__device__ __forceinline__ float gelu_arg(float v, float v2) { return __fmul_rn(v, fmaf(v2, gelu_kc1(), gelu_k())); }
 __device__ __forceinline__ float gelu_f(float v) {
-  const float e = ex2_approx(gelu_inner(v) * NEG2_L2E);
+  const float e = ex2_approx(gelu_arg(v, __fmul_rn(v, v)));
   return v * rcp_approx(1.0f + e);
 }
 
 // d/du of gelu_f (restated adjoint; the reference leaves gelu untraced):
 // 0.5*(1+t) + 0.5*u*(1-t^2)*dinner with t = tanh(inner),
-// dinner = coeff*(1 + 3*0.044715*u^2).  With s = 0.5*(1+t) = 1/(1+e),
-// e = e^{-2 inner}: 0.5*(1 - t^2) = 2 s (1 - s), and 1 - s = e*s without
-// cancellation while e <= 1 (1 - s is exact enough above that, s <= 1/2).
-__device__ __forceinline__ float gelu_grad_f(float u) {
-  const float coeff = gelu_coeff();
+// dinner = coeff*(1 + 3*0.044715*u^2) = coeff + C3*u^2.  With s = 0.5*(1+t)
+// = 1/(1+e), e = e^{-2 inner}: 0.5*(1 - t^2) = 2 s (1 - s), and 1 - s = e*s
+// without cancellation while e <= 1 (1 - s is exact enough above that,
+// s <= 1/2).  gelu_pair returns gelu_f and gelu_grad_f of one u from one
+// exponential and one reciprocal (op-tapes that apply both to one value).
+__device__ __forceinline__ void gelu_pair(float u, float& g, float& dg) {
   const float u2 = __fmul_rn(u, u);
-  const float e = ex2_approx(gelu_inner(u) * NEG2_L2E);
+  const float e = ex2_approx(gelu_arg(u, u2));
   const float s = rcp_approx(1.0f + e);
   const float oms = e <= 1.0f ? e * s : 1.0f - s;
-  const float dinner = __fmul_rn(coeff, __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, GELU_C1), u2)));
-  return s + 2.0f * u * s * oms * dinner;
+  const float dinner = fmaf(u2, gelu_c3(), gelu_coeff());
+  g = u * s;
+  dg = s + 2.0f * u * s * oms * dinner;
+}
+__device__ __forceinline__ float gelu_grad_f(float u) {
+  float g, dg;
+  gelu_pair(u, g, dg);
+  return dg;
 }
 
 // nn::sigmoid (src/nn.rs:135-140): 1 / (1 + exp(-v))

@@ -84,7 +84,7 @@ std::map<std::string, CUfunction> g_cache;  // "<device>|<structure key>" -> fun
 
 struct jx_tape {
   int n_in, n_out, n_consts;
-  std::vector<int4> code;  // register form, after power-of-two division rewriting
+  std::vector<int4> code;  // register form, after constant folding and power-of-two division rewriting
   float consts[JX_TAPE_MAX_CONSTS];
   std::string key;         // op structure (no constant values)
 };
@@ -128,6 +128,75 @@ int tape_validate(const int32_t* code, int n_instr, int n_consts, int n_inputs, 
 }
 
 namespace {
+
+// Instructions whose operands are all constants, and whose op is exact in
+// IEEE f32 (correctly rounded, so the host computes the same bits as the
+// device), are evaluated here and become constant loads: a value_and_grad
+// tape's -1/c scale costs nothing per element instead of a division.
+// Transcendentals and pow stay on the device (the host's libm rounds
+// differently); so do results that are NaN (payload bits differ between the
+// host and the device), any subnormal operand or result (a host with
+// flush-to-zero set would differ), and min/max/relu of signed zeros (the
+// sign of the result is unspecified).
+bool fold_value(int op, float a, float b, float& r) {
+  auto sub = [](float v) { return fpclassify(v) == FP_SUBNORMAL; };
+  if (sub(a) || sub(b)) return false;
+  const bool zeros = a == 0.0f && b == 0.0f;
+  if (op >= JX_OP_UNARY && op < JX_OP_BINARY) {
+    switch (op - JX_OP_UNARY) {
+      case JX_UN_NEG: r = -a; break;
+      case JX_UN_ABS: r = fabsf(a); break;
+      case JX_UN_SQRT: r = sqrtf(a); break;
+      case JX_UN_RECIP: r = 1.0f / a; break;
+      case JX_UN_SQUARE: r = a * a; break;
+      case JX_UN_RELU: if (a == 0.0f) return false; r = fmaxf(a, 0.0f); break;
+      case JX_UN_SIGN: r = a > 0.0f ? 1.0f : (a < 0.0f ? -1.0f : 0.0f); break;
+      case JX_UN_CEIL: r = ceilf(a); break;
+      case JX_UN_FLOOR: r = floorf(a); break;
+      case JX_UN_ROUND: r = roundf(a); break;
+      case JX_UN_TRUNC: r = truncf(a); break;
+      default: return false;
+    }
+  } else if (op == JX_OP_SELECT_GT) {
+    r = a > 0.0f ? b : 0.0f;
+  } else {
+    switch (op - JX_OP_BINARY) {
+      case JX_BIN_ADD: r = a + b; break;
+      case JX_BIN_SUB: r = a - b; break;
+      case JX_BIN_MUL: r = a * b; break;
+      case JX_BIN_DIV: r = a / b; break;
+      case JX_BIN_MIN: if (zeros) return false; r = fminf(a, b); break;
+      case JX_BIN_MAX: if (zeros) return false; r = fmaxf(a, b); break;
+      default: return false;
+    }
+  }
+  return !isnan(r) && !sub(r);
+}
+
+void fold_constants(std::vector<int4>& code, std::vector<float>& consts) {
+  bool known[JX_TAPE_MAX_REGS] = {false};
+  float val[JX_TAPE_MAX_REGS] = {0.0f};
+  for (int4& ins : code) {
+    const int op = ins.x;
+    if (op == JX_OP_STORE) continue;
+    if (op == JX_OP_CONST) {
+      known[ins.y] = true;
+      val[ins.y] = consts[ins.z];
+      continue;
+    }
+    const bool unary = op >= JX_OP_UNARY && op < JX_OP_BINARY;
+    float r = 0.0f;
+    if (known[ins.z] && (unary || known[ins.w]) && consts.size() < JX_TAPE_MAX_CONSTS &&
+        fold_value(op, val[ins.z], unary ? 0.0f : val[ins.w], r)) {
+      consts.push_back(r);
+      ins = make_int4(JX_OP_CONST, ins.y, (int)consts.size() - 1, 0);
+      known[ins.y] = true;
+      val[ins.y] = r;
+    } else {
+      known[ins.y] = false;
+    }
+  }
+}
 
 // Division by a constant that is a power of two becomes multiplication by its
 // exact reciprocal: the same bits, without the division sequence.  The
@@ -200,7 +269,9 @@ std::string codegen(const jx_tape* t) {
   s += "#pragma unroll\n    for (int v = 0; v < 8; ++v) {\n";
   // SSA: every definition gets a fresh name; reg_name tracks the current one.
   // First pass: the SSA name each unary op reads, to find values that are fed
-  // to both sigmoid and tanh (those share one exponential, jxm::sigmoid_tanh).
+  // to both sigmoid and tanh, or to both gelu and its derivative (each pair
+  // shares one exponential and one reciprocal: jxm::sigmoid_tanh,
+  // jxm::gelu_pair).
   std::vector<std::string> src_name(t->code.size());
   {
     std::string rn[JX_TAPE_MAX_REGS];
@@ -212,12 +283,17 @@ std::string codegen(const jx_tape* t) {
       if (c.x != JX_OP_STORE) rn[c.y] = "t" + std::to_string(nx++);
     }
   }
-  std::map<std::string, int> sig_of, tanh_of;  // SSA value -> count
-  for (size_t i = 0; i < t->code.size(); ++i) {
-    if (t->code[i].x == JX_OP_UNARY + JX_UN_SIGMOID) sig_of[src_name[i]]++;
-    if (t->code[i].x == JX_OP_UNARY + JX_UN_TANH) tanh_of[src_name[i]]++;
-  }
-  std::map<std::string, std::string> pair_done;  // SSA value -> suffix of its sg_/th_ pair
+  // pair kinds: 0 = sigmoid/tanh, 1 = gelu/gelu_grad; first op of each pair
+  const int pair_op[2][2] = {{JX_OP_UNARY + JX_UN_SIGMOID, JX_OP_UNARY + JX_UN_TANH},
+                             {JX_OP_UNARY + JX_UN_GELU, JX_OP_UNARY + JX_UN_GELU_GRAD}};
+  const char* pair_fn[2] = {"sigmoid_tanh", "gelu_pair"};
+  const char* pair_pre[2][2] = {{"sg_", "th_"}, {"gl_", "gd_"}};
+  std::map<std::string, int> seen[2][2];  // SSA value -> uses, per pair kind and member
+  for (size_t i = 0; i < t->code.size(); ++i)
+    for (int k = 0; k < 2; ++k)
+      for (int m = 0; m < 2; ++m)
+        if (t->code[i].x == pair_op[k][m]) seen[k][m][src_name[i]]++;
+  std::map<std::string, std::string> pair_done[2];  // SSA value -> suffix of its pair
   std::string reg_name[JX_TAPE_MAX_REGS];
   for (int i = 0; i < t->n_in; ++i) reg_name[i] = "x" + std::to_string(i) + "[v]";
   int next = 0;
@@ -230,16 +306,20 @@ std::string codegen(const jx_tape* t) {
     }
     const std::string nm = "t" + std::to_string(next++);
     std::string rhs;
-    const bool sig = op == JX_OP_UNARY + JX_UN_SIGMOID, th = op == JX_OP_UNARY + JX_UN_TANH;
-    if ((sig || th) && sig_of.count(src_name[i]) && tanh_of.count(src_name[i])) {
-      auto it = pair_done.find(src_name[i]);
-      if (it == pair_done.end()) {
-        const std::string k = std::to_string(pair_done.size());
-        s += "      float sg_" + k + ", th_" + k + ";\n      jxm::sigmoid_tanh(" + src_name[i] + ", sg_" + k + ", th_" + k +
+    int pk = -1, pm = -1;
+    for (int k = 0; k < 2; ++k)
+      for (int m = 0; m < 2; ++m)
+        if (op == pair_op[k][m] && seen[k][0].count(src_name[i]) && seen[k][1].count(src_name[i])) pk = k, pm = m;
+    if (pk >= 0) {
+      auto it = pair_done[pk].find(src_name[i]);
+      if (it == pair_done[pk].end()) {
+        const std::string k = std::to_string(pair_done[pk].size());
+        const std::string a = pair_pre[pk][0] + k, b = pair_pre[pk][1] + k;
+        s += "      float " + a + ", " + b + ";\n      jxm::" + pair_fn[pk] + "(" + src_name[i] + ", " + a + ", " + b +
              ");\n";
-        it = pair_done.emplace(src_name[i], k).first;
+        it = pair_done[pk].emplace(src_name[i], k).first;
       }
-      rhs = (sig ? "sg_" : "th_") + it->second;
+      rhs = pair_pre[pk][pm] + it->second;
     } else if (op == JX_OP_CONST) {
       rhs = "p.k[" + std::to_string(c.z) + "]";
     } else if (op == JX_OP_SELECT_GT) {
@@ -334,6 +414,7 @@ int jx_tape_create(const int32_t* code, int n_instr, const float* consts, int n_
     t->code.push_back(make_int4(code[4 * i], code[4 * i + 1], code[4 * i + 2], code[4 * i + 3]));
   std::vector<float> kv;
   for (int i = 0; i < n_consts; ++i) kv.push_back(consts[i]);
+  jx::fold_constants(t->code, kv);
   jx::rewrite_pow2_division(t->code, kv);
   t->n_consts = (int)kv.size();
   for (size_t i = 0; i < kv.size(); ++i) t->consts[i] = kv[i];

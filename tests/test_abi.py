@@ -101,6 +101,33 @@ def test_tape_kernel_compiles_without_gpu(jx):
     t.check()
 
 
+def _folding_tape(jx):
+    """y0 = x * -(1/3) (constant-only recip and neg: folded on the host);
+    y1 = x + sqrt(-1) (NaN result: left on the device)."""
+    U, B = jx.OP_UNARY, jx.OP_BINARY
+    code = [(jx.OP_CONST, 1, 0, 0), (U + jx.UN["recip"], 2, 1, 0), (U + jx.UN["neg"], 3, 2, 0),
+            (B + jx.BIN["mul"], 4, 0, 3), (jx.OP_CONST, 5, 1, 0), (U + jx.UN["sqrt"], 6, 5, 0),
+            (B + jx.BIN["add"], 7, 0, 6), (jx.OP_STORE, 0, 4, 0), (jx.OP_STORE, 1, 7, 0)]
+    return jx.Tape(code, [3.0, -1.0], 1, 2)
+
+
+def test_constant_subexpressions_fold(jx):
+    src = _folding_tape(jx).source()
+    assert "unary_t<8>" not in src and "unary_t<0>" not in src  # recip and neg of constants folded
+    assert "unary_t<7>" in src  # sqrt(-1) is NaN: stays on the device
+
+
+def test_value_and_grad_shares_gelu_exponential(jx):
+    """gelu and its derivative of one value come from one jxm::gelu_pair."""
+    import importlib
+    tr = importlib.import_module("jax-rs_b200.trace")
+    prog = tr.value_and_grad(lambda x: tr.gelu(x * 1.1 + 0.9) * tr.sigmoid(x) - tr.tanh(x) / 2, 1)
+    src = prog.tape_source(0)
+    assert src.count("jxm::gelu_pair(") == 1 and src.count("jxm::sigmoid_tanh(") == 1
+    assert "unary_t<11>" not in src and "unary_t<13>" not in src
+    assert "unary_t<8>" not in src  # the constant reciprocal of the division's VJP is folded
+
+
 def test_every_op_compiles(jx):
     """One tape touching every unary and binary op, in both operand orders."""
     code = [(jx.OP_CONST, 2, 0, 0)]

@@ -259,6 +259,18 @@ def test_div_by_power_of_two_constant_is_exact(jx, dev, oracle):
         assert np.array_equal(dev.get(Y), (x / np.float32(c)).astype(np.float32))
 
 
+def test_folded_constants_give_the_device_bits(jx, dev):
+    """A constant subexpression folded on the host (-(1/3)) gives the bits the
+    device's own IEEE ops give; a NaN constant result stays on the device."""
+    from test_abi import _folding_tape
+    tape = _folding_tape(jx)
+    x = np.random.default_rng(2).standard_normal(4099).astype(np.float32) * 100
+    X, Y0, Y1 = dev.put(x), dev.full(x.shape, 7.0), dev.full(x.shape, 7.0)
+    tape.run([X.data_ptr()], [Y0.data_ptr(), Y1.data_ptr()], x.size, dev.stream)
+    assert np.array_equal(dev.get(Y0), x * -(np.float32(1) / np.float32(3)))
+    assert np.isnan(dev.get(Y1)).all()
+
+
 MORE_UNARY = {  # op -> (domain lo, hi, exact)
     "sign": (-3, 3, True), "ceil": (-50, 50, True), "floor": (-50, 50, True), "round": (-50, 50, True),
     "trunc": (-50, 50, True), "tan": (-1.4, 1.4, False), "sinh": (-20, 20, False), "cosh": (-20, 20, False),
