@@ -934,7 +934,7 @@ def run_fft(args, dist, jx, torch):
         torch.cuda.synchronize()
         row_ms = e0.elapsed_time(e1) / args.steps
         kern_ms = max(ms - row_ms, 1e-6)
-        kern, kern_note = "fft1024_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
+        kern, kern_note = "fft1024_tma_kernel (column pass)", f"row pass {row_ms:.4f} ms, column pass {kern_ms:.4f} ms"
     hbm, _, basis = load_peaks()
     kgbs = nbytes / (kern_ms * 1e-3) / 1e9
     # e2e through the host-buffer FFT entry points: blocks of transforms go up,

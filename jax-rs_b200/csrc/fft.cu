@@ -14,11 +14,14 @@
 // touches shared memory only twice.  Twiddles exp(-2 pi i t/n) come from a
 // per-size table computed in double precision.  Columns of a 2-D transform
 // run the same kernel with 8 adjacent columns per CTA, so every global
-// access is a 64-byte row segment.
+// access is a 64-byte row segment; 1024-row columns have their own kernel
+// (32 x 32 in registers, tiles landed by TMA).
 #include <math.h>
 
 #include <mutex>
 #include <vector>
+
+#include <cudaTypedefs.h>
 
 #include "jx_common.cuh"
 
@@ -376,6 +379,158 @@ __global__ void __launch_bounds__(32 * F32_C, 16 / F32_C)
   }
 }
 
+// Column pass through TMA.  A tile is 8 adjacent columns of one 1024-row
+// matrix (1024 rows x 64 bytes); one CTA transforms one tile.  Its first
+// thread brings the tile into shared memory with four 256-row TMA boxes on
+// one mbarrier; a thread then reads its 32 points from the buffer (row
+// q + 32 n1 of column c), does the inner 32-point DFT and the twiddles (ten
+// table entries, products of W^(q b) and W^(8 q a)), the 32 x 32 transpose
+// goes through the same buffer in the padded layout of fft1024_kernel, and
+// the outer DFT's results are written back into the buffer as a row-major
+// tile that four TMA boxes store.  The copy engine takes the 64 global loads
+// and stores a thread issued in fft1024_kernel, and two CTAs share an SM
+// (66 KB of shared memory each), so one CTA's copies overlap the other's
+// transforms.  The wait on the load is bounded (about 4 s of wall clock); on
+// expiry the device error word gets JX_DEVERR_TIMEOUT and the CTA stops.
+constexpr int FT_THREADS = 32 * F32_C;
+constexpr int FT_ROWS_PER_BOX = 256;
+constexpr unsigned FT_TILE_BYTES = 1024u * F32_C * 8u;                                  // 64 KB landed per tile
+constexpr unsigned FT_BUF_BYTES = (unsigned)(F32_C * F32_RS * 8 + 127) / 128u * 128u;  // the padded transpose
+constexpr size_t FT_SMEM = (size_t)FT_BUF_BYTES + 128 + 16;                             // + alignment + mbarrier
+
+__device__ __forceinline__ uint64_t ft_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool ft_wait(uint64_t* bar, uint32_t parity) {
+  if (jxd::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ft_ns();
+  while (true) {
+    for (int i = 0; i < 256; ++i)
+      if (jxd::mbar_try_wait(bar, parity)) return true;
+    if (ft_ns() - t0 > 4000000000ull) return false;
+  }
+}
+
+// TMA store of a shared-memory box (no multicast), and the wait until the
+// copy engine has read the box out of shared memory.
+__device__ __forceinline__ void ft_store_3d(const void* tmap, const void* smem_src, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+               "r"(jxd::smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void ft_store_commit_and_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+template <bool INV>
+__global__ void __launch_bounds__(FT_THREADS, 2)
+    fft1024_tma_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ CUtensorMap map_out,
+                       long long tiles_per_mat, const float2* __restrict__ tw, float scale, unsigned* err) {
+  extern __shared__ uint8_t ft_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ft_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + FT_BUF_BYTES);
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  const int c = lane % F32_C;                     // column within the tile
+  const int q = wp * (32 / F32_C) + lane / F32_C;  // n2, then k1
+  const long long tile = blockIdx.x;
+  const long long b = tile / tiles_per_mat, cb = tile % tiles_per_mat;
+  if (tid == 0) {
+    jxd::mbar_init(full, 1);
+    jxd::fence_mbar_init();
+    jxd::mbar_arrive_expect_tx(full, FT_TILE_BYTES);
+#pragma unroll
+    for (int k = 0; k < 1024 / FT_ROWS_PER_BOX; ++k)
+      jxd::tma_load_3d(base + k * (FT_ROWS_PER_BOX * F32_C * 8), &map, full, (int32_t)(cb * 2 * F32_C),
+                       k * FT_ROWS_PER_BOX, (int32_t)b);
+  }
+  __syncthreads();
+  const bool ok = ft_wait(full, 0);
+  if (!__syncthreads_and(ok)) {
+    if (tid == 0) atomicOr(err, JX_DEVERR_TIMEOUT);
+    return;
+  }
+  const cf2* T = reinterpret_cast<const cf2*>(base);
+  cf2 v[32];
+#pragma unroll
+  for (int n1 = 0; n1 < 32; ++n1) v[n1] = T[(q + 32 * n1) * F32_C + c];
+  dft32<INV>(v);  // v[k1] = Y[n2 = q][k1]
+  {
+    // W^(q k1) for k1 = 8a + b as W^(q b) W^(8 q a): ten table entries and at
+    // most one complex product each, instead of 31 global loads
+    cf2 lo[8], hi[4];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) {
+      const float2 t = __ldg(tw + ((q * j) & 1023));
+      lo[j] = {t.x, INV ? -t.y : t.y};
+    }
+#pragma unroll
+    for (int a = 1; a < 4; ++a) {
+      const float2 t = __ldg(tw + ((q * 8 * a) & 1023));
+      hi[a] = {t.x, INV ? -t.y : t.y};
+    }
+#pragma unroll
+    for (int k1 = 1; k1 < 32; ++k1) {
+      const int a = k1 >> 3, bb = k1 & 7;
+      const cf2 wv = a == 0 ? lo[bb] : (bb == 0 ? hi[a] : cmul(lo[bb], hi[a]));
+      v[k1] = cmul(v[k1], wv);
+    }
+  }
+  __syncthreads();  // every thread has its points: the buffer takes the transpose
+  cf2* Sc = reinterpret_cast<cf2*>(base) + c * F32_RS;
+#pragma unroll
+  for (int k1 = 0; k1 < 32; ++k1) Sc[k1 * F32_KS + q] = v[k1];
+  __syncthreads();
+#pragma unroll
+  for (int n2 = 0; n2 < 32; ++n2) v[n2] = Sc[q * F32_KS + n2];  // now q = k1
+  dft32<INV>(v);  // v[k2] = X[q + 32 k2]
+  __syncthreads();  // the transpose is read: the buffer takes the output tile
+  cf2* R = reinterpret_cast<cf2*>(base);
+#pragma unroll
+  for (int k2 = 0; k2 < 32; ++k2) R[(q + 32 * k2) * F32_C + c] = {v[k2].x * scale, v[k2].y * scale};
+  jxd::fence_proxy_async_smem();  // this thread's writes, visible to the copy engine
+  __syncthreads();
+  if (tid == 0) {
+#pragma unroll
+    for (int k = 0; k < 1024 / FT_ROWS_PER_BOX; ++k)
+      ft_store_3d(&map_out, base + k * (FT_ROWS_PER_BOX * F32_C * 8), (int32_t)(cb * 2 * F32_C), k * FT_ROWS_PER_BOX,
+                  (int32_t)b);
+    ft_store_commit_and_wait_read();  // the buffer must outlive the copy's reads
+  }
+}
+
+// Eligible when the tensor map can describe the columns: 16-byte aligned
+// input, whole 8-column tiles (w % 8 == 0), matrices 16-byte strided.
+bool fft1024_tma_ok(const float2* in, const float2* out, long long w, long long hw, long long ntrans) {
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) || w % F32_C ||
+      (hw * 8) % 16 || w <= 0)
+    return false;
+  const long long mats = ntrans / w;
+  return ntrans % w == 0 && mats < (1LL << 31) && 2 * w < (1LL << 31);
+}
+
+int launch_fft1024_tma(const float2* in, float2* out, long long ntrans, long long w, long long hw, bool inv,
+                       float scale, cudaStream_t st) {
+  const float2* tw = nullptr;
+  if (int rc = twiddles(10, &tw)) return rc;
+  CUtensorMap map, map_out;
+  const uint64_t dims[3] = {(uint64_t)(2 * w), 1024, (uint64_t)(ntrans / w)};
+  const uint64_t strides[2] = {(uint64_t)w * 8, (uint64_t)hw * 8};
+  const uint32_t box[3] = {2 * F32_C, FT_ROWS_PER_BOX, 1};
+  if (int rc = jx::tensor_map_f32_3d(&map, in, dims, strides, box)) return rc;
+  if (int rc = jx::tensor_map_f32_3d(&map_out, out, dims, strides, box)) return rc;
+  const long long tiles_per_mat = w / F32_C, ntiles = ntrans / F32_C;
+  if (ntiles == 0) return JX_OK;
+  JX_REQUIRE(ntiles < (1LL << 31), "fft: batch too large");
+  auto k = inv ? fft1024_tma_kernel<true> : fft1024_tma_kernel<false>;
+  JX_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FT_SMEM));
+  k<<<(unsigned)ntiles, FT_THREADS, FT_SMEM, st>>>(map, map_out, tiles_per_mat, tw, scale, jx::device_error_word());
+  JX_LAUNCH_CHECK("fft1024_tma_kernel");
+  return JX_OK;
+}
+
 template <bool COLS>
 int launch_fft1024(const float2* in, float2* out, long long ntrans, Addr<COLS> ad, bool inv, float scale,
                    cudaStream_t st) {
@@ -429,6 +584,7 @@ int dispatch_size(const float2* in, float2* out, long long ntrans, bool cols, lo
   }
   Addr<true> ad{N, w, hw, 0};
   if constexpr (LOGN == 10) {
+    if (fft1024_tma_ok(in, out, w, hw, ntrans)) return launch_fft1024_tma(in, out, ntrans, w, hw, inv, scale, st);
     if (w % F32_C == 0) return launch_fft1024<true>(in, out, ntrans, ad, inv, scale, st);
   }
   if constexpr (N <= 1024) {

@@ -715,6 +715,13 @@ int gemm_make_kmajor_map(CUtensorMap* map, const float* base, int Kp, int rows, 
   int rc = get_encode();
   return rc ? rc : make_kmajor_map(map, base, Kp, rows, batch, box_rows);
 }
+
+int tensor_map_f32_3d(CUtensorMap_st* map, const void* base, const uint64_t* dims, const uint64_t* strides,
+                      const uint32_t* box) {
+  int rc = get_encode();
+  return rc ? rc : make_map_3d(map, static_cast<const float*>(base), dims[0], dims[1], dims[2], strides[0],
+                               strides[1], box[0], box[1], CU_TENSOR_MAP_SWIZZLE_NONE);
+}
 }  // namespace jx
 
 extern "C" {

@@ -58,6 +58,14 @@ unsigned int* device_error_word();
 
 }  // namespace jx
 
+struct CUtensorMap_st;
+namespace jx {
+// 3-D f32 TMA descriptor without swizzle: dims {d0 (contiguous), d1, d2},
+// byte strides {s1, s2}, box {b0, b1, 1}.
+int tensor_map_f32_3d(CUtensorMap_st* map, const void* base, const uint64_t* dims, const uint64_t* strides,
+                      const uint32_t* box);
+}  // namespace jx
+
 // Device error codes recorded in the device error word (bit flags).
 #define JX_DEVERR_NAN 0x1u
 #define JX_DEVERR_TIMEOUT 0x2u

@@ -53,7 +53,8 @@ def test_in_place(jx, dev, oracle):
 
 
 @pytest.mark.parametrize("h,w,batch", [(4, 4, 1), (8, 32, 3), (32, 8, 2), (64, 64, 5), (16, 1024, 1),
-                                       (1024, 16, 1), (2, 2, 7), (1, 8, 2)])
+                                       (1024, 16, 1), (2, 2, 7), (1, 8, 2), (1024, 8, 3), (1024, 32, 3),
+                                       (1024, 4, 2)])
 @pytest.mark.parametrize("inverse", [False, True])
 def test_fft2_vs_oracle(jx, dev, oracle, h, w, batch, inverse):
     x = _cplx(np.random.default_rng(h * w), (batch, h, w))
@@ -84,6 +85,21 @@ def test_fft2_1024_square(jx, dev, oracle):
     z = x[..., 0].astype(np.float64) + 1j * x[..., 1]
     r = np.fft.fft2(z)
     assert normwise_rel(y, np.stack([r.real, r.imag], -1)) <= 1e-5
+
+
+def test_fft2_1024_in_place_batch5(jx, dev):
+    """5 x 1024 x 1024 in place (640 column tiles of the TMA column pass, more
+    than the SMs hold at once) against a float64 FFT; the inverse brings x
+    back."""
+    x = _cplx(np.random.default_rng(12), (5, 1024, 1024))
+    X = dev.put(x)
+    jx.fft2_c2c(X.data_ptr(), X.data_ptr(), 1024, 1024, 5, False, dev.stream)
+    y = dev.get(X)
+    z = x[..., 0].astype(np.float64) + 1j * x[..., 1]
+    r = np.fft.fft2(z)
+    assert normwise_rel(y, np.stack([r.real, r.imag], -1)) <= 1e-5
+    jx.fft2_c2c(X.data_ptr(), X.data_ptr(), 1024, 1024, 5, True, dev.stream)
+    assert normwise_rel(dev.get(X), x) <= 1e-5
 
 
 def test_full_config_1d_properties(jx, dev, oracle):
