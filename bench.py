@@ -71,7 +71,7 @@ TRAFFIC = {
     "argmax": 1.0738e9 + 0.0033e9,           # argreduce_rows_kernel<max>
     "fullsum": 1.0738e9 + 0.0049e9,          # reduce_all_pass1<sum>
     "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
-    "fft2d": 8 * (0.2685e9 + 0.2162e9),      # column pass fft1024_kernel, batch 32 x 8
+    "fft2d": 8 * (0.2685e9 + 0.2158e9),      # column pass fft1024_tma_kernel, batch 32 x 8
     "conv": 2 * (0.1082e9 + 0.0551e9 + 0.1079e9 + 0.0530e9 + 0.3201e9 + 0.0709e9),  # 3 conv_gemm_kernel, B 32 x 2
     "bgemm": 2.2020e9 + 1.0442e9,            # gemm_fused_split_kernel, [64,2048,2048]^2
     "pool": 0.8228e9 + 0.1918e9,             # pool2d_kernel<max,3,3>, [64,256,112,112]
