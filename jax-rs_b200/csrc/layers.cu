@@ -551,9 +551,9 @@ __global__ void __launch_bounds__(256) norm_apply(const float* __restrict__ x, f
         r.y = norm1<AFFINE>(v[k].y, m, g, b);
         r.z = norm1<AFFINE>(v[k].z, m, g, b);
         r.w = norm1<AFFINE>(v[k].w, m, g, b);
-        __stcs(reinterpret_cast<float4*>(y) + u, r);
+        reinterpret_cast<float4*>(y)[u] = r;
       } else {
-        __stcs(y + u, norm1<AFFINE>(v[k].x, m, g, b));
+        y[u] = norm1<AFFINE>(v[k].x, m, g, b);
       }
     }
   }
