@@ -67,6 +67,7 @@ struct Conv1dArgs {
   long long B, C, L, O, K, S, P, OL, Opad;
   int icc, xw;
   int buf_floats;  // one of the two shared-memory buffers: icc*K*64 taps + icc*xw inputs, padded to 4
+  float one;       // 1.0, a kernel argument so that the compiler cannot fold it
 };
 
 // w [O][C][K] -> wt [C*K][Opad] (Opad = O rounded up to the 64-channel tile).
@@ -80,10 +81,30 @@ __global__ void __launch_bounds__(256) conv1d_filter_kernel(const float* __restr
   }
 }
 
+// acc.{x,y} = rn(rn(x * w.{x,y}) + acc.{x,y}) with packed f32x2 operations:
+// one mul.f32x2 and one fma.f32x2 for two multiply-adds, half the
+// instructions of the scalar FMUL + FADD pairs.  The add is an FMA by a
+// run-time 1.0 that the compiler cannot see, so the product keeps its own
+// rounding (a plain add.f32x2 after the mul.f32x2 is contracted into one
+// fma.f32x2 even under --fmad=false, which is 1 ulp off the reference's
+// separately rounded multiply and add).
+__device__ __forceinline__ void mac2(float2& acc, float x, float2 w, float one) {
+  asm("{\n\t.reg .b64 xa, wa, ca, oa, pa;\n\t"
+      "mov.b64 xa, {%2, %2};\n\t"
+      "mov.b64 wa, {%3, %4};\n\t"
+      "mov.b64 ca, {%0, %1};\n\t"
+      "mov.b64 oa, {%5, %5};\n\t"
+      "mul.rn.f32x2 pa, xa, wa;\n\t"
+      "fma.rn.f32x2 ca, pa, oa, ca;\n\t"
+      "mov.b64 {%0, %1}, ca;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "f"(x), "f"(w.x), "f"(w.y), "f"(one));
+}
+
 template <int SS, int KK, bool CHECKED>
 __device__ __forceinline__ void conv1d_chunk(const float* __restrict__ xs, const float* __restrict__ ws,
                                              float (&acc)[8][C1_NJ], int nic, int K_rt, int S_rt, int xw, int og,
-                                             int lane, long long in0, long long L) {
+                                             int lane, long long in0, long long L, float one) {
   const int S = SS > 0 ? SS : S_rt;
   const int K = KK > 0 ? KK : K_rt;
   for (int ic = 0; ic < nic; ++ic) {
@@ -102,7 +123,12 @@ __device__ __forceinline__ void conv1d_chunk(const float* __restrict__ xs, const
         }
         const float xv = xr[32 * j * S + k];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) acc[r][j] = __fadd_rn(acc[r][j], __fmul_rn(xv, wv[r]));
+        for (int r = 0; r < 8; r += 2) {
+          float2 a2 = make_float2(acc[r][j], acc[r + 1][j]);
+          mac2(a2, xv, make_float2(wv[r], wv[r + 1]), one);
+          acc[r][j] = a2.x;
+          acc[r + 1][j] = a2.y;
+        }
       }
     }
   }
@@ -181,9 +207,9 @@ __global__ void __launch_bounds__(C1_THREADS) conv1d_kernel(Conv1dArgs a) {
     const float* ws = c1_smem + (size_t)buf * a.buf_floats;
     const float* xs = ws + (size_t)a.icc * a.K * C1_OC;
     if (warp_interior)
-      conv1d_chunk<SS, KK, false>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
+      conv1d_chunk<SS, KK, false>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L, a.one);
     else
-      conv1d_chunk<SS, KK, true>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L);
+      conv1d_chunk<SS, KK, true>(xs, ws, acc, nic, K, S, a.xw, og, lane, in0, a.L, a.one);
     __syncthreads();  // done with this buffer before it is refilled
   }
 
@@ -590,6 +616,7 @@ int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64
   a.S = stride;
   a.P = padding;
   a.OL = OL;
+  a.one = 1.0f;
   a.xw = (int)((C1_POS - 1) * stride + kernel_len);
   const long long per_ic = (long long)kernel_len * C1_OC + a.xw;  // floats per input channel of a chunk
   const long long budget = 48 * 1024 / 4;                          // floats per buffer
