@@ -91,12 +91,13 @@ def traffic_for(args):
     return TRAFFIC.get(args.workload) if default else None
 
 
-def load_peaks(clocks=None):
-    """(HBM GB/s, bf16 TFLOP/s, basis).  The bf16 figure is the burst one,
-    or the sustained one when `clocks` shows the power cap active during the
-    timed region (a kernel that ran long enough to hit the cap is compared
-    with the GEMM throughput under the same cap)."""
-    capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or [])
+def load_peaks(clocks=None, timed_ms=0.0):
+    """(HBM GB/s, bf16 TFLOP/s, basis).  The bf16 figure is the burst one
+    (the profiling recipe's denominator for a kernel timed on its own), or
+    the sustained one when the timed region ran for a second or more with
+    the power cap active: a loop that long settles at the capped clock the
+    sustained figure was measured at."""
+    capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and timed_ms >= 1000.0
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             pk = json.load(f)
@@ -105,6 +106,18 @@ def load_peaks(clocks=None):
         return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
     except Exception:
         return 6650.0, (1400.0 if capped else 1590.0), "fallback"
+
+
+def at_run_clock(achieved, peak, clocks):
+    """achieved / (peak scaled by the median SM clock of the timed region
+    over the maximum SM clock), or None without clock samples.  Shows how
+    close a tensor-bound kernel came to the peak at the clock it actually
+    ran at (a power-capped box runs below the clock the peak was measured
+    at)."""
+    mhz, mx = (clocks or {}).get("sm_mhz"), (clocks or {}).get("sm_max_mhz")
+    if not mhz or not mx:
+        return None
+    return round(achieved / (peak * float(mhz) / float(mx)), 4)
 
 
 class ClockSampler:
@@ -463,7 +476,7 @@ def run_sgemm(args, dist, jx, torch):
     e2e_ms = dist.max(e0.elapsed_time(e1) / args.e2e_steps)
     e2e_val = flops_rank * dist.world / (e2e_ms * 1e-3) / 1e12
 
-    hbm, bf16, basis = load_peaks(clocks)
+    hbm, bf16, basis = load_peaks(clocks, ms_max * args.steps)
     peak = bf16 / 2.0 / 3.0  # tf32 issues at half the bf16 rate; 3xTF32 needs 3 MMAs per f32 product
     achieved = flops_rank / (kern_ms * 1e-3) / 1e12
     line = {
@@ -478,6 +491,7 @@ def run_sgemm(args, dist, jx, torch):
         "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
                      "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
+                     "frac_at_run_clock": at_run_clock(achieved, peak, clocks),
                      "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
                 "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
@@ -730,7 +744,7 @@ def run_conv_bgemm(args, dist, jx, torch):
     ms = dist.max(e0.elapsed_time(e1) / args.steps)
     clocks = clk.stop()
     tf = flops * dist.world / (ms * 1e-3) / 1e12
-    _, bf16, basis = load_peaks(clocks)
+    _, bf16, basis = load_peaks(clocks, ms * args.steps)
     peak = bf16 / 2.0 / 3.0
     if args.workload == "conv":
         e_ms, e_in, e_out = measure_e2e(jx, torch, dist, st, [X, Wt, G], [Y, DX, DW], step, args.e2e_steps)
@@ -752,6 +766,7 @@ def run_conv_bgemm(args, dist, jx, torch):
                                     if args.workload == "conv" else "gemm_fused_split_kernel (whole batched call)"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
+                         "frac_at_run_clock": at_run_clock(tf / dist.world, peak, clocks),
                          "traffic": traffic_for(args)},
             "e2e": {"value": round(flops * dist.world / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
@@ -1088,7 +1103,7 @@ def run_mlp(args, dist, jx, torch):
     flops = 0.0
     for l in range(len(widths) - 1):
         flops += 3 * 2.0 * batch * widths[l] * widths[l + 1]  # fwd + dX + dW GEMMs
-    _, bf16, basis = load_peaks(clocks)
+    _, bf16, basis = load_peaks(clocks, ms * args.steps)
     peak = bf16 / 2.0 / 3.0
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": dist.world, "steps": args.steps,
@@ -1105,6 +1120,7 @@ def run_mlp(args, dist, jx, torch):
                      "achieved": round(flops / (ms * 1e-3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)",
+                     "frac_at_run_clock": at_run_clock(flops / (ms * 1e-3) / 1e12, peak, clocks),
                      "traffic": None if wide else traffic_for(args),
                      "note": ("exact f32 (sequential-k, unfused): the whole step is one cooperative kernel "
                               "with grid barriers between its phases; the tensor peak is quoted for scale")
