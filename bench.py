@@ -95,9 +95,13 @@ def load_peaks(clocks=None, timed_ms=0.0):
     """(HBM GB/s, bf16 TFLOP/s, basis).  The bf16 figure is the burst one
     (the profiling recipe's denominator for a kernel timed on its own), or
     the sustained one when the timed region ran for a second or more with
-    the power cap active: a loop that long settles at the capped clock the
-    sustained figure was measured at."""
-    capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or []) and timed_ms >= 1000.0
+    the power cap active and the SM clock held below 90% of its maximum: a
+    loop like that settles at the capped clock the sustained figure was
+    measured at.  (The cap flag alone is not enough: runs at full clock
+    report it too.)"""
+    c = clocks or {}
+    slow = bool(c.get("sm_mhz")) and bool(c.get("sm_max_mhz")) and c["sm_mhz"] < 0.9 * c["sm_max_mhz"]
+    capped = "sw_power_cap" in (c.get("reasons") or []) and slow and timed_ms >= 1000.0
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             pk = json.load(f)
@@ -108,16 +112,16 @@ def load_peaks(clocks=None, timed_ms=0.0):
         return 6650.0, (1400.0 if capped else 1590.0), "fallback"
 
 
-def at_run_clock(achieved, peak, clocks):
-    """achieved / (peak scaled by the median SM clock of the timed region
-    over the maximum SM clock), or None without clock samples.  Shows how
-    close a tensor-bound kernel came to the peak at the clock it actually
-    ran at (a power-capped box runs below the clock the peak was measured
-    at)."""
+def at_run_clock(achieved, clocks):
+    """achieved / (the burst 3xTF32 peak scaled by the timed region's median
+    SM clock over the maximum SM clock), or None without clock samples: how
+    close a tensor-bound kernel came to the peak at the clock it actually ran
+    at (a power-capped box runs below the clock the peak was measured at)."""
     mhz, mx = (clocks or {}).get("sm_mhz"), (clocks or {}).get("sm_max_mhz")
     if not mhz or not mx:
         return None
-    return round(achieved / (peak * float(mhz) / float(mx)), 4)
+    _, bf16, _ = load_peaks()
+    return round(achieved / (bf16 / 6.0 * float(mhz) / float(mx)), 4)
 
 
 class ClockSampler:
@@ -491,7 +495,7 @@ def run_sgemm(args, dist, jx, torch):
         "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
                      "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
-                     "frac_at_run_clock": at_run_clock(achieved, peak, clocks),
+                     "frac_at_run_clock": at_run_clock(achieved, clocks),
                      "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
                 "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
@@ -766,7 +770,7 @@ def run_conv_bgemm(args, dist, jx, torch):
                                     if args.workload == "conv" else "gemm_fused_split_kernel (whole batched call)"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
-                         "frac_at_run_clock": at_run_clock(tf / dist.world, peak, clocks),
+                         "frac_at_run_clock": at_run_clock(tf / dist.world, clocks),
                          "traffic": traffic_for(args)},
             "e2e": {"value": round(flops * dist.world / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
@@ -1120,7 +1124,7 @@ def run_mlp(args, dist, jx, torch):
                      "achieved": round(flops / (ms * 1e-3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)",
-                     "frac_at_run_clock": at_run_clock(flops / (ms * 1e-3) / 1e12, peak, clocks),
+                     "frac_at_run_clock": at_run_clock(flops / (ms * 1e-3) / 1e12, clocks),
                      "traffic": None if wide else traffic_for(args),
                      "note": ("exact f32 (sequential-k, unfused): the whole step is one cooperative kernel "
                               "with grid barriers between its phases; the tensor peak is quoted for scale")
