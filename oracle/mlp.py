@@ -1,7 +1,7 @@
 """MLP training restated with the oracle's C routines -- TEST INFRASTRUCTURE ONLY.
 
 The reference trains its MLP example (examples/mlp_training.rs:19-36,94-145)
-with finite differences and SGD; the north-star configuration asks for Adam.
+with finite differences and SGD; the 784-256-128-10 training workload runs Adam.
 This module composes the reference's own pieces in the order a jax-rs program
 would: Array::matmul (src/ops/linalg.rs:215-232), broadcast bias add
 (src/ops/manipulation.rs:919-946), nn::relu (src/nn.rs:22-26), per-row
