@@ -342,8 +342,27 @@ __global__ void __launch_bounds__(FS_THREADS, 2) mlp_fused_step_kernel(FusedStep
     }
   }
 
+  // Adam for parameter i with gradient gi (the separate kernel's formula).
+  const float2 rr = a.tab[t - 1];
+  const bool first = t == 1;
+  auto adam = [&](long long i, float gi) {
+    const float mi = first ? __fmul_rn(gi, a.omb1) : __fadd_rn(__fmul_rn(a.m[i], a.b1), __fmul_rn(gi, a.omb1));
+    const float g2 = __fmul_rn(gi, gi);
+    const float vi = first ? __fmul_rn(g2, a.omb2) : __fadd_rn(__fmul_rn(a.v[i], a.b2), __fmul_rn(g2, a.omb2));
+    const float mh = __fmul_rn(mi, rr.x);
+    const float vh = __fmul_rn(vi, rr.y);
+    a.params[i] = __fsub_rn(a.params[i], __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), a.eps)), a.lr));
+    a.m[i] = mi;
+    a.v[i] = vi;
+  };
+
   // ---- backward: dW_l = h_{l-1}^T dz, db_l = column sums of dz,
   //      dz_{l-1} = (dz W_l^T) * act'(pre_{l-1}) ----
+  // Adam needs no phase of its own.  Layer l + 1's parameters are updated
+  // during layer l's phase: W_{l+1} was last read by the previous phase,
+  // whose barrier has passed, and nothing reads it again.  Layer 1's are
+  // updated in the dW_1 tiles themselves (no later phase reads W_1), so the
+  // last phase ends the kernel without a barrier.
   float* dz = a.dzA;
   float* dzn = a.dzB;
   for (int l = a.L; l >= 1; --l) {
@@ -356,8 +375,20 @@ __global__ void __launch_bounds__(FS_THREADS, 2) mlp_fused_step_kernel(FusedStep
     const int tiles_h = l > 1 ? ((B + FS_T - 1) / FS_T) * ((K + FS_T - 1) / FS_T) : 0;
     for (int tile = blockIdx.x; tile < tiles_w + tiles_h; tile += gridDim.x) {
       if (tile < tiles_w) {
+        const long long wo = a.woff[l - 1];
         fs_tile<true, false>(
-            sm, tile, hin, dz, K, N, B, K, N, [&](int r, int c, float sum) { gW[(long long)r * N + c] = sum; }, gb);
+            sm, tile, hin, dz, K, N, B, K, N,
+            [&](int r, int c, float sum) {
+              gW[(long long)r * N + c] = sum;
+              if (l == 1) adam(wo + (long long)r * N + c, sum);
+            },
+            gb);
+        if (l == 1) {
+          // the bias gradient this thread's colsum wrote (first row of tiles, first row of threads)
+          const int tiles_n = (N + FS_T - 1) / FS_T;
+          const int c = (tile % tiles_n) * FS_T + (threadIdx.x & (FS_T - 1));
+          if (tile / tiles_n == 0 && threadIdx.x < FS_T && c < N) adam(a.boff[0] + c, gb[c]);
+        }
       } else {
         const float* pre = a.pre[l - 1];
         const int act = a.act[l - 2];
@@ -366,25 +397,20 @@ __global__ void __launch_bounds__(FS_THREADS, 2) mlp_fused_step_kernel(FusedStep
         });
       }
     }
+    if (l < a.L) {
+      // layer l + 1: its gradients are complete (previous phase)
+      const int Kn = a.w[l], Nn = a.w[l + 1];
+      const long long wo = a.woff[l], bo = a.boff[l], nw = (long long)Kn * Nn;
+      for (long long i = gtid; i < nw + Nn; i += gthreads) {
+        const long long p = i < nw ? wo + i : bo + (i - nw);
+        adam(p, __ldcg(a.grads + p));
+      }
+    }
+    if (l == 1) break;  // the last phase: no barrier, the kernel ends
     if (!fs_grid_sync(cnt, nbar++, a.err, &sm.ok)) return;
     float* tmp = dz;
     dz = dzn;
     dzn = tmp;
-  }
-
-  // ---- Adam over every parameter ----
-  const float2 rr = a.tab[t - 1];
-  const bool first = t == 1;
-  for (long long i = gtid; i < a.nparams; i += gthreads) {
-    const float gi = __ldcg(a.grads + i);
-    const float mi = first ? __fmul_rn(gi, a.omb1) : __fadd_rn(__fmul_rn(a.m[i], a.b1), __fmul_rn(gi, a.omb1));
-    const float g2 = __fmul_rn(gi, gi);
-    const float vi = first ? __fmul_rn(g2, a.omb2) : __fadd_rn(__fmul_rn(a.v[i], a.b2), __fmul_rn(g2, a.omb2));
-    const float mh = __fmul_rn(mi, rr.x);
-    const float vh = __fmul_rn(vi, rr.y);
-    a.params[i] = __fsub_rn(a.params[i], __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), a.eps)), a.lr));
-    a.m[i] = mi;
-    a.v[i] = vi;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *a.step = t + 1;
 }
