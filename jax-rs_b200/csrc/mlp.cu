@@ -59,7 +59,8 @@ __global__ void step_inc_kernel(int* step) { *step += 1; }
 // ---------------------------------------------------------------------------
 // Fused step (JX_PREC_EXACT, one GPU): forward, softmax cross-entropy,
 // backward and Adam in one cooperative launch instead of ~23 kernels.  Phases
-// are separated by a grid barrier (2L+1 of them); inside a phase every block
+// are separated by a grid barrier (2L of them; Adam runs inside the backward
+// phases); inside a phase every block
 // takes work items in a grid-stride loop.  The arithmetic is the separate
 // kernels' own: the exact GEMM's ascending-k unfused sums (one thread per
 // output of a 16 x 16 tile, K through a cp.async ring of 128-wide chunks),
