@@ -544,7 +544,7 @@ template <bool AFFINE, bool VEC, typename IDX>
 __global__ void __launch_bounds__(256) norm_apply(const float* __restrict__ x, float* __restrict__ y,
                                                   const float4* __restrict__ ms, const float* __restrict__ gamma,
                                                   const float* __restrict__ beta, long long n, long long C_,
-                                                  long long inner_) {
+                                                  long long inner_, unsigned in_m, int in_l, unsigned c_m, int c_l) {
   constexpr int U = 4;
   const IDX units = (IDX)(VEC ? n / 4 : n), C = (IDX)C_, inner = (IDX)inner_;
   const IDX nthreads = (IDX)gridDim.x * blockDim.x;
@@ -568,7 +568,13 @@ __global__ void __launch_bounds__(256) norm_apply(const float* __restrict__ x, f
       const IDX u = base + (IDX)k * nthreads;
       if (u >= units) continue;
       const IDX e = VEC ? u * 4 : u;
-      const IDX c = (e / inner) % C;
+      IDX c;
+      if constexpr (sizeof(IDX) == 4) {  // e < 2^31: channel by multiply-high divisions
+        const unsigned q = fast_div((unsigned)e, in_m, in_l);
+        c = (IDX)(q - fast_div(q, c_m, c_l) * (unsigned)C);
+      } else {
+        c = (e / inner) % C;
+      }
       const float4 m = ms[c];
       const float g = AFFINE ? __ldg(gamma + c) : 1.0f, b = AFFINE ? __ldg(beta + c) : 0.0f;
       if (VEC) {
@@ -786,12 +792,20 @@ int jx_batchnorm_f32(const float* x, const float* gamma, const float* beta, floa
                      (reinterpret_cast<uintptr_t>(y) & 15) == 0;
     const int grid = grid_for(vec ? n / 4 : n, 256, 8);
     const bool small = n + 4LL * 256 * grid < (1LL << 31);
-#define JX_NORM_APPLY(AFF, VEC)                                                                   \
-  do {                                                                                            \
-    if (small)                                                                                    \
-      norm_apply<AFF, VEC, unsigned><<<grid, 256, 0, st>>>(x, y, ms, gamma, beta, n, channels, spatial);  \
-    else                                                                                          \
-      norm_apply<AFF, VEC, long long><<<grid, 256, 0, st>>>(x, y, ms, gamma, beta, n, channels, spatial); \
+    unsigned in_m = 0, c_m = 0;
+    int in_l = 0, c_l = 0;
+    if (small) {
+      fast_div_params((unsigned)spatial, in_m, in_l);
+      fast_div_params((unsigned)channels, c_m, c_l);
+    }
+#define JX_NORM_APPLY(AFF, VEC)                                                                                 \
+  do {                                                                                                          \
+    if (small)                                                                                                  \
+      norm_apply<AFF, VEC, unsigned><<<grid, 256, 0, st>>>(x, y, ms, gamma, beta, n, channels, spatial, in_m, in_l, \
+                                                           c_m, c_l);                                          \
+    else                                                                                                        \
+      norm_apply<AFF, VEC, long long><<<grid, 256, 0, st>>>(x, y, ms, gamma, beta, n, channels, spatial, 0, 0, 0, \
+                                                            0);                                                 \
   } while (0)
     if (gamma) {
       if (vec)
