@@ -6,7 +6,9 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-SIZES = [1, 2, 31, 32, 1000, 262143, 262144, 262145, 1 << 20, 3_000_001]
+# around a thread's 2048-value range, a warp's 65536 and a block's 524288
+SIZES = [1, 2, 31, 32, 1000, 2047, 2048, 2049, 65535, 65536, 65537, 262143, 262144, 262145, 524287, 524289,
+         1 << 20, 3_000_001]
 
 
 def _key(oracle, seed):
