@@ -5,15 +5,22 @@ Default workload (the headline): f32 GEMM M=N=K=8192 through the C ABI
 (jx_gemm_f32, tcgen05 3xTF32), one GEMM per step.  With --gpus N each rank
 computes its own 8192-row shard of a (8192*N) x 8192 x 8192 product with a
 replica of B (M-row sharding, no collective), so per-GPU work is fixed: weak
-scaling.  Other workloads: --workload chain | rowsum | argmax | fullsum.
+scaling (--strong splits the rows of one --size^3 product instead).  The
+default line also carries `wide_mlp`: data-parallel training of the wide MLP
+(8192 -> 4 x 8192 GELU -> 1000, global batch 65536 split over the N ranks,
+NCCL gradient all-reduce per layer), timed in the same process.  Other
+workloads (--workload): chain, chain_grad, rng, rowsum, argmax, fullsum,
+sum_vjp, max_vjp, bgemm, conv, fft1d, fft2d (these four split their global
+batch over the ranks), mlp, wide_mlp, conv1d, pool, batchnorm.
 
 Timing: W warm-up steps, then exactly K steps between barrier +
 torch.cuda.synchronize(), CUDA events on the launching stream, max over
 ranks.  Operands are 256 MiB each (larger than the 126 MB L2).
 
 `--impl reference` times the reference's CPU implementation of the same
-workload (the oracle's C restatement of jax-rs's CPU loop, all host threads,
-a bounded row sample per step) and prints the same JSON line.
+workload (the oracle's C restatement of jax-rs's CPU loop on one host
+thread, as the single-threaded reference runs, a bounded row sample per
+step) and prints the same JSON line.
 """
 from __future__ import annotations
 
@@ -51,19 +58,25 @@ def parse():
     p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
     p.add_argument("--fft-batch", type=int, default=0, help="override the FFT batch (smaller cases for profiling)")
     p.add_argument("--conv-batch", type=int, default=0, help="override the conv batch (smaller cases for profiling)")
-    p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank")
+    p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank (with --strong: of the whole product)")
+    p.add_argument("--strong", action="store_true",
+                   help="sgemm: split the M rows of one size^3 product over the ranks (strong scaling) instead of "
+                        "giving every rank its own size-row shard")
+    p.add_argument("--no-wide-mlp", action="store_true",
+                   help="sgemm: skip the wide-MLP data-parallel measurement the default line carries")
+    p.add_argument("--wide-steps", type=int, default=8, help="timed steps of that wide-MLP measurement")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-rows", type=int, default=24, help="GEMM rows timed by the CPU baseline")
+    p.add_argument("--cpu-rows", type=int, default=8, help="GEMM rows timed by the CPU baseline")
     return p.parse_args()
 
 
 # DRAM bytes (read + write) per launch of each workload's dominant kernel at
 # the default size, from one ncu capture of dram__bytes_read.sum +
-# dram__bytes_write.sum (commands and figures: profiles/dram_traffic_by_kernel.md).
-# FFT and conv were captured on a smaller batch and scaled by the batch; their
-# traffic is proportional to it.  batchnorm sums its three kernels (the
-# roofline covers the whole call).  None for any other size.
+# dram__bytes_write.sum, taken once, not in this run.  FFT and conv were
+# captured on a smaller batch and scaled by the batch; their traffic is
+# proportional to it.  batchnorm sums its three kernels (the roofline covers
+# the whole call).  None for any other size.
 TRAFFIC = {
     "sgemm": 4.5905e9 + 0.2583e9,            # gemm_3xtf32_kernel, 8192^3
     "chain": 1.0738e9 + 1.0275e9,            # jx_tape_kernel, 2^28
@@ -84,11 +97,22 @@ TRAFFIC = {
 }
 
 
-def traffic_for(args):
-    default = (args.size == 8192 and not args.fft_batch and not args.conv_batch)
+TRAFFIC_BASIS = "ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the default size, not this run"
+BATCH_SPLIT = ("fft1d", "fft2d", "conv", "bgemm")  # workloads whose global batch splits over the ranks
+
+
+def traffic_for(args, world=1):
+    """Per-launch DRAM bytes of this rank's dominant kernel, or None.  Where
+    the global batch splits over the ranks, a rank's launch moves its share."""
+    default = (args.size == 8192 and not args.fft_batch and not args.conv_batch and not args.strong)
     if args.workload == "mlp" and args.precision not in (None, "exact"):
         return None  # the figure is the fused exact step's
-    return TRAFFIC.get(args.workload) if default else None
+    t = TRAFFIC.get(args.workload) if default else None
+    if t is not None and args.workload in BATCH_SPLIT:
+        t /= world
+    elif t is not None and world > 1 and args.workload != "sgemm":
+        return None
+    return t
 
 
 def load_peaks(clocks=None, timed_ms=0.0):
@@ -215,6 +239,13 @@ class Dist:
         if self.pg:
             self.pg.barrier()
             self.pg.destroy_process_group()
+
+
+def shard(global_n, dist, what):
+    """This rank's share of a global count that splits evenly over the ranks."""
+    if global_n % dist.world:
+        raise SystemExit(f"{what} {global_n} does not split evenly over {dist.world} ranks")
+    return global_n // dist.world
 
 
 # ---------------------------------------------------------------------------
@@ -404,7 +435,8 @@ def measure_e2e(jx, torch, dist, st, inputs, outputs, step, steps):
 # our arm
 # ---------------------------------------------------------------------------
 def run_sgemm(args, dist, jx, torch):
-    M = N = K = args.size
+    N = K = args.size
+    M = shard(args.size, dist, "sgemm rows") if args.strong else args.size
     dev = torch.device("cuda", dist.local)
     st = torch.cuda.current_stream()
     s = st.cuda_stream
@@ -486,17 +518,18 @@ def run_sgemm(args, dist, jx, torch):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic U(-1,1) operands (torch generator, seed 1)",
+        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic U(-1,1) operands (torch generator, seed 1)",
         "config": {"workload": f"sgemm {M}x{N}x{K} f32 per rank (M-row shard of a {M * dist.world}x{N}x{K} "
                                f"product, B replicated), JX_PREC_3XTF32",
                    "global_batch": None, "seq_len": None, "parallelism": f"M-row shards x{dist.world}, no collective",
-                   "l2": "operands 256 MiB each > 126 MB L2; no flush needed"},
+                   "l2": f"operands {M * K * 4 / 2**20:.0f} and {K * N * 4 / 2**20:.0f} MiB; "
+                         + ("> 126 MB L2, no flush needed" if M * K * 4 > 126e6 else "B re-read from L2 across steps")},
         "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
                      "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
                      "frac_at_run_clock": at_run_clock(achieved, clocks),
-                     "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4)},
+                     "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS, "kernel_ms": round(kern_ms, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
                 "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": 3 * args.steps,
@@ -576,7 +609,7 @@ def run_chain(args, dist, jx, torch):
                        "l2": "1 GiB in + 1 GiB out > L2", "bytes_per_element": 12 if grad else 8},
             "roofline": {"bound": "hbm", "kernel": "jx_tape_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
-                         "peak_basis": basis, "traffic": traffic_for(args)},
+                         "peak_basis": basis, "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS},
             "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps, "clocks": clocks}
@@ -620,7 +653,7 @@ def run_rng(args, dist, jx, torch):
                        "l2": "1 GiB out > L2"},
             "roofline": {"bound": "hbm", "kernel": "rng_kernel", "achieved": round(gbs / dist.world, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4),
-                         "peak_basis": basis, "traffic": traffic_for(args)},
+                         "peak_basis": basis, "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS},
             "e2e": {"value": round(bytes_step * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps, "clocks": clocks}
@@ -696,7 +729,7 @@ def run_reduce(args, dist, jx, torch):
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(gbs / dist.world, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(gbs / dist.world / hbm, 4), "peak_basis": basis,
-                         "traffic": traffic_for(args)},
+                         "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS},
             "gpu_launches": args.steps * (2 if args.workload == "fullsum" else 1), "clocks": clocks}
 
 
@@ -709,7 +742,8 @@ def run_conv_bgemm(args, dist, jx, torch):
     g = torch.Generator(device=dev)
     g.manual_seed(3 + dist.rank)
     if args.workload == "conv":
-        B, C, H, W, O, K = args.conv_batch or 64, 256, 56, 56, 256, 3
+        Bg = args.conv_batch or 64  # global batch, split over the ranks
+        B, C, H, W, O, K = shard(Bg, dist, "conv batch"), 256, 56, 56, 256, 3
         geo = (B, C, H, W, O, K, K, 1, 1)
         X = torch.randn((B, C, H, W), device=dev, generator=g)
         Wt = torch.randn((O, C, K, K), device=dev, generator=g) * float(np.sqrt(2.0 / (C * K * K)))
@@ -721,9 +755,10 @@ def run_conv_bgemm(args, dist, jx, torch):
             jx.call("jx_conv2d_bwd_data_f32", G.data_ptr(), Wt.data_ptr(), DX.data_ptr(), *geo, s)
             jx.call("jx_conv2d_bwd_filter_f32", X.data_ptr(), G.data_ptr(), DW.data_ptr(), *geo, s)
         flops = 3 * 2.0 * B * O * C * K * K * H * W
-        wl = f"conv2d [{B},256,56,56] x [256,256,3,3] s1 p1: forward + input grad + weight grad per step"
+        wl = (f"conv2d [{Bg},256,56,56] x [256,256,3,3] s1 p1: forward + input grad + weight grad per step, "
+              f"{B} images per rank (per-rank weight-gradient partials, no collective)")
     else:
-        nb, n = 64, 2048
+        nb, n = shard(64, dist, "bgemm batch"), 2048
         A = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)
         Bm = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)
         Cm = torch.empty((nb, n, n), device=dev)
@@ -732,7 +767,8 @@ def run_conv_bgemm(args, dist, jx, torch):
             jx.gemm(A.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), n, n, n, batch=nb, strideA=n * n, strideB=n * n,
                     strideC=n * n, stream=s)
         flops = 2.0 * nb * n ** 3
-        wl = "batched sgemm [64,2048,2048] x [64,2048,2048] per rank (einsum bij,bjk->bik), JX_PREC_3XTF32"
+        wl = (f"batched sgemm [64,2048,2048] x [64,2048,2048] (einsum bij,bjk->bik), {nb} batch entries per rank, "
+              "JX_PREC_3XTF32")
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -762,20 +798,20 @@ def run_conv_bgemm(args, dist, jx, torch):
         e_ms = time_host_steps(torch, dist, st, host_step, args.e2e_steps)
         e_in, e_out = 2 * hA.numel() * 4, hC.numel() * 4
     return {"metric": METRIC, "value": round(tf, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": wl,
-                                                                                 "parallelism": f"batch shards x{dist.world}"},
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl, "parallelism": f"global batch split over {dist.world} rank(s), no collective"},
             "roofline": {"bound": "tensor",
                          "kernel": ("conv_gemm_kernel x3 (implicit GEMM; whole step incl. filter/dY splits)"
                                     if args.workload == "conv" else "gemm_fused_split_kernel (whole batched call)"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
                          "frac_at_run_clock": at_run_clock(tf / dist.world, clocks),
-                         "traffic": traffic_for(args)},
+                         "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS},
             "e2e": {"value": round(flops * dist.world / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps * (10 if args.workload == "conv" else
-                                          gemm_kernels(2048, 2048, 2048, False, False, False, batch=64)),
+                                          gemm_kernels(2048, 2048, 2048, False, False, False, batch=nb)),
             "clocks": clocks}
 
 
@@ -861,7 +897,7 @@ def run_layers(args, dist, jx, torch):
         roof = {"bound": "fp32 issue", "kernel": "conv1d_kernel", "achieved": round(val / dist.world, 2),
                 "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(val / dist.world / peak, 4),
                 "peak_basis": f"nominal: 148 SMs x 128 FP32 lanes x {mhz:.0f} MHz, one flop per unfused FMUL or "
-                              "FADD (no measured FP32 peak)", "traffic": traffic_for(args)}
+                              "FADD (no measured FP32 peak)", "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS}
     else:
         val = work * dist.world / (ms * 1e-3) / 1e9
         e2e = work * dist.world / (e_ms * 1e-3) / 1e9
@@ -869,7 +905,8 @@ def run_layers(args, dist, jx, torch):
         roof = {"bound": "hbm", "kernel": "pool2d_kernel" if args.workload == "pool" else
                 "norm_stats_wide + norm_finalize + norm_apply (whole call)",
                 "achieved": round(val / dist.world, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(val / dist.world / hbm, 4), "peak_basis": basis, "traffic": traffic_for(args),
+                "frac": round(val / dist.world / hbm, 4), "peak_basis": basis, "traffic": traffic_for(args, dist.world),
+                "traffic_basis": TRAFFIC_BASIS,
                 "note": "algorithmic bytes: one read of x and one write of y" +
                         ("; the statistics need a second read of x (12 B per element moved at best without L2 "
                          "reuse), so 8 B per element is a floor no two-pass kernel reaches"
@@ -908,22 +945,24 @@ def run_fft(args, dist, jx, torch):
     g = torch.Generator(device=dev)
     g.manual_seed(3 + dist.rank)
     if args.workload == "fft1d":
-        n, batch = 4096, args.fft_batch or 65536
+        n, batch = 4096, shard(args.fft_batch or 65536, dist, "FFT batch")
         X = torch.randn((batch, n, 2), device=dev, generator=g)
         Y = torch.empty_like(X)
 
         def step():
             jx.fft_c2c(X.data_ptr(), Y.data_ptr(), n, batch, False, s)
-        wl, kern, launches = f"1-D complex FFT n={n} x batch {batch} per rank (2 GiB in, 2 GiB out)", "fft_kernel", 1
+        wl, kern, launches = (f"1-D complex FFT n={n} x batch {batch * dist.world}, {batch} transforms per rank",
+                              "fft_kernel", 1)
     else:
         h = w = 1024
-        batch = args.fft_batch or 256
+        batch = shard(args.fft_batch or 256, dist, "FFT batch")
         X = torch.randn((batch, h, w, 2), device=dev, generator=g)
         Y = torch.empty_like(X)
 
         def step():
             jx.fft2_c2c(X.data_ptr(), Y.data_ptr(), h, w, batch, False, s)
-        wl, kern, launches = f"2-D complex FFT {h}x{w} x batch {batch} per rank (rows, then columns)", "fft_kernel", 2
+        wl, kern, launches = (f"2-D complex FFT {h}x{w} x batch {batch * dist.world}, {batch} images per rank "
+                              "(rows, then columns)", "fft_kernel", 2)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -968,13 +1007,13 @@ def run_fft(args, dist, jx, torch):
     e_ms, _, _ = measure_e2e(jx, torch, dist, st, [], [], host_step, args.e2e_steps)
     e_in, e_out = hX.numel() * 4, hY.numel() * 4
     return {"metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 (complex64)", "data": "synthetic N(0,1) real and imaginary parts",
-            "config": {"workload": wl, "l2": "2 GiB per pass > L2",
-                       "parallelism": f"batch shards x{dist.world}, no collective"},
+            "config": {"workload": wl, "l2": f"{nbytes / 2 / 2**30:.2f} GiB per pass per rank",
+                       "parallelism": f"global batch split over {dist.world} rank(s), no collective"},
             "roofline": {"bound": "hbm", "kernel": kern, "achieved": round(kgbs, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(kgbs / hbm, 4), "peak_basis": basis,
-                         "traffic": traffic_for(args), "kernel_ms": round(kern_ms, 4), "note": kern_note},
+                         "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS, "kernel_ms": round(kern_ms, 4), "note": kern_note},
             "e2e": {"value": round(nbytes * dist.world / (e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": e_in, "d2h_bytes_per_step": e_out, "ms_per_step": round(e_ms, 3)},
             "gpu_launches": args.steps * launches, "clocks": clocks}
@@ -993,29 +1032,39 @@ def gemm_kernels(M, N, K, transA, transB, exact, batch=1, sms=148):
     return 1 if fused else 3
 
 
-def mlp_launches(widths, batch, exact):
+def mlp_launches(widths, batch, exact, dp=False):
     """Kernels in one jx_mlp_train_step: forward GEMM + bias/activation per
     layer; softmax-xent (2); backward dW GEMM (A transposed) + column sums (2)
     per layer, dh GEMM (B transposed) + activation backward below the top
-    layer; Adam + step counter (2)."""
+    layer; Adam + step counter (2).  Data parallel (dp): one Adam launch per
+    layer bucket, and layer 1's weight gradient as two split passes + column
+    sums (2) + one main kernel per row chunk (2) when its width splits into
+    two multiples of 128 (NCCL's own kernels are not counted)."""
     L, n = len(widths) - 1, 4
     for l in range(L):
         K, N = widths[l], widths[l + 1]
         n += gemm_kernels(batch, N, K, False, False, exact) + 1
-        n += gemm_kernels(K, N, batch, True, False, exact) + 2
+        if dp and l == 0 and not exact and K % 256 == 0:
+            n += 2 + 2 + 2
+        else:
+            n += gemm_kernels(K, N, batch, True, False, exact) + 2
         if l > 0:
             n += gemm_kernels(batch, K, N, False, True, exact) + 1
+    if dp:
+        n += L - 1
     return n
 
 
-def run_mlp(args, dist, jx, torch):
+def run_mlp(args, dist, jx, torch, steps=None, warmup=None, e2e=True):
     """MLP training through the native trainer (jx_mlp_train_step).
 
     mlp:      784-256-128-10 ReLU, batch 128, Adam; one GPU (replicas for N > 1).
     wide_mlp: 8192 -> 4 x (8192 GELU) -> 1000, global batch split over the
               ranks, gradients all-reduced per layer with NCCL (data parallel).
     """
-    wide = args.workload == "wide_mlp"
+    wide = args.workload == "wide_mlp" or steps is not None
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     if wide:
         widths, acts = [8192, 8192, 8192, 8192, 8192, 1000], ["gelu"] * 4
         gb = args.global_batch
@@ -1068,7 +1117,7 @@ def run_mlp(args, dist, jx, torch):
     def step(i):
         net.step(X[i % nb].data_ptr(), Y[i % nb].data_ptr(), loss.data_ptr(), s)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     dist.barrier()
@@ -1077,11 +1126,11 @@ def run_mlp(args, dist, jx, torch):
     clk.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for i in range(args.steps):
+    for i in range(steps):
         step(i)
     e1.record(st)
     torch.cuda.synchronize()
-    ms = dist.max(e0.elapsed_time(e1) / args.steps)
+    ms = dist.max(e0.elapsed_time(e1) / steps)
     clocks = clk.stop()
     final_loss = float(loss.item())
     samples = gb if wide else batch * dist.world
@@ -1092,7 +1141,7 @@ def run_mlp(args, dist, jx, torch):
     hl = torch.empty((1,), dtype=torch.float32).pin_memory()
     hx.copy_(X[0].cpu())
     hy.copy_(Y[0].cpu())
-    e2e_steps = max(1, min(args.steps, 20 if not wide else 3))
+    e2e_steps = max(1, min(steps, 20 if not wide else 3))
     dist.barrier()
     torch.cuda.synchronize()
     e0.record(st)
@@ -1107,11 +1156,11 @@ def run_mlp(args, dist, jx, torch):
     flops = 0.0
     for l in range(len(widths) - 1):
         flops += 3 * 2.0 * batch * widths[l] * widths[l + 1]  # fwd + dX + dW GEMMs
-    _, bf16, basis = load_peaks(clocks, ms * args.steps)
+    _, bf16, basis = load_peaks(clocks, ms * steps)
     peak = bf16 / 2.0 / 3.0
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "metric": METRIC, "value": round(value, 1), "unit": "samples/s", "n_gpus": dist.world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if wide else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic N(0,1) inputs, uniform integer labels (torch generator)",
         "config": {"workload": ("wide MLP 8192-4x8192(GELU)-1000, softmax-CE, Adam, data parallel"
@@ -1125,7 +1174,7 @@ def run_mlp(args, dist, jx, torch):
                      "frac": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} / 2 / 3 (3xTF32)",
                      "frac_at_run_clock": at_run_clock(flops / (ms * 1e-3) / 1e12, clocks),
-                     "traffic": None if wide else traffic_for(args),
+                     "traffic": None if wide else traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS,
                      "note": ("exact f32 (sequential-k, unfused): the whole step is one cooperative kernel "
                               "with grid barriers between its phases; the tensor peak is quoted for scale")
                      if prec == jx.PREC_EXACT else ""},
@@ -1133,15 +1182,44 @@ def run_mlp(args, dist, jx, torch):
                 "h2d_bytes_per_step": (hx.numel() + hy.numel()) * 4, "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
         # exact precision on one GPU: the whole step is one cooperative kernel
-        "gpu_launches": args.steps * (1 if prec == jx.PREC_EXACT and comm is None
-                                      else mlp_launches(widths, batch, prec == jx.PREC_EXACT)),
+        "gpu_launches": steps * (1 if prec == jx.PREC_EXACT and comm is None
+                                      else mlp_launches(widths, batch, prec == jx.PREC_EXACT, comm is not None)),
         "clocks": clocks,
     }
+    if wide:
+        # where a step's time goes: CUDA events on the caller's stream around
+        # the forward pass, the backward pass as enqueued there, and the tail
+        # that waits for the last all-reduces and Adam updates (max over ranks)
+        net.set_timing(True)
+        ph = []
+        for i in range(3):
+            step(i)
+            ph.append(net.step_times())
+        net.set_timing(False)
+        fw, bw, tail = (dist.max(statistics.median(p[k] for p in ph)) for k in range(3))
+        line["phases_ms"] = {"forward": round(fw, 3), "backward": round(bw, 3), "tail": round(tail, 3),
+                             "tail_frac": round(tail / max(fw + bw + tail, 1e-9), 4),
+                             "note": "CUDA events in separate (untimed) steps; tail = exposed all-reduce + Adam"
+                                     if comm is not None else "CUDA events in separate (untimed) steps; tail = Adam"}
     if comm is not None:
         torch.cuda.synchronize()
         del net
         jx.call("jx_nccl_destroy", comm)
     return line
+
+
+def wide_mlp_sub(args, dist, jx, torch):
+    """The wide-MLP data-parallel training measurement the default line
+    carries beside its GEMM headline: 8192 -> 4 x 8192 (GELU) -> 1000, global
+    batch 65536 split over the ranks, NCCL all-reduce of every layer's
+    gradient bucket, Adam; its own warm-up (>= 3 steps) and timed steps."""
+    torch.cuda.empty_cache()
+    w = max(3, min(args.warmup, 5))
+    k = max(3, args.wide_steps)
+    sub = run_mlp(args, dist, jx, torch, steps=k, warmup=w)
+    keep = ("value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "config", "final_loss",
+            "roofline", "e2e", "gpu_launches", "clocks", "phases_ms")
+    return {key: sub[key] for key in keep if key in sub}
 
 
 def main():
@@ -1155,6 +1233,8 @@ def main():
     jx.init(dist.local)
     if args.workload == "sgemm":
         line = run_sgemm(args, dist, jx, torch)
+        if not args.no_wide_mlp:
+            line["wide_mlp"] = wide_mlp_sub(args, dist, jx, torch)
     elif args.workload in ("chain", "chain_grad"):
         line = run_chain(args, dist, jx, torch)
     elif args.workload == "rng":
@@ -1178,11 +1258,14 @@ def main():
 
 def reference_arm(args):
     """The reference's CPU implementation of the same workload (the oracle's
-    restatement of its loops) on all host threads, a bounded sample per step."""
+    restatement of its loops), a bounded sample per step, on one host thread:
+    the reference's CPU path is single-threaded (no rayon, no threads), so one
+    thread is all it can use.  The same restatement split over every host
+    thread is reported beside it as `value_all_threads`."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = 1
     steps = max(1, min(args.steps, 3))
     vals, pers, sample, unit = [], [], "", ""
     for _ in range(steps):
@@ -1194,13 +1277,17 @@ def reference_arm(args):
         vals.append(v)
         pers.append(per)
     value = statistics.median(vals)
+    all_threads = os.cpu_count() or 1
+    r_all = cpu_measure(args, all_threads, budget_s=4.0) if all_threads > 1 else None
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": args.gpus,
+        "value_all_threads": {"value": round(r_all[0], 6), "cores": all_threads} if r_all else None,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(pers) * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.workload} (sample of the GPU arm's workload)"},
         "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port",
-                         "sample": sample + " (oracle restatement of the reference CPU loop)"},
+                         "sample": sample + " (oracle restatement of the reference CPU loop; the reference is "
+                                            "single-threaded)"},
         "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

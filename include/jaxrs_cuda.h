@@ -47,20 +47,35 @@ typedef void *jx_stream_t; /* a cudaStream_t */
 /* ---- context / device (src/backend/webgpu.rs:31-75, src/device.rs:10-80) -- */
 JX_API const char *jx_last_error(void);
 JX_API int jx_version(void);
-/* WebGpuContext::init (src/backend/webgpu.rs:31-64): select and initialise a device. */
+/* WebGpuContext::init (src/backend/webgpu.rs:31-64): select and initialise a device.
+ * device < 0 selects the process default: the JAXRS_DEVICE environment
+ * variable, else device 0 (the reference's set-once default device,
+ * src/device.rs:55-80). */
 JX_API int jx_init(int device);
 JX_API int jx_device_count(int *count);
 JX_API int jx_set_device(int device);
 JX_API int jx_get_device(int *device);
 /* Device-side error word (bit 0: NaN met by an arg-reduction, bit 1: a bounded
- * wait timed out).  Reads and clears it; synchronises the device. */
+ * wait timed out).  Reads and clears it, together with the fixed error word of
+ * jx_gemm_f32_noalloc's launches (ORed in); synchronises the device. */
 JX_API int jx_device_status(unsigned int *flags);
 
 /* ---- storage (src/buffer.rs:40-122,581-590,700-749) ------------------------ */
 /* Buffer::zeros (src/buffer.rs:40-74) when zero != 0; stream-ordered allocation. */
 JX_API int jx_malloc(void **ptr, size_t nbytes, int zero, jx_stream_t stream);
-/* Last drop of a Buffer (Arc<BufferInner>); stream-ordered free. */
+/* Last drop of a Buffer (Arc<BufferInner>); stream-ordered free.  With
+ * JAXRS_CHECK=1 set when the buffer was allocated, jx_malloc puts 256 canary
+ * bytes after its end and jx_free checks them (synchronising the stream):
+ * JX_EDEVICE if a kernel wrote past the end. */
 JX_API int jx_free(void *ptr, jx_stream_t stream);
+/* JAXRS_CHECK (no reference counterpart): checks the canary tails of every
+ * live guarded buffer (synchronises the device); *corrupted = how many were
+ * overwritten. */
+JX_API int jx_check_guards(int *corrupted);
+/* Fault injection on the host (no reference counterpart): the next `count`
+ * device allocations (jx_malloc and the library's own scratch) fail with
+ * JX_ENOMEM; 0 disarms. */
+JX_API int jx_selftest_fail_alloc(int count);
 /* Buffer::from_f32 upload (src/buffer.rs:81-122).  `src` is host memory. */
 JX_API int jx_memcpy_h2d(void *dst, const void *src, size_t nbytes, jx_stream_t stream);
 /* Buffer::to_f32_vec readback (src/buffer.rs:581-590,711-749): blocks until the
@@ -134,9 +149,13 @@ JX_API int jx_gemm_batched_f32_host(const float *A, const float *B, float *C, in
  * workspace is a fixed 64 MiB device array inside the library, held by every
  * GPU that loads the library until the process exits.  Limit:
  * 2*batch*(M+N)*round_up(K,32) <= 16777216 floats, else JX_EINVAL.  The first
- * call on each device looks up the array's address (cudaGetSymbolAddress), so
- * make that first call before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race and must be serialised by the caller. */
+ * call on each device does that device's one-time set-up under a mutex (the
+ * array's address by cudaGetSymbolAddress, the tensor-map encoder, the
+ * kernel's shared-memory limit), so make that first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller.  K == 0 zero-fills C, as jx_gemm_f32.  A
+ * bounded wait that gives up inside its launches is reported by
+ * jx_device_status. */
 JX_API int jx_gemm_f32_noalloc(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
                                int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                                int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream);
@@ -458,19 +477,36 @@ JX_API int jx_mlp_train_step(jx_mlp *mlp, const float *x, const float *labels, f
  * same arithmetic as the separate kernels, bit-identical).  enable = 0 selects
  * the captured graph of separate kernels instead.  On by default. */
 JX_API int jx_mlp_set_fused(jx_mlp *mlp, int enable);
+/* Phase timing of training steps (no reference counterpart: the reference has
+ * no profiler, timestamp_writes: None at src/backend/ops.rs:139).  enable != 0
+ * records CUDA events in every following step (which then runs as separate
+ * launches, not a captured graph or the fused kernel); jx_mlp_step_times
+ * waits for the last timed step and returns ms[0] forward (through the
+ * softmax cross-entropy), ms[1] backward as enqueued on the caller's stream,
+ * ms[2] the tail after it: the wait for outstanding gradient all-reduces and
+ * Adam updates on the communication stream (with a communicator), else the
+ * flat Adam update. */
+JX_API int jx_mlp_set_timing(jx_mlp *mlp, int enable);
+JX_API int jx_mlp_step_times(jx_mlp *mlp, float *ms);
 /* Self-test of the bounded waits (no reference counterpart): a two-block
  * grid barrier waiting for one arrival more than the grid has.  Each block's
  * wait gives up after timeout_ms (1..5000), records JX_DEVERR_TIMEOUT in the
  * device error word and returns; *timed_out = 1 if the kernel reported it.
  * The context stays usable. */
 JX_API int jx_selftest_barrier_timeout(int timeout_ms, int *timed_out);
+/* Test hook (no reference counterpart): ORs flags into the current device's
+ * jx_gemm_f32_noalloc error word, so a test can check that the word reaches
+ * jx_device_status without making a wait run out. */
+JX_API int jx_selftest_noalloc_flag(unsigned int flags);
 JX_API int jx_mlp_destroy(jx_mlp *mlp);
 
 /* ---- data-parallel collectives (no reference counterpart: the reference has
  *      a single global device, src/backend/webgpu.rs:6) -------------------- */
 JX_API int jx_nccl_unique_id_size(void);
 JX_API int jx_nccl_get_unique_id(void *id_out /* jx_nccl_unique_id_size() bytes */);
-/* Non-blocking communicator init with a host watchdog of timeout_ms. */
+/* Non-blocking communicator init with a host watchdog of timeout_ms; a
+ * timeout_ms <= 0 takes JAXRS_NCCL_TIMEOUT_MS from the environment, else
+ * 120000. */
 JX_API int jx_nccl_init(const void *id, int nranks, int rank, int timeout_ms, void **comm_out);
 /* In-place sum all-reduce of count floats; polls for async errors up to timeout_ms. */
 JX_API int jx_nccl_allreduce_sum_f32(void *comm, float *buf, int64_t count, jx_stream_t stream);

@@ -56,6 +56,8 @@ _SIGS = {
     "jx_device_status": [C.POINTER(C.c_uint)],
     "jx_malloc": [C.POINTER(vp), C.c_size_t, ci, vp],
     "jx_free": [vp, vp],
+    "jx_check_guards": [C.POINTER(ci)],
+    "jx_selftest_fail_alloc": [ci],
     "jx_memcpy_h2d": [vp, vp, C.c_size_t, vp],
     "jx_memcpy_d2h": [vp, vp, C.c_size_t, vp],
     "jx_memcpy_d2d": [vp, vp, C.c_size_t, vp],
@@ -142,7 +144,10 @@ _SIGS = {
     "jx_mlp_attach_comm": [vp, vp, ci, i64],
     "jx_mlp_train_step": [vp, vp, vp, vp, vp],
     "jx_mlp_set_fused": [vp, ci],
+    "jx_mlp_set_timing": [vp, ci],
+    "jx_mlp_step_times": [vp, C.POINTER(cf)],
     "jx_selftest_barrier_timeout": [ci, C.POINTER(ci)],
+    "jx_selftest_noalloc_flag": [C.c_uint],
     "jx_mlp_destroy": [vp],
     "jx_nccl_unique_id_size": [],
     "jx_nccl_get_unique_id": [vp],
@@ -370,6 +375,15 @@ class MLP:
 
     def step(self, x, labels, loss_out=None, stream=None):
         call("jx_mlp_train_step", self.handle, x, labels, loss_out, stream)
+
+    def set_timing(self, enable=True):
+        call("jx_mlp_set_timing", self.handle, 1 if enable else 0)
+
+    def step_times(self):
+        """(forward, backward, tail) milliseconds of the last timed step."""
+        ms = (cf * 3)()
+        call("jx_mlp_step_times", self.handle, ms)
+        return tuple(ms)
 
     def __del__(self):
         try:

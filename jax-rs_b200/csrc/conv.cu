@@ -808,6 +808,7 @@ extern "C" {
 
 int jx_conv2d_fwd_f32(const float* x, const float* w, float* y, int64_t B, int64_t C, int64_t H, int64_t W, int64_t O,
                       int64_t KH, int64_t KW, int64_t stride, int64_t pad, jx_stream_t stream) {
+  JX_TRACE("jx_conv2d_fwd_f32");
   Geo g;
   int rc = check_geo(B, C, H, W, O, KH, KW, stride, pad, &g);
   if (rc) return rc;
@@ -840,6 +841,7 @@ int jx_conv2d_fwd_f32(const float* x, const float* w, float* y, int64_t B, int64
 
 int jx_conv2d_bwd_data_f32(const float* dy, const float* w, float* dx, int64_t B, int64_t C, int64_t H, int64_t W,
                            int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad, jx_stream_t stream) {
+  JX_TRACE("jx_conv2d_bwd_data_f32");
   Geo g;
   int rc = check_geo(B, C, H, W, O, KH, KW, stride, pad, &g);
   if (rc) return rc;
@@ -876,6 +878,7 @@ int jx_conv2d_bwd_data_f32(const float* dy, const float* w, float* dx, int64_t B
 
 int jx_conv2d_bwd_filter_f32(const float* x, const float* dy, float* dw, int64_t B, int64_t C, int64_t H, int64_t W,
                              int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad, jx_stream_t stream) {
+  JX_TRACE("jx_conv2d_bwd_filter_f32");
   Geo g;
   int rc = check_geo(B, C, H, W, O, KH, KW, stride, pad, &g);
   if (rc) return rc;

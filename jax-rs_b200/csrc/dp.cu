@@ -10,6 +10,7 @@
 // the process has already loaded (e.g. the one torch ships), so loading this
 // library never pins a different NCCL than the rest of the process uses.
 #include <dlfcn.h>
+#include <stdlib.h>
 #include <nccl.h>
 
 #include <chrono>
@@ -113,6 +114,7 @@ extern "C" {
 int jx_nccl_unique_id_size(void) { return (int)sizeof(ncclUniqueId); }
 
 int jx_nccl_get_unique_id(void* id_out) {
+  JX_TRACE("jx_nccl_get_unique_id");
   JX_REQUIRE(id_out, "jx_nccl_get_unique_id: NULL");
   JX_NCCL_API(api);
   ncclUniqueId id;
@@ -123,9 +125,14 @@ int jx_nccl_get_unique_id(void* id_out) {
 }
 
 int jx_nccl_init(const void* id, int nranks, int rank, int timeout_ms, void** comm_out) {
+  JX_TRACE("jx_nccl_init");
   JX_REQUIRE(id && comm_out, "jx_nccl_init: NULL argument");
   JX_REQUIRE(nranks >= 1 && rank >= 0 && rank < nranks, "jx_nccl_init: rank %d of %d", rank, nranks);
-  JX_REQUIRE(timeout_ms > 0, "jx_nccl_init: timeout must be positive");
+  if (timeout_ms <= 0) {  // the process default: JAXRS_NCCL_TIMEOUT_MS, else 120 s
+    const char* e = getenv("JAXRS_NCCL_TIMEOUT_MS");
+    timeout_ms = e && *e ? atoi(e) : 0;
+    if (timeout_ms <= 0) timeout_ms = 120000;
+  }
   *comm_out = nullptr;
   JX_NCCL_API(api);
   Comm* c = new Comm();
@@ -150,6 +157,7 @@ int jx_nccl_init(const void* id, int nranks, int rank, int timeout_ms, void** co
 }
 
 int jx_nccl_allreduce_sum_f32(void* comm, float* buf, int64_t count, jx_stream_t stream) {
+  JX_TRACE("jx_nccl_allreduce_sum_f32");
   JX_REQUIRE(count >= 0, "allreduce: negative count");
   if (count == 0) return JX_OK;
   JX_REQUIRE(buf, "allreduce: NULL buffer");
@@ -157,6 +165,7 @@ int jx_nccl_allreduce_sum_f32(void* comm, float* buf, int64_t count, jx_stream_t
 }
 
 int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
+  JX_TRACE("jx_nccl_wait");
   JX_NCCL_API(api);
   Comm* c = reinterpret_cast<Comm*>(comm);
   JX_REQUIRE(c && c->comm, "jx_nccl_wait: communicator is NULL or was aborted");
@@ -179,6 +188,7 @@ int jx_nccl_wait(void* comm, jx_stream_t stream, int timeout_ms) {
 }
 
 int jx_nccl_destroy(void* comm) {
+  JX_TRACE("jx_nccl_destroy");
   Comm* c = reinterpret_cast<Comm*>(comm);
   if (!c) return JX_OK;
   JX_NCCL_API(api);

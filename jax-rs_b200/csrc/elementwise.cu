@@ -88,6 +88,7 @@ int grid_for(long long work, int threads) {
 extern "C" {
 
 int jx_unary_f32(int op, const float* x, float* y, int64_t n, jx_stream_t stream) {
+  JX_TRACE("jx_unary_f32");
   JX_REQUIRE(op >= 0 && op <= JX_UN_LOG2, "unary: unknown op %d", op);
   JX_REQUIRE(n >= 0, "unary: negative size");
   if (n == 0) return JX_OK;
@@ -100,6 +101,7 @@ int jx_unary_f32(int op, const float* x, float* y, int64_t n, jx_stream_t stream
 
 int jx_binary_f32(int op, const float* a, const int64_t* a_shape, int a_ndim, const float* b, const int64_t* b_shape,
                   int b_ndim, float* out, jx_stream_t stream) {
+  JX_TRACE("jx_binary_f32");
   JX_REQUIRE(op >= 0 && op <= JX_BIN_MAX, "binary: unknown op %d", op);
   JX_REQUIRE(a_ndim >= 0 && a_ndim <= BMAX_DIMS && b_ndim >= 0 && b_ndim <= BMAX_DIMS, "binary: rank > %d",
              BMAX_DIMS);

@@ -714,6 +714,7 @@ int log2_exact(long long n) {
 extern "C" {
 
 int jx_fft_c2c_f32(const float* in, float* out, int64_t n, int64_t batch, int inverse, jx_stream_t stream) {
+  JX_TRACE("jx_fft_c2c_f32");
   JX_REQUIRE(n >= 1 && batch >= 0, "fft: bad size");
   const int logn = log2_exact(n);
   JX_REQUIRE(logn >= 0, "FFT size must be a power of 2, got %lld", (long long)n);
@@ -728,6 +729,7 @@ int jx_fft_c2c_f32(const float* in, float* out, int64_t n, int64_t batch, int in
 
 int jx_fft2_c2c_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batch, int inverse,
                     jx_stream_t stream) {
+  JX_TRACE("jx_fft2_c2c_f32");
   JX_REQUIRE(h >= 1 && w >= 1 && batch >= 0, "fft2: bad size");
   const int lh = log2_exact(h), lw = log2_exact(w);
   JX_REQUIRE(lh >= 0 && lw >= 0, "FFT size must be a power of 2, got %lld x %lld", (long long)h, (long long)w);
@@ -745,6 +747,7 @@ int jx_fft2_c2c_f32(const float* in, float* out, int64_t h, int64_t w, int64_t b
 }
 
 int jx_fft_r2c_f32(const float* in, float* out, int64_t n, int64_t batch, int full, jx_stream_t stream) {
+  JX_TRACE("jx_fft_r2c_f32");
   JX_REQUIRE(n >= 2 && batch >= 0, "fft: bad size");
   const int logn = log2_exact(n);
   JX_REQUIRE(logn >= 0, "FFT size must be power of 2");
@@ -770,6 +773,7 @@ int jx_fft_r2c_f32(const float* in, float* out, int64_t n, int64_t batch, int fu
 }
 
 int jx_fft_c2r_f32(const float* in, float* out, int64_t n, int64_t batch, jx_stream_t stream) {
+  JX_TRACE("jx_fft_c2r_f32");
   JX_REQUIRE(n >= 2 && batch >= 0, "irfft: bad size");
   const int logn = log2_exact(n);
   JX_REQUIRE(logn >= 0, "FFT size must be power of 2");
@@ -791,6 +795,7 @@ int jx_fft_c2r_f32(const float* in, float* out, int64_t n, int64_t batch, jx_str
 }
 
 int jx_rfft2_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream) {
+  JX_TRACE("jx_rfft2_f32");
   JX_REQUIRE(h >= 1 && w >= 2 && batch >= 0, "rfftn: bad size");
   const int lh = log2_exact(h), lw = log2_exact(w);
   JX_REQUIRE(lh >= 0 && lw >= 0, "FFT size must be power of 2");
@@ -806,6 +811,7 @@ int jx_rfft2_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batc
 }
 
 int jx_irfft2_f32(const float* in, float* out, int64_t h, int64_t w, int64_t batch, jx_stream_t stream) {
+  JX_TRACE("jx_irfft2_f32");
   JX_REQUIRE(h >= 1 && w >= 2 && batch >= 0, "irfftn: bad size");
   const int lh = log2_exact(h), lw = log2_exact(w);
   JX_REQUIRE(lh >= 0 && lw >= 0, "FFT size must be power of 2");

@@ -544,10 +544,13 @@ bool fused_split_ok(const float* A, const float* B, int transA, int transB, long
 
 // Per device, once: the fused kernel's shared-memory limit and its register
 // count at launch.
+std::mutex g_prepare_mu;  // guards the per-device one-time attribute settings below
+
 int fused_prepare(int* regs_out) {
   static int regs[64] = {0};
   int dev = 0;
   JX_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_prepare_mu);
   if (!regs[dev & 63]) {
     cudaFuncAttributes fa;
     JX_CUDA(cudaFuncGetAttributes(&fa, gemm_fused_split_kernel));
@@ -555,6 +558,20 @@ int fused_prepare(int* regs_out) {
     regs[dev & 63] = fa.numRegs;
   }
   if (regs_out) *regs_out = regs[dev & 63];
+  return JX_OK;
+}
+
+// Per device, once: the main kernel's shared-memory limit.  Two host threads
+// making their first call on a device serialise on the mutex.
+int main_prepare() {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_prepare_mu);
+  if (!attr_set[dev & 63]) {
+    JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+    attr_set[dev & 63] = true;
+  }
   return JX_OK;
 }
 
@@ -643,13 +660,7 @@ int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const f
   if ((rc = make_kmajor_map(&mAl, Al, Kp, M, a_bcast ? 1 : batch, BM))) return rc;
   if ((rc = make_kmajor_map(&mBh, Bh, Kp, N, b_bcast ? 1 : batch, BN))) return rc;
   if ((rc = make_kmajor_map(&mBl, Bl, Kp, N, b_bcast ? 1 : batch, BN))) return rc;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-    attr_set[dev & 63] = true;
-  }
+  if ((rc = main_prepare())) return rc;
   const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
   const long long nt = (long long)tiles_m * tiles_n * batch;
   if (nt > 0x7fffffffLL) return fail(JX_EINVAL, "gemm: too many tiles");
@@ -677,9 +688,9 @@ int gemm_presplit_splitk(const float* Ah, const float* Al, const float* Bh, cons
   if ((rc = make_map_3d(&mAl, Al, Ks, M, S, row, slice, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   if ((rc = make_map_3d(&mBh, Bh, Ks, N, S, row, slice, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
   if ((rc = make_map_3d(&mBl, Bl, Ks, N, S, row, slice, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  if ((rc = main_prepare())) return rc;
   void* part = nullptr;
   if ((rc = scratch_get(sizeof(float) * (size_t)S * M * N, &part, st))) return rc;
-  JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
   const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
   const int nt = tiles_m * tiles_n * S;
   float* pp = static_cast<float*>(part);
@@ -700,8 +711,9 @@ int gemm_presplit_splitk(const float* Ah, const float* Al, const float* Bh, cons
 // Sets the main kernel's shared-memory limit on the current device once, up
 // front (jx_init), so no later call -- e.g. one inside a stream capture -- has to.
 int gemm_prepare() {
-  JX_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-  return fused_prepare(nullptr);
+  int rc = get_encode();
+  if (!rc) rc = main_prepare();
+  return rc ? rc : fused_prepare(nullptr);
 }
 
 int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
@@ -727,6 +739,7 @@ int tensor_map_f32_3d(CUtensorMap_st* map, const void* base, const uint64_t* dim
 extern "C" {
 
 int jx_gemm_kpad(int64_t K, int64_t* Kp) {
+  JX_TRACE("jx_gemm_kpad");
   JX_REQUIRE(Kp && K >= 0, "jx_gemm_kpad: bad argument");
   *Kp = round_up(K, BK);
   return JX_OK;
@@ -734,6 +747,7 @@ int jx_gemm_kpad(int64_t K, int64_t* Kp) {
 
 int jx_gemm_split_f32(const float* src, float* hi, float* lo, int64_t rows, int64_t K, int64_t ld, int trans,
                       int64_t batch, int64_t stride, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_split_f32");
   JX_REQUIRE(rows >= 0 && K >= 0 && batch >= 0, "gemm split: negative dimension");
   if (rows == 0 || batch == 0) return JX_OK;
   JX_REQUIRE(src && hi && lo, "gemm split: NULL pointer");
@@ -746,6 +760,7 @@ int jx_gemm_split_f32(const float* src, float* hi, float* lo, int64_t rows, int6
 
 int jx_gemm_presplit_f32(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int64_t M,
                          int64_t N, int64_t Kp, int64_t ldc, int64_t batch, int64_t strideC, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_presplit_f32");
   JX_REQUIRE(M >= 0 && N >= 0 && Kp >= 0 && batch >= 0, "gemm presplit: negative dimension");
   if (M == 0 || N == 0 || batch == 0) return JX_OK;
   JX_REQUIRE(Ah && Al && Bh && Bl && C, "gemm presplit: NULL pointer");
@@ -762,6 +777,7 @@ int jx_gemm_presplit_f32(const float* Ah, const float* Al, const float* Bh, cons
 }
 
 int jx_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t batch, size_t* bytes) {
+  JX_TRACE("jx_gemm_workspace_size");
   JX_REQUIRE(bytes, "jx_gemm_workspace_size: NULL");
   long long Kp = round_up(K, BK);
   *bytes = (size_t)2 * (size_t)batch * (size_t)(M + N) * (size_t)Kp * sizeof(float);
@@ -771,6 +787,7 @@ int jx_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t batch, size_
 int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int transA, int transB,
                 int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t strideA, int64_t strideB,
                 int64_t strideC, int precision, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_f32");
   JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
   if (M == 0 || N == 0 || batch == 0) return JX_OK;
   JX_REQUIRE(A && B && C, "matmul: NULL operand");
@@ -848,14 +865,22 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
 //     rejected with JX_EINVAL before anything is launched.
 //   * Every GPU that loads this library keeps the 64 MiB array until the
 //     process exits.
-//   * The array's device address is looked up with cudaGetSymbolAddress on the
-//     first call made on each device (with that device current). That first
-//     call should therefore come before any stream capture.
+//   * The first call made on each device (with that device current) does
+//     that device's one-time set-up under a mutex: it looks up the array's
+//     device address with cudaGetSymbolAddress, resolves the tensor-map
+//     encoder and sets the main kernel's shared-memory limit. That first call
+//     should therefore come before any stream capture.
 //   * All calls share the one array and it keeps the last call's contents:
 //     the split pass rewrites every element a call reads (K padding included),
 //     so nothing needs clearing. Calls that overlap on the GPU (for example
 //     on two streams of one device) race on the array; the caller must
 //     serialise them.
+//   * A bounded wait that gives up inside one of these launches sets
+//     JX_DEVERR_TIMEOUT in a second fixed device word, g_noalloc_err, which
+//     jx_device_status reads, ORs into its result and clears, like the
+//     context's own error word.
+//   * K == 0 zero-fills C, as jx_gemm_f32 does (cudaMemset2DAsync, no
+//     allocation).
 // ---------------------------------------------------------------------------
 namespace {
 constexpr size_t NOALLOC_SCRATCH_FLOATS = (size_t)16 << 20;  // 64 MiB of f32
@@ -874,6 +899,8 @@ int noalloc_setup(float** scratch, unsigned int** err) {
   if (dev < 0 || dev >= 64) return jx::fail(JX_EUNSUPPORTED, "gemm noalloc: device index %d >= 64", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
+    if (int rc = get_encode()) return rc;
+    if (int rc = main_prepare()) return rc;
     void* p = nullptr;
     void* q = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -889,15 +916,59 @@ int noalloc_setup(float** scratch, unsigned int** err) {
 }
 }  // namespace
 
+namespace jx {
+// For jx_device_status: the current device's noalloc error word, read and
+// cleared (0 when this entry point has not run on the device).  The caller
+// has synchronised the device.
+int noalloc_take_error(unsigned int* flags) {
+  *flags = 0;
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return JX_OK;
+  unsigned int* w = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    w = g_noalloc_err_ptr[dev];
+  }
+  if (!w) return JX_OK;
+  JX_CUDA(cudaMemcpy(flags, w, sizeof(unsigned int), cudaMemcpyDeviceToHost));
+  JX_CUDA(cudaMemset(w, 0, sizeof(unsigned int)));
+  return JX_OK;
+}
+}  // namespace jx
+
+// Test hook: ORs `flags` into the noalloc error word of the current device,
+// so a test can check that the word reaches jx_device_status without making
+// a kernel's wait run out.
+extern "C" int jx_selftest_noalloc_flag(unsigned int flags) {
+  JX_TRACE("jx_selftest_noalloc_flag");
+  float* ws = nullptr;
+  unsigned int* err = nullptr;
+  int rc = noalloc_setup(&ws, &err);
+  if (rc) return rc;
+  unsigned int v = 0;
+  JX_CUDA(cudaDeviceSynchronize());
+  JX_CUDA(cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost));
+  v |= flags;
+  JX_CUDA(cudaMemcpy(err, &v, sizeof(v), cudaMemcpyHostToDevice));
+  return JX_OK;
+}
+
 extern "C" int jx_gemm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                                    int transA, int transB, int64_t lda, int64_t ldb, int64_t ldc, int64_t batch,
                                    int64_t strideA, int64_t strideB, int64_t strideC, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_f32_noalloc");
   JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
   if (M == 0 || N == 0 || batch == 0) return JX_OK;
   JX_REQUIRE(A && B && C, "matmul: NULL operand");
   JX_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && batch < 65536, "matmul: dimension too large");
   JX_REQUIRE(lda >= (transA ? M : K) && ldb >= (transB ? K : N) && ldc >= N, "matmul: leading dimension too small");
-  JX_REQUIRE(K > 0, "gemm noalloc: K must be positive");
+  cudaStream_t st = jx::as_stream(stream);
+  if (K == 0) {
+    for (int64_t b = 0; b < batch; ++b)
+      JX_CUDA(cudaMemset2DAsync(C + b * strideC, ldc * 4, 0, N * 4, M, st));
+    return JX_OK;
+  }
   const long long Kp = round_up(K, BK);
   const double need = 2.0 * (double)batch * (double)(M + N) * (double)Kp;
   if (need > (double)NOALLOC_SCRATCH_FLOATS)
@@ -909,7 +980,6 @@ extern "C" int jx_gemm_f32_noalloc(const float* A, const float* B, float* C, int
   unsigned int* err = nullptr;
   int rc = noalloc_setup(&ws, &err);
   if (rc) return rc;
-  cudaStream_t st = jx::as_stream(stream);
   float* Ah = ws;
   float* Al = Ah + (size_t)batch * M * Kp;
   float* Bh = Al + (size_t)batch * M * Kp;

@@ -312,27 +312,32 @@ int emit(const jx_graph* g, const std::vector<int>& order, int s, int e, const R
 extern "C" {
 
 int jx_graph_create(jx_graph** out) {
+  JX_TRACE("jx_graph_create");
   JX_REQUIRE(out, "jx_graph_create: NULL");
   *out = new jx_graph();
   return JX_OK;
 }
 
 int jx_graph_destroy(jx_graph* g) {
+  JX_TRACE("jx_graph_destroy");
   delete g;
   return JX_OK;
 }
 
 int jx_graph_input(jx_graph* g, int* node) {
+  JX_TRACE("jx_graph_input");
   JX_REQUIRE(g && node, "jx_graph_input: NULL");
   return add_node(g, K_INPUT, 0, -1, -1, 0.f, node);
 }
 
 int jx_graph_const(jx_graph* g, float value, int* node) {
+  JX_TRACE("jx_graph_const");
   JX_REQUIRE(g && node, "jx_graph_const: NULL");
   return add_node(g, K_CONST, 0, -1, -1, value, node);
 }
 
 int jx_graph_unary(jx_graph* g, int op, int x, int* node) {
+  JX_TRACE("jx_graph_unary");
   JX_REQUIRE(g && node, "jx_graph_unary: NULL");
   JX_REQUIRE(op >= JX_UN_NEG && op <= JX_UN_LOG2, "jx_graph_unary: unknown op %d", op);
   JX_REQUIRE(valid(g, x), "jx_graph_unary: operand %d is not a node of this graph", x);
@@ -340,6 +345,7 @@ int jx_graph_unary(jx_graph* g, int op, int x, int* node) {
 }
 
 int jx_graph_binary(jx_graph* g, int op, int x, int y, int* node) {
+  JX_TRACE("jx_graph_binary");
   JX_REQUIRE(g && node, "jx_graph_binary: NULL");
   JX_REQUIRE(op >= JX_BIN_ADD && op <= JX_BIN_MAX, "jx_graph_binary: unknown op %d", op);
   JX_REQUIRE(valid(g, x) && valid(g, y), "jx_graph_binary: operand is not a node of this graph");
@@ -347,12 +353,14 @@ int jx_graph_binary(jx_graph* g, int op, int x, int y, int* node) {
 }
 
 int jx_graph_select_gt(jx_graph* g, int x, int y, int* node) {
+  JX_TRACE("jx_graph_select_gt");
   JX_REQUIRE(g && node, "jx_graph_select_gt: NULL");
   JX_REQUIRE(valid(g, x) && valid(g, y), "jx_graph_select_gt: operand is not a node of this graph");
   return add_node(g, K_SEL, 0, x, y, 0.f, node);
 }
 
 int jx_graph_size(const jx_graph* g, int* n_nodes, int* n_inputs) {
+  JX_TRACE("jx_graph_size");
   JX_REQUIRE(g, "jx_graph_size: NULL");
   if (n_nodes) *n_nodes = (int)g->nodes.size();
   if (n_inputs) *n_inputs = g->n_inputs;
@@ -360,6 +368,7 @@ int jx_graph_size(const jx_graph* g, int* n_nodes, int* n_inputs) {
 }
 
 int jx_graph_vjp(jx_graph* g, int n_out, const int* outs, const int* cts, int n_wrt, const int* wrt, int* grads) {
+  JX_TRACE("jx_graph_vjp");
   JX_REQUIRE(g && n_out >= 1 && outs && cts && n_wrt >= 1 && wrt && grads, "jx_graph_vjp: bad arguments");
   for (int i = 0; i < n_out; ++i)
     JX_REQUIRE(valid(g, outs[i]) && valid(g, cts[i]), "jx_graph_vjp: output or cotangent is not a node");
@@ -455,6 +464,7 @@ int jx_graph_vjp(jx_graph* g, int n_out, const int* outs, const int* cts, int n_
 }
 
 int jx_graph_compile(const jx_graph* g, int n_out, const int* outs, jx_program** out) {
+  JX_TRACE("jx_graph_compile");
   JX_REQUIRE(g && out && n_out >= 1 && outs, "jx_graph_compile: bad arguments");
   for (int i = 0; i < n_out; ++i) JX_REQUIRE(valid(g, outs[i]), "jx_graph_compile: output %d is not a node", i);
   const int n = (int)g->nodes.size();
@@ -577,6 +587,7 @@ int jx_graph_compile(const jx_graph* g, int n_out, const int* outs, jx_program**
 }
 
 int jx_program_info(const jx_program* p, int* n_tapes, int* n_inputs, int* n_outputs, int* n_scratch) {
+  JX_TRACE("jx_program_info");
   JX_REQUIRE(p, "jx_program_info: NULL");
   if (n_tapes) *n_tapes = (int)p->tapes.size();
   if (n_inputs) *n_inputs = p->n_inputs;
@@ -586,6 +597,7 @@ int jx_program_info(const jx_program* p, int* n_tapes, int* n_inputs, int* n_out
 }
 
 int jx_program_tape(const jx_program* p, int i, const jx_tape** tape) {
+  JX_TRACE("jx_program_tape");
   JX_REQUIRE(p && tape && i >= 0 && i < (int)p->tapes.size(), "jx_program_tape: bad index");
   *tape = p->tapes[i].tape;
   return JX_OK;
@@ -593,6 +605,7 @@ int jx_program_tape(const jx_program* p, int i, const jx_tape** tape) {
 
 int jx_program_run(const jx_program* p, const float* const* ins, float* const* outs, int64_t n,
                    jx_stream_t stream) {
+  JX_TRACE("jx_program_run");
   JX_REQUIRE(p && (ins || p->n_inputs == 0) && outs && n >= 0, "jx_program_run: bad arguments");
   if (n == 0) return JX_OK;
   cudaStream_t st = jx::as_stream(stream);
@@ -645,6 +658,7 @@ int jx_program_run(const jx_program* p, const float* const* ins, float* const* o
 }
 
 int jx_program_destroy(jx_program* p) {
+  JX_TRACE("jx_program_destroy");
   if (!p) return JX_OK;
   for (auto& tr : p->tapes) jx_tape_destroy(tr.tape);
   delete p;

@@ -122,6 +122,7 @@ extern "C" {
 
 int jx_gemm_f32_host(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                      int64_t ldb, int64_t ldc, int64_t block_rows, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_f32_host");
   JX_REQUIRE(M >= 0 && N >= 0 && K >= 0, "matmul: negative dimension");
   if (M == 0 || N == 0) return JX_OK;
   JX_REQUIRE(K > 0, "gemm host: K must be positive");
@@ -192,6 +193,7 @@ int jx_gemm_f32_host(const float* A, const float* B, float* C, int64_t M, int64_
 
 int jx_tape_run_host(const jx_tape* tape, const float* const* ins, float* const* outs, int64_t n,
                      int64_t block_elems, jx_stream_t stream) {
+  JX_TRACE("jx_tape_run_host");
   JX_REQUIRE(tape && n >= 0, "jx_tape_run_host: bad arguments");
   if (n == 0) return JX_OK;
   int n_in = 0, n_out = 0;
@@ -275,6 +277,7 @@ int fft_host(const float* in, float* out, long long elems_per_item, long long it
 
 int jx_fft_c2c_f32_host(const float* in, float* out, int64_t n, int64_t batch, int inverse, int64_t block_items,
                         jx_stream_t stream) {
+  JX_TRACE("jx_fft_c2c_f32_host");
   JX_REQUIRE(n >= 1 && batch >= 0, "fft: bad size");
   if (batch == 0) return JX_OK;
   JX_REQUIRE(in && out, "fft: NULL pointer");
@@ -283,6 +286,7 @@ int jx_fft_c2c_f32_host(const float* in, float* out, int64_t n, int64_t batch, i
 
 int jx_fft2_c2c_f32_host(const float* in, float* out, int64_t h, int64_t w, int64_t batch, int inverse,
                          int64_t block_items, jx_stream_t stream) {
+  JX_TRACE("jx_fft2_c2c_f32_host");
   JX_REQUIRE(h >= 1 && w >= 1 && batch >= 0, "fft2: bad size");
   if (batch == 0) return JX_OK;
   JX_REQUIRE(in && out, "fft2: NULL pointer");
@@ -291,6 +295,7 @@ int jx_fft2_c2c_f32_host(const float* in, float* out, int64_t h, int64_t w, int6
 
 int jx_gemm_batched_f32_host(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                              int64_t batch, int64_t block_items, jx_stream_t stream) {
+  JX_TRACE("jx_gemm_batched_f32_host");
   JX_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 0, "matmul: negative dimension");
   if (M == 0 || N == 0 || batch == 0) return JX_OK;
   JX_REQUIRE(K > 0, "gemm host: K must be positive");
@@ -332,6 +337,7 @@ int jx_gemm_batched_f32_host(const float* A, const float* B, float* C, int64_t M
 int jx_pool2d_f32_host(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
                        int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w, int64_t pad_h,
                        int64_t pad_w, int op, int64_t block_items, jx_stream_t stream) {
+  JX_TRACE("jx_pool2d_f32_host");
   // geometry checks (and their messages) are jx_pool2d_f32's: run them once on an empty batch
   if (int rc = jx_pool2d_f32(nullptr, nullptr, 0, channels, input_h, input_w, pool_h, pool_w, stride_h, stride_w,
                              pad_h, pad_w, op, stream))

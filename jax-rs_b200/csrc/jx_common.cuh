@@ -13,6 +13,8 @@
 
 #include "../../include/jaxrs_cuda.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 // ---------------------------------------------------------------------------
 // Host-side error reporting
 // ---------------------------------------------------------------------------
@@ -40,6 +42,17 @@ int check_cuda(cudaError_t e, const char* what);
   do {                                                                      \
     if (!(cond)) return ::jx::fail(JX_EINVAL, __VA_ARGS__);                 \
   } while (0)
+
+// NVTX range around a C-ABI entry point: an Nsight Systems / Nsight Compute
+// timeline shows each call by its entry-point name, nested calls inside it.
+// With no tool attached the push and pop return at once.
+struct TraceRange {
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
+#define JX_TRACE(name) ::jx::TraceRange jx_trace_range_(name)
 
 int num_sms();                // SM count of the current device (cached)
 cudaStream_t as_stream(jx_stream_t s);

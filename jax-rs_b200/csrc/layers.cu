@@ -598,6 +598,7 @@ extern "C" {
 int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64_t in_channels,
                   int64_t out_channels, int64_t input_len, int64_t kernel_len, int64_t stride, int64_t padding,
                   jx_stream_t stream) {
+  JX_TRACE("jx_conv1d_f32");
   JX_REQUIRE(batch >= 0 && in_channels >= 1 && out_channels >= 0 && input_len >= 1,
              "jx_conv1d_f32: bad dims (batch %lld, in %lld, out %lld, len %lld)", (long long)batch,
              (long long)in_channels, (long long)out_channels, (long long)input_len);
@@ -657,6 +658,7 @@ int jx_conv1d_f32(const float* x, const float* w, float* y, int64_t batch, int64
 int jx_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
                   int64_t pool_h, int64_t pool_w, int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
                   int op, jx_stream_t stream) {
+  JX_TRACE("jx_pool2d_f32");
   JX_REQUIRE(op == JX_POOL_MAX || op == JX_POOL_AVG, "jx_pool2d_f32: unknown op %d", op);
   JX_REQUIRE(pool_h > 0 && pool_w > 0, "Pool size must be positive");
   JX_REQUIRE(stride_h > 0 && stride_w > 0, "Stride must be positive");
@@ -708,18 +710,21 @@ int jx_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int
 
 int jx_maxpool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
                      int64_t pool_h, int64_t pool_w, int64_t stride, int64_t padding, jx_stream_t stream) {
+  JX_TRACE("jx_maxpool2d_f32");
   return jx_pool2d_f32(x, y, batch, channels, input_h, input_w, pool_h, pool_w, stride, stride, padding, padding,
                        JX_POOL_MAX, stream);
 }
 
 int jx_avgpool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int64_t input_h, int64_t input_w,
                      int64_t pool_h, int64_t pool_w, int64_t stride, int64_t padding, jx_stream_t stream) {
+  JX_TRACE("jx_avgpool2d_f32");
   return jx_pool2d_f32(x, y, batch, channels, input_h, input_w, pool_h, pool_w, stride, stride, padding, padding,
                        JX_POOL_AVG, stream);
 }
 
 int jx_global_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channels, int64_t height, int64_t width,
                          int op, jx_stream_t stream) {
+  JX_TRACE("jx_global_pool2d_f32");
   JX_REQUIRE(op == JX_POOL_MAX || op == JX_POOL_AVG, "jx_global_pool2d_f32: unknown op %d", op);
   JX_REQUIRE(batch >= 0 && channels >= 0 && height >= 1 && width >= 1, "jx_global_pool2d_f32: bad dims");
   const long long N = batch * channels, S = height * width;
@@ -737,6 +742,7 @@ int jx_global_pool2d_f32(const float* x, float* y, int64_t batch, int64_t channe
 int jx_batchnorm_f32(const float* x, const float* gamma, const float* beta, float* y, int64_t batch,
                      int64_t channels, int64_t spatial, float epsilon, float* mean_out, float* var_out,
                      jx_stream_t stream) {
+  JX_TRACE("jx_batchnorm_f32");
   JX_REQUIRE(batch >= 1 && channels >= 1 && spatial >= 1, "jx_batchnorm_f32: bad dims (%lld, %lld, %lld)",
              (long long)batch, (long long)channels, (long long)spatial);
   JX_REQUIRE((gamma == nullptr) == (beta == nullptr), "jx_batchnorm_f32: gamma and beta go together");

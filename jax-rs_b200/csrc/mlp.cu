@@ -23,6 +23,11 @@
 namespace jx {
 int col_sum(const float* dy, float* db, long long rows, int cols, cudaStream_t st);
 int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st);
+int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
+                       int batch, bool transposed, cudaStream_t st);
+int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
+                  int Kp, long long ldc, long long strideC, int batch, cudaStream_t st);
+long long gemm_kpad(long long K);
 }  // namespace jx
 
 namespace {
@@ -437,6 +442,12 @@ struct jx_mlp {
   long long global_B = 0;
   cudaStream_t cstream = nullptr;
   std::vector<cudaEvent_t> ev;
+  int dw1_chunks = 2;  // row chunks of layer 1's weight gradient under data parallelism
+  // phase timing (jx_mlp_set_timing): events at step start, forward end,
+  // backward end on the caller's stream, and step end
+  bool timing = false;
+  cudaEvent_t tev[4] = {nullptr, nullptr, nullptr, nullptr};
+  bool tev_recorded = false;
   cudaGraphExec_t gexec = nullptr;
   long long steps = 0;
   // fused step (exact precision, one GPU)
@@ -451,6 +462,8 @@ namespace {
 
 void free_all(jx_mlp* n) {
   if (n->gexec) cudaGraphExecDestroy(n->gexec);
+  for (cudaEvent_t e : n->tev)
+    if (e) cudaEventDestroy(e);
   for (cudaEvent_t e : n->ev) cudaEventDestroy(e);
   if (n->cstream) cudaStreamDestroy(n->cstream);
   for (float* p : n->h) cudaFree(p);
@@ -488,10 +501,68 @@ int grid_elems(long long n) {
   return blocks < 1 ? 1 : (int)blocks;
 }
 
+// Adam over params[off, off + count) (and the same range of the gradients and
+// moments) on stream s.
+void adam_range(jx_mlp* n, long long off, long long count, cudaStream_t s) {
+  adam_flat_kernel<<<grid_elems(count), 256, 0, s>>>(n->params + off, n->grads + off, n->m + off, n->v + off, count,
+                                                     n->step, n->tab, n->lr, n->b1, n->b2, n->eps, 1.0f - n->b1,
+                                                     1.0f - n->b2);
+}
+
+// Layer 1's weight gradient under data parallelism, in n->dw1_chunks row
+// chunks: the operands are split once, then each chunk's product is
+// all-reduced and its Adam update applied on the communication stream while
+// the next chunk's product runs.  This is the last gradient of the step, so
+// without the chunks its whole all-reduce and update would sit behind the
+// backward pass with nothing to overlap.
+int dw1_chunked(jx_mlp* n, cudaStream_t st, int& evi) {
+  const long long B = n->B, K = n->w[0], N = n->w[1];
+  const int S = n->dw1_chunks;
+  const long long rows = K / S, Kp = jx::gemm_kpad(B);
+  float* gW = n->grads + n->woff[0];
+  void* ws = nullptr;
+  int rc = jx::scratch_get(sizeof(float) * (size_t)(2 * (K + N) * Kp), &ws, st);
+  if (rc) return rc;
+  float* Ah = static_cast<float*>(ws);
+  float* Al = Ah + K * Kp;
+  float* Bh = Al + K * Kp;
+  float* Bl = Bh + N * Kp;
+  // A = h0^T (element (feature r, sample k) = h0[k*K + r]); B = dz (element (n, k) = dz[k*N + n])
+  rc = jx::gemm_split_operand(n->h[0], Ah, Al, (int)K, (int)B, (int)Kp, K, 0, 1, true, st);
+  if (!rc) rc = jx::gemm_split_operand(n->dz, Bh, Bl, (int)N, (int)B, (int)Kp, N, 0, 1, true, st);
+  if (!rc) rc = jx::col_sum(n->dz, n->grads + n->boff[0], B, (int)N, st);
+  for (int c = 0; !rc && c < S; ++c) {
+    const long long r0 = c * rows;
+    rc = jx::gemm_presplit(Ah + r0 * Kp, Al + r0 * Kp, Bh, Bl, gW + r0 * N, (int)rows, (int)N, (int)Kp, N, 0, 1, st);
+    if (rc) break;
+    cudaEvent_t e = n->ev[evi++];
+    cudaError_t ce = cudaEventRecord(e, st);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(n->cstream, e, 0);
+    if (ce != cudaSuccess) {
+      rc = jx::check_cuda(ce, "mlp: layer-1 chunk hand-off");
+      break;
+    }
+    // the last chunk carries the bias gradient, which follows W1 in the bucket
+    const long long count = rows * N + (c == S - 1 ? N : 0);
+    rc = jx::nccl_allreduce(n->comm, gW + r0 * N, count, n->cstream);
+    if (!rc) adam_range(n, n->woff[0] + r0 * N, count, n->cstream);
+  }
+  const int rc2 = jx::scratch_release(ws, st);
+  return rc ? rc : rc2;
+}
+
 // One training step on stream st (forward, backward, optional all-reduce, Adam).
+//
+// With a communicator attached, layer l's gradient bucket (W_l then b_l) is
+// all-reduced on the communication stream as soon as backward has produced
+// it, and that bucket's Adam update follows on the same stream once the
+// backward GEMM that reads W_l (dh = dz W_l^T) is done; both overlap the
+// backward of the layers below.  The caller's stream waits for the
+// communication stream before the step counter moves on.
 int run_step(jx_mlp* n, cudaStream_t st) {
   int rc;
   const long long B = n->B;
+  if (n->timing) JX_CUDA(cudaEventRecord(n->tev[0], st));
   for (int l = 1; l <= n->L; ++l) {
     const long long K = n->w[l - 1], N = n->w[l];
     if ((rc = jx_gemm_f32(n->h[l - 1], n->params + n->woff[l - 1], n->h[l], B, N, K, 0, 0, K, N, N, 1, 0, 0, 0,
@@ -504,16 +575,31 @@ int run_step(jx_mlp* n, cudaStream_t st) {
   const long long C = n->w[n->L];
   if ((rc = jx_softmax_xent_f32(n->h[n->L], n->labels, nullptr, n->dz, n->loss, B, C, n->global_B * C, st)))
     return rc;
+  if (n->timing) JX_CUDA(cudaEventRecord(n->tev[1], st));
+  int evi = 0;
+  // the communication stream waits for everything enqueued on st so far
+  auto hand_off = [&]() -> int {
+    cudaEvent_t e = n->ev[evi++];
+    JX_CUDA(cudaEventRecord(e, st));
+    JX_CUDA(cudaStreamWaitEvent(n->cstream, e, 0));
+    return JX_OK;
+  };
   for (int l = n->L; l >= 1; --l) {
     const long long K = n->w[l - 1], N = n->w[l];
     float* gW = n->grads + n->woff[l - 1];
-    // dW_l = h_{l-1}^T dz (transpose_matmul's dB = A^T dC, src/trace/transpose_rules.rs:537-567)
-    if ((rc = jx_gemm_f32(n->h[l - 1], n->dz, gW, K, N, B, 1, 0, K, N, N, 1, 0, 0, 0, n->prec, st))) return rc;
-    if ((rc = jx::col_sum(n->dz, n->grads + n->boff[l - 1], B, (int)N, st))) return rc;
-    if (n->comm) {
-      JX_CUDA(cudaEventRecord(n->ev[l - 1], st));
-      JX_CUDA(cudaStreamWaitEvent(n->cstream, n->ev[l - 1], 0));
-      if ((rc = jx::nccl_allreduce(n->comm, gW, K * N + N, n->cstream))) return rc;
+    const long long bucket = K * N + N;  // W_l then b_l, contiguous
+    const bool chunked = n->comm && l == 1 && n->prec == JX_PREC_3XTF32 && n->dw1_chunks > 1 &&
+                         K % (n->dw1_chunks * 128LL) == 0;
+    if (chunked) {
+      if ((rc = dw1_chunked(n, st, evi))) return rc;
+    } else {
+      // dW_l = h_{l-1}^T dz (transpose_matmul's dB = A^T dC, src/trace/transpose_rules.rs:537-567)
+      if ((rc = jx_gemm_f32(n->h[l - 1], n->dz, gW, K, N, B, 1, 0, K, N, N, 1, 0, 0, 0, n->prec, st))) return rc;
+      if ((rc = jx::col_sum(n->dz, n->grads + n->boff[l - 1], B, (int)N, st))) return rc;
+      if (n->comm) {
+        if ((rc = hand_off())) return rc;
+        if ((rc = jx::nccl_allreduce(n->comm, gW, bucket, n->cstream))) return rc;
+      }
     }
     if (l > 1) {
       // dh = dz W_l^T (transpose_matmul's dA = dC B^T), then dz = dh * act'(pre)
@@ -522,16 +608,25 @@ int run_step(jx_mlp* n, cudaStream_t st) {
         return rc;
       if ((rc = jx_act_bwd_f32(n->dh, n->pre[l - 1], n->dz, nullptr, B, K, n->act[l - 2], st))) return rc;
     }
+    if (n->comm && !chunked) {
+      if ((rc = hand_off())) return rc;  // W_l is no longer read by this step
+      adam_range(n, n->woff[l - 1], bucket, n->cstream);
+    }
   }
+  if (n->timing) JX_CUDA(cudaEventRecord(n->tev[2], st));
   if (n->comm) {
-    JX_CUDA(cudaEventRecord(n->ev[n->L], n->cstream));
-    JX_CUDA(cudaStreamWaitEvent(st, n->ev[n->L], 0));
+    cudaEvent_t e = n->ev[evi++];
+    JX_CUDA(cudaEventRecord(e, n->cstream));
+    JX_CUDA(cudaStreamWaitEvent(st, e, 0));
+  } else {
+    adam_range(n, 0, n->nparams, st);
   }
-  adam_flat_kernel<<<grid_elems(n->nparams), 256, 0, st>>>(n->params, n->grads, n->m, n->v, n->nparams, n->step,
-                                                           n->tab, n->lr, n->b1, n->b2, n->eps, 1.0f - n->b1,
-                                                           1.0f - n->b2);
   step_inc_kernel<<<1, 1, 0, st>>>(n->step);
   JX_LAUNCH_CHECK("adam_flat_kernel");
+  if (n->timing) {
+    JX_CUDA(cudaEventRecord(n->tev[3], st));
+    n->tev_recorded = true;
+  }
   return JX_OK;
 }
 
@@ -545,7 +640,7 @@ __global__ void fs_barrier_selftest_kernel(unsigned* cnt, unsigned* err, unsigne
 }
 
 bool fused_eligible(const jx_mlp* n) {
-  if (!n->fused || n->comm || n->prec != JX_PREC_EXACT || n->L > FS_MAXL || n->B > (1 << 24)) return false;
+  if (!n->fused || n->comm || n->timing || n->prec != JX_PREC_EXACT || n->L > FS_MAXL || n->B > (1 << 24)) return false;
   for (long long x : n->w)
     if (x > (1 << 24)) return false;
   return true;
@@ -616,6 +711,7 @@ int run_fused_step(jx_mlp* n, const float* x, const float* labels, float* loss_o
 extern "C" {
 
 int jx_mlp_create(const int64_t* widths, int n_layers, const int* acts, int64_t batch, int precision, jx_mlp** out) {
+  JX_TRACE("jx_mlp_create");
   JX_REQUIRE(out && widths, "jx_mlp_create: NULL argument");
   *out = nullptr;
   JX_REQUIRE(n_layers >= 1 && n_layers <= 64, "jx_mlp_create: 1..64 layers");
@@ -677,12 +773,14 @@ int jx_mlp_create(const int64_t* widths, int n_layers, const int* acts, int64_t 
 }
 
 int jx_mlp_param_count(const jx_mlp* n, int64_t* count) {
+  JX_TRACE("jx_mlp_param_count");
   JX_REQUIRE(n && count, "jx_mlp_param_count: NULL argument");
   *count = n->nparams;
   return JX_OK;
 }
 
 int jx_mlp_param_offsets(const jx_mlp* n, int64_t* w_off, int64_t* b_off) {
+  JX_TRACE("jx_mlp_param_offsets");
   JX_REQUIRE(n && w_off && b_off, "jx_mlp_param_offsets: NULL argument");
   for (int l = 0; l < n->L; ++l) {
     w_off[l] = n->woff[l];
@@ -692,6 +790,7 @@ int jx_mlp_param_offsets(const jx_mlp* n, int64_t* w_off, int64_t* b_off) {
 }
 
 int jx_mlp_set_params(jx_mlp* n, const float* host, int64_t count) {
+  JX_TRACE("jx_mlp_set_params");
   JX_REQUIRE(n && host, "jx_mlp_set_params: NULL argument");
   JX_REQUIRE(count == n->nparams, "jx_mlp_set_params: expected %lld floats, got %lld", (long long)n->nparams,
              (long long)count);
@@ -700,6 +799,7 @@ int jx_mlp_set_params(jx_mlp* n, const float* host, int64_t count) {
 }
 
 int jx_mlp_get_params(const jx_mlp* n, float* host, int64_t count) {
+  JX_TRACE("jx_mlp_get_params");
   JX_REQUIRE(n && host, "jx_mlp_get_params: NULL argument");
   JX_REQUIRE(count == n->nparams, "jx_mlp_get_params: expected %lld floats", (long long)n->nparams);
   JX_CUDA(cudaDeviceSynchronize());
@@ -708,6 +808,7 @@ int jx_mlp_get_params(const jx_mlp* n, float* host, int64_t count) {
 }
 
 int jx_mlp_set_adam(jx_mlp* n, float lr, float beta1, float beta2, float eps) {
+  JX_TRACE("jx_mlp_set_adam");
   JX_REQUIRE(n, "jx_mlp_set_adam: NULL");
   n->lr = lr;
   n->b1 = beta1;
@@ -727,13 +828,16 @@ int jx_mlp_set_adam(jx_mlp* n, float lr, float beta1, float beta2, float eps) {
 }
 
 int jx_mlp_attach_comm(jx_mlp* n, void* comm, int world, int64_t global_batch) {
+  JX_TRACE("jx_mlp_attach_comm");
   JX_REQUIRE(n && comm, "jx_mlp_attach_comm: NULL argument");
   JX_REQUIRE(world >= 1 && global_batch == n->B * world, "jx_mlp_attach_comm: global batch must be batch * world");
   n->comm = comm;
   n->global_B = global_batch;
   if (!n->cstream) JX_CUDA(cudaStreamCreateWithFlags(&n->cstream, cudaStreamNonBlocking));
   if (n->ev.empty()) {
-    n->ev.resize(n->L + 1);
+    // hand-offs per step: two per layer above the first, up to dw1_chunks
+    // (or two) for the first, one at the end
+    n->ev.resize(2 * n->L + 8);
     for (auto& e : n->ev) JX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
   if (n->gexec) {
@@ -744,6 +848,7 @@ int jx_mlp_attach_comm(jx_mlp* n, void* comm, int world, int64_t global_batch) {
 }
 
 int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* loss_out, jx_stream_t stream) {
+  JX_TRACE("jx_mlp_train_step");
   JX_REQUIRE(n && x && labels, "jx_mlp_train_step: NULL argument");
   JX_REQUIRE(n->steps < ADAM_TABLE_STEPS, "jx_mlp_train_step: more than %lld steps", ADAM_TABLE_STEPS);
   cudaStream_t st = jx::as_stream(stream);
@@ -755,8 +860,8 @@ int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* los
   JX_CUDA(cudaMemcpyAsync(n->h[0], x, sizeof(float) * n->B * n->w[0], cudaMemcpyDeviceToDevice, st));
   JX_CUDA(cudaMemcpyAsync(n->labels, labels, sizeof(float) * n->B, cudaMemcpyDeviceToDevice, st));
   int rc;
-  if (n->comm) {
-    rc = run_step(n, st);  // collectives stay outside graphs
+  if (n->comm || n->timing) {
+    rc = run_step(n, st);  // collectives and phase-timing events stay outside graphs
   } else {
     if (!n->gexec) {
       // capture on a private stream, then replay on the caller's stream
@@ -788,6 +893,7 @@ int jx_mlp_train_step(jx_mlp* n, const float* x, const float* labels, float* los
 }
 
 int jx_selftest_barrier_timeout(int timeout_ms, int* timed_out) {
+  JX_TRACE("jx_selftest_barrier_timeout");
   JX_REQUIRE(timed_out && timeout_ms >= 1 && timeout_ms <= 5000, "jx_selftest_barrier_timeout: 1..5000 ms");
   void* buf = nullptr;
   JX_CUDA(cudaMalloc(&buf, 64));
@@ -808,13 +914,35 @@ int jx_selftest_barrier_timeout(int timeout_ms, int* timed_out) {
   return JX_OK;
 }
 
+int jx_mlp_set_timing(jx_mlp* n, int enable) {
+  JX_TRACE("jx_mlp_set_timing");
+  JX_REQUIRE(n, "jx_mlp_set_timing: NULL");
+  if (enable)
+    for (cudaEvent_t& e : n->tev)
+      if (!e) JX_CUDA(cudaEventCreate(&e));
+  n->timing = enable != 0;
+  n->tev_recorded = false;
+  return JX_OK;
+}
+
+int jx_mlp_step_times(jx_mlp* n, float* ms) {
+  JX_TRACE("jx_mlp_step_times");
+  JX_REQUIRE(n && ms, "jx_mlp_step_times: NULL argument");
+  JX_REQUIRE(n->timing && n->tev_recorded, "jx_mlp_step_times: no timed step yet (call jx_mlp_set_timing first)");
+  JX_CUDA(cudaEventSynchronize(n->tev[3]));
+  for (int i = 0; i < 3; ++i) JX_CUDA(cudaEventElapsedTime(&ms[i], n->tev[i], n->tev[i + 1]));
+  return JX_OK;
+}
+
 int jx_mlp_set_fused(jx_mlp* n, int enable) {
+  JX_TRACE("jx_mlp_set_fused");
   JX_REQUIRE(n, "jx_mlp_set_fused: NULL");
   n->fused = enable != 0;
   return JX_OK;
 }
 
 int jx_mlp_destroy(jx_mlp* n) {
+  JX_TRACE("jx_mlp_destroy");
   if (!n) return JX_OK;
   cudaDeviceSynchronize();
   free_all(n);

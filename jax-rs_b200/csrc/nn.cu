@@ -221,6 +221,7 @@ void adam_scalars(float lr, float b1, float b2, float eps, long long step, void*
 extern "C" {
 
 int jx_softmax_rows_f32(const float* x, float* y, int64_t rows, int64_t cols, jx_stream_t stream) {
+  JX_TRACE("jx_softmax_rows_f32");
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "softmax: bad size");
   if (rows == 0) return JX_OK;
   JX_REQUIRE(x && y, "softmax: NULL pointer");
@@ -231,6 +232,7 @@ int jx_softmax_rows_f32(const float* x, float* y, int64_t rows, int64_t cols, jx
 
 int jx_softmax_xent_f32(const float* logits, const float* labels, float* probs, float* dlogits, float* loss_out,
                         int64_t rows, int64_t cols, int64_t count, jx_stream_t stream) {
+  JX_TRACE("jx_softmax_xent_f32");
   JX_REQUIRE(rows >= 1 && cols >= 1 && cols < (1LL << 31), "cross_entropy: bad size");
   JX_REQUIRE(count >= 1, "cross_entropy: count must be positive");
   JX_REQUIRE(logits && labels && loss_out, "cross_entropy: NULL pointer");
@@ -249,6 +251,7 @@ int jx_softmax_xent_f32(const float* logits, const float* labels, float* probs, 
 }
 
 int jx_bias_act_f32(float* y, const float* bias, float* pre, int64_t rows, int64_t cols, int act, jx_stream_t stream) {
+  JX_TRACE("jx_bias_act_f32");
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "bias_act: bad size");
   JX_REQUIRE(act >= 0 && act <= 2, "bias_act: act must be 0 (none), 1 (relu) or 2 (gelu)");
   if (rows == 0) return JX_OK;
@@ -266,6 +269,7 @@ int jx_bias_act_f32(float* y, const float* bias, float* pre, int64_t rows, int64
 
 int jx_act_bwd_f32(const float* dy, const float* pre, float* dz, float* db, int64_t rows, int64_t cols, int act,
                    jx_stream_t stream) {
+  JX_TRACE("jx_act_bwd_f32");
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "act_bwd: bad size");
   JX_REQUIRE(act >= 0 && act <= 2, "act_bwd: act must be 0, 1 or 2");
   if (rows == 0) return JX_OK;
@@ -285,6 +289,7 @@ int jx_act_bwd_f32(const float* dy, const float* pre, float* dz, float* db, int6
 }
 
 int jx_col_sum_f32(const float* dy, float* db, int64_t rows, int64_t cols, jx_stream_t stream) {
+  JX_TRACE("jx_col_sum_f32");
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "col_sum: bad size");
   JX_REQUIRE(dy && db, "col_sum: NULL pointer");
   if (rows == 0) {
@@ -297,6 +302,7 @@ int jx_col_sum_f32(const float* dy, float* db, int64_t rows, int64_t cols, jx_st
 int jx_adam_step_f32(float* const* params, const float* const* grads, float* const* m, float* const* v,
                      const int64_t* sizes, int count, float lr, float beta1, float beta2, float eps, int64_t step,
                      jx_stream_t stream) {
+  JX_TRACE("jx_adam_step_f32");
   JX_REQUIRE(count >= 0, "adam: negative tensor count");
   JX_REQUIRE(step >= 1, "adam: step must be >= 1 (the state's step after increment)");
   if (count == 0) return JX_OK;

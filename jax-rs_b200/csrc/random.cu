@@ -288,6 +288,7 @@ extern "C" {
 
 // PRNGKey::from_seed (src/random.rs:29-32): [seed, seed * 0x9e3779b97f4a7c15]
 int jx_random_key_from_seed(uint64_t seed, uint64_t* s0, uint64_t* s1) {
+  JX_TRACE("jx_random_key_from_seed");
   JX_REQUIRE(s0 && s1, "jx_random_key_from_seed: NULL");
   *s0 = seed;
   *s1 = seed * 0x9e3779b97f4a7c15ull;
@@ -298,6 +299,7 @@ int jx_random_key_from_seed(uint64_t seed, uint64_t* s0, uint64_t* s1) {
 // to word 0 and rotates word 1 left by 27; the second adds 0x3c6ef372fe94f82a
 // and rotates right by 17.
 int jx_random_key_split(uint64_t s0, uint64_t s1, uint64_t* a0, uint64_t* a1, uint64_t* b0, uint64_t* b1) {
+  JX_TRACE("jx_random_key_split");
   JX_REQUIRE(a0 && a1 && b0 && b1, "jx_random_key_split: NULL");
   *a0 = s0 + 0x9e3779b97f4a7c15ull;
   *a1 = (s1 << 27) | (s1 >> 37);
@@ -307,6 +309,7 @@ int jx_random_key_split(uint64_t s0, uint64_t s1, uint64_t* a0, uint64_t* a1, ui
 }
 
 int jx_random_jump(uint64_t* s0, uint64_t* s1, uint64_t steps) {
+  JX_TRACE("jx_random_jump");
   JX_REQUIRE(s0 && s1, "jx_random_jump: NULL");
   int rc = poly_init();
   if (rc) return rc;
@@ -317,6 +320,7 @@ int jx_random_jump(uint64_t* s0, uint64_t* s1, uint64_t steps) {
 
 int jx_random_uniform_f32(uint64_t s0, uint64_t s1, float* out, int64_t n, float minval, float maxval,
                           jx_stream_t stream) {
+  JX_TRACE("jx_random_uniform_f32");
   JX_REQUIRE(n >= 0, "random: negative size");
   if (n == 0) return JX_OK;
   JX_REQUIRE(out, "random: NULL output");
@@ -326,6 +330,7 @@ int jx_random_uniform_f32(uint64_t s0, uint64_t s1, float* out, int64_t n, float
 
 int jx_random_randint_f32(uint64_t s0, uint64_t s1, float* out, int64_t n, int32_t minval, int32_t maxval,
                           jx_stream_t stream) {
+  JX_TRACE("jx_random_randint_f32");
   JX_REQUIRE(n >= 0, "random: negative size");
   JX_REQUIRE(minval < maxval, "minval must be less than maxval");
   if (n == 0) return JX_OK;
@@ -335,6 +340,7 @@ int jx_random_randint_f32(uint64_t s0, uint64_t s1, float* out, int64_t n, int32
 }
 
 int jx_random_normal_f32(uint64_t s0, uint64_t s1, float* out, int64_t n, jx_stream_t stream) {
+  JX_TRACE("jx_random_normal_f32");
   JX_REQUIRE(n >= 0, "random: negative size");
   if (n == 0) return JX_OK;
   JX_REQUIRE(out, "random: NULL output");

@@ -327,6 +327,7 @@ int grid_rows(long long rows, int warps_per_block) {
 extern "C" {
 
 int jx_reduce_all_f32(const float* x, float* out, int64_t n, int op, jx_stream_t stream) {
+  JX_TRACE("jx_reduce_all_f32");
   JX_REQUIRE(op >= JX_RED_SUM && op <= JX_RED_PROD, "reduce: unknown op %d", op);
   JX_REQUIRE(n >= 0, "reduce: negative size");
   JX_REQUIRE(out && (n == 0 || x), "reduce: NULL pointer");
@@ -355,6 +356,7 @@ int jx_reduce_all_f32(const float* x, float* out, int64_t n, int op, jx_stream_t
 
 int jx_reduce_axis_f32(const float* x, float* out, int64_t outer, int64_t len, int64_t inner, int op,
                        jx_stream_t stream) {
+  JX_TRACE("jx_reduce_axis_f32");
   JX_REQUIRE(op >= JX_RED_SUM && op <= JX_RED_PROD, "reduce: unknown op %d", op);
   JX_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, "reduce: negative size");
   if (outer == 0 || inner == 0) return JX_OK;
@@ -380,6 +382,7 @@ int jx_reduce_axis_f32(const float* x, float* out, int64_t outer, int64_t len, i
 
 int jx_argreduce_rows_f32(const float* x, int32_t* out_idx, float* out_val, int64_t rows, int64_t cols, int is_max,
                           jx_stream_t stream) {
+  JX_TRACE("jx_argreduce_rows_f32");
   JX_REQUIRE(rows >= 0, "argreduce: negative rows");
   JX_REQUIRE(cols >= 1 && cols < (1LL << 31), "argreduce: cols must be in [1, 2^31)");
   if (rows == 0) return JX_OK;
@@ -397,6 +400,7 @@ int jx_argreduce_rows_f32(const float* x, int32_t* out_idx, float* out_val, int6
 }
 
 int jx_sum_rows_vjp_f32(const float* ct, float* dx, int64_t rows, int64_t cols, jx_stream_t stream) {
+  JX_TRACE("jx_sum_rows_vjp_f32");
   JX_REQUIRE(rows >= 0 && cols >= 0 && cols < (1LL << 31), "sum vjp: bad size");
   if (rows == 0 || cols == 0) return JX_OK;
   JX_REQUIRE(ct && dx, "sum vjp: NULL pointer");
@@ -409,6 +413,7 @@ int jx_sum_rows_vjp_f32(const float* ct, float* dx, int64_t rows, int64_t cols, 
 }
 
 int jx_max_rows_vjp_f32(const float* x, const float* ct, float* dx, int64_t rows, int64_t cols, jx_stream_t stream) {
+  JX_TRACE("jx_max_rows_vjp_f32");
   JX_REQUIRE(rows >= 0 && cols >= 1 && cols < (1LL << 31), "max vjp: bad size");
   if (rows == 0) return JX_OK;
   JX_REQUIRE(x && ct && dx, "max vjp: NULL pointer");

@@ -401,6 +401,7 @@ extern "C" {
 
 int jx_tape_create(const int32_t* code, int n_instr, const float* consts, int n_consts, int n_inputs, int n_outputs,
                    jx_tape** out) {
+  JX_TRACE("jx_tape_create");
   JX_REQUIRE(out, "jx_tape_create: out is NULL");
   *out = nullptr;
   int rc = jx::tape_validate(code, n_instr, n_consts, n_inputs, n_outputs);
@@ -424,11 +425,13 @@ int jx_tape_create(const int32_t* code, int n_instr, const float* consts, int n_
 }
 
 int jx_tape_destroy(jx_tape* tape) {
+  JX_TRACE("jx_tape_destroy");
   delete tape;
   return JX_OK;
 }
 
 int jx_tape_source(const jx_tape* tape, char* buf, size_t cap, size_t* len) {
+  JX_TRACE("jx_tape_source");
   JX_REQUIRE(tape && len, "jx_tape_source: NULL argument");
   const std::string src = jx::codegen(tape);
   *len = src.size() + 1;
@@ -441,18 +444,21 @@ int jx_tape_source(const jx_tape* tape, char* buf, size_t cap, size_t* len) {
 }
 
 int jx_tape_check(const jx_tape* tape) {
+  JX_TRACE("jx_tape_check");
   JX_REQUIRE(tape, "jx_tape_check: NULL tape");
   std::vector<char> cubin;
   return jx::nvrtc_build(std::string(kPrelude) + jx::codegen(tape), cubin);
 }
 
 int jx_tape_compile(const jx_tape* tape) {
+  JX_TRACE("jx_tape_compile");
   JX_REQUIRE(tape, "jx_tape_compile: NULL tape");
   CUfunction f;
   return jx::compile_tape(tape, &f);
 }
 
 int jx_tape_info(const jx_tape* tape, int* n_inputs, int* n_outputs, int* n_instr) {
+  JX_TRACE("jx_tape_info");
   JX_REQUIRE(tape, "jx_tape_info: NULL tape");
   if (n_inputs) *n_inputs = tape->n_in;
   if (n_outputs) *n_outputs = tape->n_out;
@@ -461,6 +467,7 @@ int jx_tape_info(const jx_tape* tape, int* n_inputs, int* n_outputs, int* n_inst
 }
 
 int jx_tape_run(const jx_tape* tape, const float* const* ins, float* const* outs, int64_t n, jx_stream_t stream) {
+  JX_TRACE("jx_tape_run");
   JX_REQUIRE(tape, "jx_tape_run: NULL tape");
   JX_REQUIRE(n >= 0, "jx_tape_run: negative size");
   if (n == 0) return JX_OK;

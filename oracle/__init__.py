@@ -73,7 +73,7 @@ def lib():
         L.jxo_matmul_f64.argtypes = [f32p, f32p, f64p, i64, i64, i64]
         L.jxo_bmm.argtypes = [f32p, f32p, f32p, i64, i64, i64, i64, C.c_int]
         L.jxo_transpose.argtypes = [f32p, f32p, i64, i64]
-        for nm in ("jxo_gelu", "jxo_sigmoid", "jxo_relu", "jxo_tanh", "jxo_exp"):
+        for nm in ("jxo_gelu", "jxo_gelu_grad", "jxo_sigmoid", "jxo_relu", "jxo_tanh", "jxo_exp"):
             getattr(L, nm).argtypes = [f32p, f32p, i64]
         L.jxo_unary.argtypes = [C.c_int, f32p, f32p, i64]
         L.jxo_binary_broadcast.argtypes = [C.c_int, f32p, C.POINTER(C.c_int64), C.c_int, f32p,
@@ -212,6 +212,14 @@ def unary(name, x):
     x = _c(x)
     y = np.empty_like(x)
     lib().jxo_unary(UNOPS[name], x, y, x.size)
+    return y
+
+
+def gelu_grad(x):
+    """Derivative of nn::gelu's tanh form (src/nn.rs:111-122), elementwise."""
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().jxo_gelu_grad(x, y, x.size)
     return y
 
 

@@ -214,6 +214,18 @@ static inline float sigmoid1(float v) { return 1.0f / (1.0f + expf(-v)); }
 static inline float relu1(float v) { return fmaxf(v, 0.0f); }
 
 void jxo_gelu(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = gelu1(x[i]); }
+/* Derivative of gelu1 (the mathematical derivative of src/nn.rs:111-122, which
+ * the reference leaves untraced): 0.5*(1+t) + 0.5*v*(1-t^2)*coeff*(1 + 3*0.044715*v^2),
+ * t = tanh(inner), the same expression jxo_chain_vjp uses for its gelu term. */
+void jxo_gelu_grad(const float *x, float *y, int64_t n) {
+    const float coeff = sqrtf(2.0f / JXO_PI_F);
+    for (int64_t i = 0; i < n; ++i) {
+        float v = x[i], v2 = v * v;
+        float t = tanhf(coeff * (v + GELU_C1 * (v * v2)));
+        float dinner = coeff * (1.0f + 3.0f * GELU_C1 * v2);
+        y[i] = 0.5f * (1.0f + t) + 0.5f * v * (1.0f - t * t) * dinner;
+    }
+}
 void jxo_sigmoid(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = sigmoid1(x[i]); }
 void jxo_relu(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = relu1(x[i]); }
 void jxo_tanh(const float *x, float *y, int64_t n) { for (int64_t i = 0; i < n; ++i) y[i] = tanhf(x[i]); }

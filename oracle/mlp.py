@@ -21,8 +21,8 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import (adam_update, col_sum, cross_entropy, dense_fwd, key_from_seed, matmul, normal, one_hot, randint,
-               softmax_rows, softmax_xent_bwd, transpose, uniform_range)
+from . import (adam_update, col_sum, cross_entropy, dense_fwd, gelu_grad, key_from_seed, matmul, normal, one_hot,
+               randint, softmax_rows, softmax_xent_bwd, transpose, unary, uniform_range)
 
 
 def xavier_params(widths, seed=1):
@@ -50,11 +50,30 @@ def batches(steps, batch, features, classes, seed=0):
     return out
 
 
-def train(Ws, bs, data, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, nthreads=8):
-    """Runs len(data) Adam steps; returns (losses, Ws, bs)."""
+def _act(name, z):
+    if name == "relu":
+        return np.maximum(z, np.float32(0.0))  # nn::relu (f32::max)
+    if name == "gelu":
+        return unary("gelu", z)  # nn::gelu, src/nn.rs:111-122
+    return z
+
+
+def _act_grad(name, pre):
+    if name == "relu":
+        return (pre > 0).astype(np.float32)
+    if name == "gelu":
+        return gelu_grad(pre)
+    return np.ones_like(pre)
+
+
+def train(Ws, bs, data, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, nthreads=8, acts=None):
+    """Runs len(data) Adam steps; returns (losses, Ws, bs).  acts names each
+    hidden layer's activation ("relu", the default, or "gelu"); with gelu the
+    backward multiplies by its derivative (dz = dh * gelu'(pre))."""
     Ws = [w.copy() for w in Ws]
     bs = [b.copy() for b in bs]
     L = len(Ws)
+    acts = list(acts) if acts is not None else ["relu"] * (L - 1)
     mW = [np.zeros_like(w) for w in Ws]
     vW = [np.zeros_like(w) for w in Ws]
     mb = [np.zeros_like(b) for b in bs]
@@ -67,7 +86,7 @@ def train(Ws, bs, data, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, nthreads=8):
             z = dense_fwd(h, Ws[l], bs[l], nthreads)
             if l < L - 1:
                 pres.append(z)
-                h = np.maximum(z, np.float32(0.0))  # nn::relu (f32::max)
+                h = _act(acts[l], z)
             else:
                 h = z
             hs.append(h)
@@ -80,7 +99,7 @@ def train(Ws, bs, data, lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, nthreads=8):
             gb = col_sum(dz)
             if l > 0:
                 dh = matmul(dz, transpose(Ws[l]), nthreads)
-                dz = (dh * (pres[l - 1] > 0).astype(np.float32)).astype(np.float32)
+                dz = (dh * _act_grad(acts[l - 1], pres[l - 1])).astype(np.float32)
             Ws[l], mW[l], vW[l] = adam_update(Ws[l], gW, mW[l], vW[l], lr, b1, b2, eps, step, step == 1)
             bs[l], mb[l], vb[l] = adam_update(bs[l], gb, mb[l], vb[l], lr, b1, b2, eps, step, step == 1)
     return losses, Ws, bs
