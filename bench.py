@@ -43,6 +43,10 @@ sys.path.insert(0, ROOT)
 METRIC = "f32 GEMM TFLOP/s + MLP train samples/s at 1/2/4/8 B200; fused-elt HBM GB/s"
 
 
+WORKLOADS = ("sgemm", "chain", "chain_grad", "rng", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d",
+             "fft2d", "conv", "bgemm", "conv1d", "pool", "batchnorm", "sum_vjp", "max_vjp")
+
+
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -50,8 +54,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="sgemm",
-                   choices=["sgemm", "chain", "chain_grad", "rng", "rowsum", "argmax", "fullsum", "mlp", "wide_mlp", "fft1d", "fft2d",
-                            "conv", "bgemm", "conv1d", "pool", "batchnorm", "sum_vjp", "max_vjp"])
+                   help="one of " + ", ".join(WORKLOADS) + "; a comma-separated list runs each in turn in the "
+                        "same processes and prints one line per workload")
     p.add_argument("--precision", default=None, choices=["3xtf32", "exact"],
                    help="GEMM precision of the MLP trainer (default: exact for mlp, whose one-tile products the "
                         "sequential-k kernel runs faster and bit-identically; 3xtf32 for wide_mlp)")
@@ -68,7 +72,11 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=8, help="GEMM rows timed by the CPU baseline")
-    return p.parse_args()
+    args = p.parse_args()
+    for wl in args.workload.split(","):
+        if wl not in WORKLOADS:
+            p.error(f"unknown workload {wl!r}")
+    return args
 
 
 # DRAM bytes (read + write) per launch of each workload's dominant kernel at
@@ -1155,7 +1163,9 @@ def run_mlp(args, dist, jx, torch, steps=None, warmup=None, e2e=True):
     e2e_ms = dist.max(e0.elapsed_time(e1) / e2e_steps)
     flops = 0.0
     for l in range(len(widths) - 1):
-        flops += 3 * 2.0 * batch * widths[l] * widths[l + 1]  # fwd + dX + dW GEMMs
+        # forward and weight-gradient GEMMs per layer; the input gradient
+        # (dh = dz W^T) for every layer but the first
+        flops += (3 if l > 0 else 2) * 2.0 * batch * widths[l] * widths[l + 1]
     _, bf16, basis = load_peaks(clocks, ms * steps)
     peak = bf16 / 2.0 / 3.0
     line = {
@@ -1231,29 +1241,36 @@ def main():
     torch.cuda.set_device(dist.local)
     jx = importlib.import_module("jax-rs_b200")
     jx.init(dist.local)
-    if args.workload == "sgemm":
-        line = run_sgemm(args, dist, jx, torch)
-        if not args.no_wide_mlp:
-            line["wide_mlp"] = wide_mlp_sub(args, dist, jx, torch)
-    elif args.workload in ("chain", "chain_grad"):
-        line = run_chain(args, dist, jx, torch)
-    elif args.workload == "rng":
-        line = run_rng(args, dist, jx, torch)
-    elif args.workload in ("mlp", "wide_mlp"):
-        line = run_mlp(args, dist, jx, torch)
-    elif args.workload in ("fft1d", "fft2d"):
-        line = run_fft(args, dist, jx, torch)
-    elif args.workload in ("conv", "bgemm"):
-        line = run_conv_bgemm(args, dist, jx, torch)
-    elif args.workload in ("conv1d", "pool", "batchnorm"):
-        line = run_layers(args, dist, jx, torch)
-    else:
-        line = run_reduce(args, dist, jx, torch)
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        attach_cpu_baseline(line, args, threads=1)
+    lines = []
+    for wl in args.workload.split(","):
+        args.workload = wl
+        if wl == "sgemm":
+            line = run_sgemm(args, dist, jx, torch)
+            if not args.no_wide_mlp:
+                line["wide_mlp"] = wide_mlp_sub(args, dist, jx, torch)
+        elif wl in ("chain", "chain_grad"):
+            line = run_chain(args, dist, jx, torch)
+        elif wl == "rng":
+            line = run_rng(args, dist, jx, torch)
+        elif wl in ("mlp", "wide_mlp"):
+            line = run_mlp(args, dist, jx, torch)
+        elif wl in ("fft1d", "fft2d"):
+            line = run_fft(args, dist, jx, torch)
+        elif wl in ("conv", "bgemm"):
+            line = run_conv_bgemm(args, dist, jx, torch)
+        elif wl in ("conv1d", "pool", "batchnorm"):
+            line = run_layers(args, dist, jx, torch)
+        else:
+            line = run_reduce(args, dist, jx, torch)
+        if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+            attach_cpu_baseline(line, args, threads=1)
+        lines.append(line)
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     dist.close()
     if dist.rank == 0:
-        print(json.dumps(line), flush=True)
+        for line in lines:
+            print(json.dumps(line), flush=True)
 
 
 def reference_arm(args):
@@ -1265,6 +1282,7 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    args.workload = args.workload.split(",")[0]
     threads = 1
     steps = max(1, min(args.steps, 3))
     vals, pers, sample, unit = [], [], "", ""
