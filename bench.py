@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--fft-batch", type=int, default=0, help="override the FFT batch (smaller cases for profiling)")
     p.add_argument("--conv-batch", type=int, default=0, help="override the conv batch (smaller cases for profiling)")
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank (with --strong: of the whole product)")
+    p.add_argument("--gemm-prec", default="3xtf32", choices=["3xtf32", "pair"],
+                   help="sgemm/bgemm: JX_PREC_3XTF32 (the dispatcher's choice) or JX_PREC_3XTF32_PAIR (SM-pair "
+                        "kernel, split in shared memory)")
     p.add_argument("--strong", action="store_true",
                    help="sgemm: split the M rows of one size^3 product over the ranks (strong scaling) instead of "
                         "giving every rank its own size-row shard")
@@ -458,8 +461,10 @@ def run_sgemm(args, dist, jx, torch):
     Ah, Al = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
     Bh, Bl = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
 
+    gprec = jx.PREC_3XTF32_PAIR if args.gemm_prec == "pair" else jx.PREC_3XTF32
+
     def step():
-        jx.gemm(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, stream=s)
+        jx.gemm(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, precision=gprec, stream=s)
 
     for _ in range(args.warmup):
         step()
@@ -771,9 +776,11 @@ def run_conv_bgemm(args, dist, jx, torch):
         Bm = torch.empty((nb, n, n), device=dev).uniform_(-1, 1, generator=g)
         Cm = torch.empty((nb, n, n), device=dev)
 
+        gprec = jx.PREC_3XTF32_PAIR if args.gemm_prec == "pair" else jx.PREC_3XTF32
+
         def step():
             jx.gemm(A.data_ptr(), Bm.data_ptr(), Cm.data_ptr(), n, n, n, batch=nb, strideA=n * n, strideB=n * n,
-                    strideC=n * n, stream=s)
+                    strideC=n * n, precision=gprec, stream=s)
         flops = 2.0 * nb * n ** 3
         wl = (f"batched sgemm [64,2048,2048] x [64,2048,2048] (einsum bij,bjk->bik), {nb} batch entries per rank, "
               "JX_PREC_3XTF32")

@@ -103,6 +103,13 @@ JX_API int jx_host_unregister(void *ptr);
  * picks this kernel where it is faster (products of at least one 128x256 tile
  * per SM with small M or N). */
 #define JX_PREC_3XTF32_FUSED 2
+/* JX_PREC_3XTF32 on SM pairs (tcgen05 cta_group::2, a 256x256 tile per pair
+ * of SMs, each SM holding half of B), the hi/lo split done in shared memory
+ * from the caller's f32 buffers: no split pass, no workspace, any
+ * transposition.  Needs 16-byte aligned A and B with lda, ldb and batch
+ * strides multiples of 4 and at least one 256x256 tile per SM pair;
+ * otherwise JX_EINVAL. */
+#define JX_PREC_3XTF32_PAIR 3
 /* C[b] = op(A[b]) . op(B[b]) for b < batch, row-major.  op(X) = X or X^T per
  * trans flags: A is [M,K] (or [K,M] when transA), B is [K,N] (or [N,K]).
  * lda/ldb/ldc: row strides in elements; stride*: batch strides in elements. */

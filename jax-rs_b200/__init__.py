@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(HERE, "libjaxrs_cuda.so")
 JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, JX_EDEVICE, JX_EINTERNAL = range(9)
 STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "JX_ENCCL", 5: "JX_ETIMEOUT",
                 6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE", 8: "JX_EINTERNAL"}
-PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED = 0, 1, 2
+PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED, PREC_3XTF32_PAIR = 0, 1, 2, 3
 POOL_MAX, POOL_AVG = 0, 1
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,

@@ -645,6 +645,18 @@ int launch_split(const float* src, float* hi, float* lo, int rows, int K, int Kp
 }  // namespace
 
 namespace jx {
+// For the SM-pair kernel (gemm_pair.cu).
+int get_encode_fn() { return get_encode(); }
+int make_map_3d_fn(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                   uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  return make_map_3d(map, base, d0, d1, d2, s1, s2, b0, b1, sw);
+}
+bool pair_gemm_ok(const float* A, const float* B, long long M, long long N, long long lda, long long ldb,
+                  long long batch, long long sA, long long sB);
+int launch_pair_gemm(const float* A, const float* B, float* C, long long M, long long N, long long K, bool transA,
+                     bool transB, long long lda, long long ldb, long long ldc, long long batch, long long sA,
+                     long long sB, long long sC, cudaStream_t st);
+
 // Shared by conv2d (implicit GEMM) and the dense layers: 3xTF32 GEMM on
 // pre-split K-major operands.  Ah/Al: [batch][M][Kp]; Bh/Bl: [batch][N][Kp].
 // Launches the main kernel; `err` is the device word it flags a timed-out wait in.
@@ -806,6 +818,13 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
                                                      strideA, strideB, strideC);
     JX_LAUNCH_CHECK("gemm_exact_kernel");
     return JX_OK;
+  }
+  if (precision == JX_PREC_3XTF32_PAIR) {
+    JX_REQUIRE(jx::pair_gemm_ok(A, B, M, N, lda, ldb, batch, strideA, strideB),
+               "matmul: JX_PREC_3XTF32_PAIR needs 16-byte aligned operands with lda, ldb and batch strides "
+               "multiples of 4 and at least one 256x256 tile per SM pair");
+    return jx::launch_pair_gemm(A, B, C, M, N, K, transA != 0, transB != 0, lda, ldb, ldc, batch, strideA, strideB,
+                                strideC, st);
   }
   if (precision == JX_PREC_3XTF32_FUSED) {
     JX_REQUIRE(fused_split_ok(A, B, transA, transB, lda, ldb, batch, strideA, strideB),
