@@ -17,10 +17,13 @@
 //   warp 1 (even CTA)   TMEM allocation (both CTAs) + the single-thread pair
 //                       MMA issuer: Al.Bh + Ah.Bl + Ah.Bh per k-step, into
 //                       one of two TMEM span buffers (256 columns each)
-//   warps 4..11 (each)  split: lo = tf32_rn(x - trunc(x)) next to every raw
+//   warps 4..7 (each)   split: lo = tf32_rn(x - trunc(x)) next to every raw
 //                       value of the stage (the tf32 MMA reads the raw value
-//                       as hi = trunc(x)); then drain the TMEM spans into the
-//                       f32 accumulator registers and store C
+//                       as hi = trunc(x))
+//   warps 8..15 (each)  drain the TMEM spans into the f32 accumulator
+//                       registers and store C
+// The split has a warpgroup of its own so that it never waits behind a span
+// drain: with eight warps doing both, the MMA starved while they drained.
 //
 // Operand layouts by transposition: an operand whose K is contiguous in
 // memory (A untransposed, B transposed) is a K-major tile with 128-byte
@@ -30,10 +33,18 @@
 //
 // Handshakes (every wait bounded, about 4 s, then JX_DEVERR_TIMEOUT):
 //   raw_full[s]  (each CTA)  its TMA landed stage s
-//   full[s]      (even CTA)  both CTAs' split warps wrote lo of stage s (16 arrivals)
+//   full[s]      (even CTA)  both CTAs wrote lo of stage s (one arrival per CTA)
 //   empty[s]     (each CTA)  the pair's MMAs on stage s retired (multicast commit)
 //   sfull[p]     (each CTA)  span buffer p holds a finished partial sum (multicast commit)
-//   sempty[p]    (even CTA)  both CTAs drained span buffer p (16 arrivals)
+//   sempty[p]    (even CTA)  both CTAs drained span buffer p (one arrival per CTA)
+//   gfull[s], gempty[p] (each CTA)  local: the four split / eight drain warps are done
+// Each warp of a group arrives on its CTA's local barrier (CTA-scope
+// release); the group's first thread waits for all of them (bounded) and
+// alone arrives, with release at cluster scope, on the even CTA's barrier:
+// one cluster-scope release per stage per CTA instead of one per warp (the
+// per-warp cluster-scope fences were the main stall, `membar`, of an earlier
+// form).  Only the MMA issuer, whose barriers receive the other CTA's
+// arrivals, waits with cluster-scope acquire.
 // No TMA load uses cluster multicast: each CTA loads only its own tiles.
 #include <algorithm>
 #include <mutex>
@@ -49,15 +60,18 @@ constexpr int PR_TILE = 256;                                // output tile edge 
 constexpr int PR_STAGES = 3;
 constexpr int PR_OP = PR_ROWS * BK * 4;                     // 16 KB: one operand's raw (or lo) tile per CTA
 constexpr int PR_STAGE = 4 * PR_OP;                         // [A raw][A lo][B raw][B lo]
-constexpr int PR_THREADS = 384;
-constexpr int PR_FIRST_EPI = 4;
-constexpr int PR_LAUNCH_REGS = 168;
-constexpr int PR_LOW_REGS = 40;
-constexpr int PR_HIGH_REGS = 232;
+constexpr int PR_THREADS = 512;
+constexpr int PR_FIRST_SPLIT = 4;                           // warps 4..7: the split warpgroup
+constexpr int PR_SPLIT_WARPS = 4;
+constexpr int PR_FIRST_EPI = 8;                             // warps 8..15: drain + store
+constexpr int PR_LAUNCH_REGS = 128;
+constexpr int PR_LOW_REGS = 40;                             // TMA / MMA warpgroup
+constexpr int PR_SPLIT_REGS = 72;
+constexpr int PR_HIGH_REGS = 200;
 constexpr int PR_BOX = 32 * BK * 4;                         // one 32 x 32 MN-major box: 4 KB
 constexpr uint32_t PR_TMEM_COLS = 2 * PR_TILE;              // two span buffers of 256 columns
 constexpr size_t PR_SMEM = (size_t)PR_STAGES * PR_STAGE + 1024 /*align*/ + 256 /*barriers*/;
-static_assert(128 * PR_LOW_REGS + 256 * PR_HIGH_REGS <= PR_THREADS * PR_LAUNCH_REGS,
+static_assert(128 * PR_LOW_REGS + 128 * PR_SPLIT_REGS + 256 * PR_HIGH_REGS <= PR_THREADS * PR_LAUNCH_REGS,
               "register split exceeds the launch allocation");
 
 __device__ __forceinline__ bool wait_cl(uint64_t* bar, uint32_t parity, unsigned int* err) {
@@ -109,7 +123,9 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
   uint64_t* empty = bars + 2 * PR_STAGES;          // [PR_STAGES]
   uint64_t* sfull = bars + 3 * PR_STAGES;          // [2]
   uint64_t* sempty = bars + 3 * PR_STAGES + 2;     // [2] (even CTA)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * PR_STAGES + 4);
+  uint64_t* gfull = bars + 3 * PR_STAGES + 4;      // [PR_STAGES] local: split warps done
+  uint64_t* gempty = bars + 4 * PR_STAGES + 4;     // [2] local: drain warps done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * PR_STAGES + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -120,12 +136,14 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < PR_STAGES; ++s) {
       jxd::mbar_init(&raw_full[s], 1);
-      jxd::mbar_init(&full[s], 2 * EPI_WARPS);
+      jxd::mbar_init(&full[s], 2);
       jxd::mbar_init(&empty[s], 1);
+      jxd::mbar_init(&gfull[s], PR_SPLIT_WARPS);
     }
     for (int s = 0; s < 2; ++s) {
       jxd::mbar_init(&sfull[s], 1);
-      jxd::mbar_init(&sempty[s], 2 * EPI_WARPS);
+      jxd::mbar_init(&sempty[s], 2);
+      jxd::mbar_init(&gempty[s], EPI_WARPS);
     }
     *abort_flag = 0;
     jxd::fence_mbar_init();
@@ -143,8 +161,32 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
   jxd::cluster_sync_all();  // the peer's barriers are initialised before anyone signals them
   jxd::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full0 = jxd::mapa_shared(&full[0], 0), sempty0 = jxd::mapa_shared(&sempty[0], 0);
 
-  if (warp < PR_FIRST_EPI) {
+  // A bounded wait whose outcome is the same in every lane of the warp (the
+  // warp is converged again on return, as tcgen05.ld needs).
+  auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    const bool got = !*abort_flag && wait_bounded(bar, parity, err);
+    if (__all_sync(0xffffffffu, got)) return true;
+    *abort_flag = 1;
+    return false;
+  };
+  // Every warp of a group arrives on the local barrier `gbar`; the group's
+  // first thread (`first`) waits for all of them (bounded), then alone
+  // signals the even CTA's barrier at `cluster_bar`.  Warp-uniform outcome.
+  auto group_arrive = [&](uint64_t* gbar, uint32_t parity, uint32_t cluster_bar, bool first) -> bool {
+    __syncwarp();
+    if (lane == 0) jxd::mbar_arrive(gbar);
+    int ok = 1;
+    if (first) {
+      ok = wait_bounded(gbar, parity, err) ? 1 : 0;
+      if (ok) jxd::mbar_arrive_cluster(cluster_bar);
+      else *abort_flag = 1;
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  };
+
+  if (warp < PR_FIRST_SPLIT) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PR_LOW_REGS));
     if (warp == 0 && jxd::elect_one()) {
       // ---------------- TMA: this CTA's raw A and B slices ----------------
@@ -154,7 +196,7 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
         const int ya = ti.m_blk * PR_TILE + (int)rank * PR_ROWS, yb = ti.n_blk * PR_TILE + (int)rank * PR_ROWS;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!wait_cl(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          if (!wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
           uint8_t* st = smem + stage * PR_STAGE;
           jxd::mbar_arrive_expect_tx(&raw_full[stage], 2 * PR_OP);
           load_op<A_MN>(st, &tmA, &raw_full[stage], kb, ya, ti.b);
@@ -163,7 +205,7 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         }
       }
       for (int s = 0; s < PR_STAGES; ++s) {
-        if (!wait_cl(&empty[stage], phase ^ 1u, err)) break;
+        if (!wait_bounded(&empty[stage], phase ^ 1u, err)) break;
         if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
       }
     }
@@ -202,78 +244,76 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         }
       }
     }
+  } else if (warp < PR_FIRST_EPI) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PR_SPLIT_REGS));
+    // ---------------- split (warps 4..7): lo next to every raw value ----------------
+    const int sid = threadIdx.x - PR_FIRST_SPLIT * 32;  // 0..127
+    constexpr int CHUNKS = 2 * PR_OP / 16 / (32 * PR_SPLIT_WARPS);  // 16-byte chunks per thread per stage
+    constexpr int BATCH = 8;                                         // loads in flight before the arithmetic
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < num_tiles; t += npairs) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!warp_wait(&raw_full[stage], phase)) { ok = false; break; }
+        uint8_t* st = smem + stage * PR_STAGE;
+        // 2048 16-byte chunks of raw values per stage (A: 1024, then B: 1024),
+        // consecutive threads on consecutive chunks; lo goes PR_OP bytes after
+        // its raw chunk
+#pragma unroll
+        for (int j0 = 0; j0 < CHUNKS; j0 += BATCH) {
+          float4 x[BATCH];
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int f = sid + 32 * PR_SPLIT_WARPS * (j0 + j);
+            x[j] = *reinterpret_cast<const float4*>(st + (f < PR_OP / 16 ? f * 16 : PR_OP + f * 16));
+          }
+#pragma unroll
+          for (int j = 0; j < BATCH; ++j) {
+            const int f = sid + 32 * PR_SPLIT_WARPS * (j0 + j);
+            float4 l;
+            l.x = jxd::tf32_lo_of_trunc(x[j].x);
+            l.y = jxd::tf32_lo_of_trunc(x[j].y);
+            l.z = jxd::tf32_lo_of_trunc(x[j].z);
+            l.w = jxd::tf32_lo_of_trunc(x[j].w);
+            *reinterpret_cast<float4*>(st + PR_OP + (f < PR_OP / 16 ? f * 16 : PR_OP + f * 16)) = l;
+          }
+        }
+        jxd::fence_proxy_async_smem();  // this thread's generic-proxy writes -> the tensor cores
+        if (!group_arrive(&gfull[stage], phase, full0 + stage * 8, sid == 0)) { ok = false; break; }
+        if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(PR_HIGH_REGS));
-    // ---------------- split, drain the spans, store C ----------------
+    // ---------------- drain the spans, store C (warps 8..15) ----------------
     const int gt = threadIdx.x - PR_FIRST_EPI * 32;  // 0..255
     const int q = warp & 3, half = (warp - PR_FIRST_EPI) >> 2;
     const bool vec_ok = ((ldc & 3) == 0) && ((strideC & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
-    const uint32_t full0 = jxd::mapa_shared(&full[0], 0), sempty0 = jxd::mapa_shared(&sempty[0], 0);
-    int stage = 0;
-    uint32_t phase = 0, span_ctr = 0;
+    uint32_t span_ctr = 0;
     const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
-    // Drain span buffer `span_ctr` into acc and hand it back to the MMA issuer.
-    auto drain = [&](float (&acc)[EPI_COLS]) -> bool {
-      const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
-      if (*abort_flag || !wait_cl(&sfull[p], ph, err)) { *abort_flag = 1; return false; }
-      jxd::tc_fence_after();
-      const uint32_t t_addr =
-          tmem_base + ((uint32_t)(q * 32) << 16) + p * (uint32_t)PR_TILE + (uint32_t)(half * EPI_COLS);
-#pragma unroll
-      for (int c = 0; c < EPI_COLS; c += 32) {
-        uint32_t r[32];
-        jxd::tmem_ld32(t_addr + c, r);
-        jxd::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c + j] = __fadd_rn(acc[c + j], __uint_as_float(r[j]));
-      }
-      jxd::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) jxd::mbar_arrive_cluster(sempty0 + p * 8);
-      ++span_ctr;
-      return true;
-    };
     for (int t = pair; t < num_tiles; t += npairs) {
       float acc[EPI_COLS];
 #pragma unroll
       for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
       bool ok = true;
-      int spans_done = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (*abort_flag || !wait_cl(&raw_full[stage], phase, err)) {
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        uint8_t* st = smem + stage * PR_STAGE;
-        // 2048 16-byte chunks of raw values per stage (A: 1024, B: 1024), 8 per
-        // thread; lo goes PR_OP bytes after its raw chunk
+      for (int sp = 0; sp < nspan; ++sp) {
+        const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+        if (!warp_wait(&sfull[p], ph)) { ok = false; break; }
+        jxd::tc_fence_after();
+        const uint32_t t_addr =
+            tmem_base + ((uint32_t)(q * 32) << 16) + p * (uint32_t)PR_TILE + (uint32_t)(half * EPI_COLS);
 #pragma unroll
-        for (int j = 0; j < 2 * PR_OP / 16 / 256; ++j) {
-          const int f = gt + 256 * j;
-          uint8_t* hp = st + (f < PR_OP / 16 ? f * 16 : PR_OP + f * 16);
-          const float4 x = *reinterpret_cast<const float4*>(hp);
-          float4 l;
-          l.x = jxd::tf32_lo_of_trunc(x.x);
-          l.y = jxd::tf32_lo_of_trunc(x.y);
-          l.z = jxd::tf32_lo_of_trunc(x.z);
-          l.w = jxd::tf32_lo_of_trunc(x.w);
-          *reinterpret_cast<float4*>(hp + PR_OP) = l;
+        for (int c = 0; c < EPI_COLS; c += 16) {
+          uint32_t r[16];
+          jxd::tmem_ld16(t_addr + c, r);
+          jxd::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c + j] = __fadd_rn(acc[c + j], __uint_as_float(r[j]));
         }
-        // generic-proxy writes -> the pair's tensor cores (both SMs read this CTA's B half)
-        asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) jxd::mbar_arrive_cluster(full0 + stage * 8);
-        if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
-        // once span i is fully split, drain span i-1
-        if ((kb % SPAN_KB == SPAN_KB - 1 || kb == num_kb - 1) && kb >= SPAN_KB) {
-          if (!drain(acc)) { ok = false; break; }
-          ++spans_done;
-        }
-      }
-      while (ok && spans_done < nspan) {
-        if (!drain(acc)) ok = false;
-        ++spans_done;
+        jxd::tc_fence_before();
+        ++span_ctr;
+        if (!group_arrive(&gempty[p], ph, sempty0 + p * 8, gt == 0)) { ok = false; break; }
       }
       if (!ok) break;
       const TileInfo ti = tile_coords(t, tiles_m, tiles_n);

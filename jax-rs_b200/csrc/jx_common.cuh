@@ -267,11 +267,14 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 // lo part for a hi taken as the truncation of x to tf32 (what the tf32 MMA
 // reads from a raw f32 value): x - trunc(x) is exact in f32, then rounded to
 // the nearest tf32.
+// The rounding is done on the bits (integer pipes): adding half of a tf32
+// ulp (bit 12) to the magnitude and clearing the 13 low bits rounds to the
+// nearest tf32 with ties away from zero, as cvt.rna.tf32.f32 does for any
+// finite value.
 __device__ __forceinline__ float tf32_lo_of_trunc(float x) {
   const float hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
-  uint32_t l;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(__fsub_rn(x, hi)));
-  return __uint_as_float(l);
+  const uint32_t r = __float_as_uint(__fsub_rn(x, hi));
+  return __uint_as_float((r + 0x1000u) & 0xffffe000u);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
