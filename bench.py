@@ -89,7 +89,7 @@ def parse():
 # proportional to it.  batchnorm sums its three kernels (the roofline covers
 # the whole call).  None for any other size.
 TRAFFIC = {
-    "sgemm": 4.5905e9 + 0.2583e9,            # gemm_3xtf32_kernel, 8192^3
+    "sgemm": None,                           # gemm_pair_kernel, 8192^3: not captured yet
     "chain": 1.0738e9 + 1.0275e9,            # jx_tape_kernel, 2^28
     "rowsum": 1.0738e9 + 0.0039e9,           # reduce_rows_kernel<sum>
     "argmax": 1.0738e9 + 0.0033e9,           # argreduce_rows_kernel<max>
@@ -97,7 +97,7 @@ TRAFFIC = {
     "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
     "fft2d": 8 * (0.2685e9 + 0.2158e9),      # column pass fft1024_tma_kernel, batch 32 x 8
     "conv": 2 * (0.1082e9 + 0.0551e9 + 0.1079e9 + 0.0530e9 + 0.3201e9 + 0.0709e9),  # 3 conv_gemm_kernel, B 32 x 2
-    "bgemm": 2.2020e9 + 1.0442e9,            # gemm_fused_split_kernel, [64,2048,2048]^2
+    "bgemm": None,                           # gemm_pair_kernel, [64,2048,2048]^2: not captured yet
     "pool": 0.8228e9 + 0.1918e9,             # pool2d_kernel<max,3,3>, [64,256,112,112]
     "batchnorm": (0.2055e9 + 0.0036e9) + 0.0005e9 + (0.2056e9 + 0.1571e9),  # stats + finalize + apply
     "conv1d": 0.2704e9 + 0.2296e9,           # conv1d_kernel<1,3>, [64,256,4096]
@@ -457,11 +457,10 @@ def run_sgemm(args, dist, jx, torch):
     g.manual_seed(1)
     B = torch.empty((K, N), device=dev).uniform_(-1, 1, generator=g)   # replicated
     Cm = torch.empty((M, N), device=dev)
-    Kp = jx.gemm_kpad(K)
-    Ah, Al = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
-    Bh, Bl = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
-
     gprec = jx.PREC_3XTF32_PAIR if args.gemm_prec == "pair" else jx.PREC_3XTF32
+    # one launch of the SM-pair kernel per step where it applies, else the
+    # split passes and the main kernel on pre-split operands
+    pair = args.gemm_prec == "pair" or pair_ok(M, N, K, False, False)
 
     def step():
         jx.gemm(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, precision=gprec, stream=s)
@@ -487,19 +486,28 @@ def run_sgemm(args, dist, jx, torch):
     flops_rank = 2.0 * M * N * K
     value = flops_rank * dist.world / (ms_max * 1e-3) / 1e12
 
-    # dominant kernel alone: the tcgen05 main loop on pre-split operands
-    jx.gemm_split(A.data_ptr(), Ah.data_ptr(), Al.data_ptr(), M, K, stream=s)
-    jx.gemm_split(B.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), N, K, ld=N, trans=True, stream=s)
-    for _ in range(3):
-        jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp, stream=s)
-    torch.cuda.synchronize()
-    e0.record(st)
-    for _ in range(args.steps):
-        jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp, stream=s)
-    e1.record(st)
-    torch.cuda.synchronize()
-    kern_ms = e0.elapsed_time(e1) / args.steps
-    del Ah, Al, Bh, Bl
+    if pair:
+        # the step is one launch of the dominant kernel: its time is the step's
+        kern_ms, kern_name = ms, "gemm_pair_kernel (tcgen05 cta_group::2, split in shared memory)"
+    else:
+        # dominant kernel alone: the tcgen05 main loop on pre-split operands
+        Kp = jx.gemm_kpad(K)
+        Ah, Al = torch.empty((M, Kp), device=dev), torch.empty((M, Kp), device=dev)
+        Bh, Bl = torch.empty((N, Kp), device=dev), torch.empty((N, Kp), device=dev)
+        jx.gemm_split(A.data_ptr(), Ah.data_ptr(), Al.data_ptr(), M, K, stream=s)
+        jx.gemm_split(B.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), N, K, ld=N, trans=True, stream=s)
+        for _ in range(3):
+            jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp,
+                             stream=s)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            jx.gemm_presplit(Ah.data_ptr(), Al.data_ptr(), Bh.data_ptr(), Bl.data_ptr(), Cm.data_ptr(), M, N, Kp,
+                             stream=s)
+        e1.record(st)
+        torch.cuda.synchronize()
+        kern_ms, kern_name = e0.elapsed_time(e1) / args.steps, "gemm_3xtf32_kernel"
+        del Ah, Al, Bh, Bl
 
     # e2e: host buffers through the C ABI (jx_gemm_f32_host): per step, B and
     # the row blocks of A go up from pinned host memory and C comes back,
@@ -538,14 +546,14 @@ def run_sgemm(args, dist, jx, torch):
                    "global_batch": None, "seq_len": None, "parallelism": f"M-row shards x{dist.world}, no collective",
                    "l2": f"operands {M * K * 4 / 2**20:.0f} and {K * N * 4 / 2**20:.0f} MiB; "
                          + ("> 126 MB L2, no flush needed" if M * K * 4 > 126e6 else "B re-read from L2 across steps")},
-        "roofline": {"bound": "tensor", "kernel": "gemm_3xtf32_kernel", "achieved": round(achieved, 2),
+        "roofline": {"bound": "tensor", "kernel": kern_name, "achieved": round(achieved, 2),
                      "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_basis": f"{basis} bf16 {bf16} TFLOP/s / 2 (tf32 rate) / 3 (3 MMAs per product)",
                      "frac_at_run_clock": at_run_clock(achieved, clocks),
                      "traffic": traffic_for(args, dist.world), "traffic_basis": TRAFFIC_BASIS, "kernel_ms": round(kern_ms, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": nbA + nbB,
                 "d2h_bytes_per_step": nbC, "ms_per_step": round(e2e_ms, 3)},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": (1 if pair else 3) * args.steps,
         "clocks": clocks,
     }
     return line
@@ -818,7 +826,9 @@ def run_conv_bgemm(args, dist, jx, torch):
             "config": {"workload": wl, "parallelism": f"global batch split over {dist.world} rank(s), no collective"},
             "roofline": {"bound": "tensor",
                          "kernel": ("conv_gemm_kernel x3 (implicit GEMM; whole step incl. filter/dY splits)"
-                                    if args.workload == "conv" else "gemm_fused_split_kernel (whole batched call)"),
+                                    if args.workload == "conv" else
+                                    ("gemm_pair_kernel" if pair_ok(2048, 2048, 2048, False, False, nb)
+                                     else "gemm_fused_split_kernel") + " (whole batched call)"),
                          "achieved": round(tf / dist.world, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                          "frac": round(tf / dist.world / peak, 4), "peak_basis": f"{basis} bf16 / 2 / 3",
                          "frac_at_run_clock": at_run_clock(tf / dist.world, clocks),
@@ -1034,12 +1044,21 @@ def run_fft(args, dist, jx, torch):
             "gpu_launches": args.steps * launches, "clocks": clocks}
 
 
+def pair_ok(M, N, K, transA, transB, batch=1, sms=148):
+    """Whether jx_gemm_f32 (JX_PREC_3XTF32) takes the SM-pair kernel: leading
+    dimensions (contiguous operands) multiples of 4 floats and at least one
+    256x256 tile per SM pair."""
+    lda = M if transA else K
+    ldb = K if transB else N
+    return lda % 4 == 0 and ldb % 4 == 0 and -(-M // 256) * -(-N // 256) * batch >= sms // 2
+
+
 def gemm_kernels(M, N, K, transA, transB, exact, batch=1, sms=148):
-    """Kernels one jx_gemm_f32 call launches: 1 (exact, or the fused-split
-    kernel: untransposed rows of multiples of 4 floats, 250*(1/M + 1/N) > 0.2,
-    at least one 128x256 tile per SM) or 3 (two tf32 split passes + the
-    tcgen05 kernel)."""
-    if exact:
+    """Kernels one jx_gemm_f32 call launches: 1 (exact, the SM-pair kernel, or
+    the fused-split kernel: untransposed rows of multiples of 4 floats,
+    250*(1/M + 1/N) > 0.2, at least one 128x256 tile per SM) or 3 (two tf32
+    split passes + the tcgen05 kernel)."""
+    if exact or pair_ok(M, N, K, transA, transB, batch, sms):
         return 1
     tiles = -(-M // 128) * -(-N // 256) * batch
     fused = (not transA and not transB and K % 4 == 0 and N % 4 == 0 and 250.0 * (1.0 / M + 1.0 / N) > 0.2
@@ -1052,15 +1071,15 @@ def mlp_launches(widths, batch, exact, dp=False):
     layer; softmax-xent (2); backward dW GEMM (A transposed) + column sums (2)
     per layer, dh GEMM (B transposed) + activation backward below the top
     layer; Adam + step counter (2).  Data parallel (dp): one Adam launch per
-    layer bucket, and layer 1's weight gradient as two split passes + column
-    sums (2) + one main kernel per row chunk (2) when its width splits into
-    two multiples of 128 (NCCL's own kernels are not counted)."""
+    layer bucket, and layer 1's weight gradient as column sums (2) + one GEMM
+    per row chunk (2) when its width splits into two multiples of 128 (NCCL's
+    own kernels are not counted)."""
     L, n = len(widths) - 1, 4
     for l in range(L):
         K, N = widths[l], widths[l + 1]
         n += gemm_kernels(batch, N, K, False, False, exact) + 1
         if dp and l == 0 and not exact and K % 256 == 0:
-            n += 2 + 2 + 2
+            n += 2 + 2 * gemm_kernels(K // 2, N, batch, True, False, exact)
         else:
             n += gemm_kernels(K, N, batch, True, False, exact) + 2
         if l > 0:

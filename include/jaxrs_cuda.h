@@ -94,13 +94,18 @@ JX_API int jx_host_unregister(void *ptr);
 
 /* ---- GEMM (gpu_matmul src/backend/ops.rs:460-467; Array::matmul
  *      src/ops/linalg.rs:154-237; einsum "bij,bjk->bik" src/ops/einsum.rs:488-523) */
-#define JX_PREC_3XTF32 0 /* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32 */
+/* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32.  Products
+ * with at least one 256x256 tile per SM pair and TMA-compatible operands
+ * (16-byte aligned, lda/ldb/batch strides multiples of 4) run on the SM-pair
+ * kernel (see JX_PREC_3XTF32_PAIR); others split the operands into library
+ * scratch first. */
+#define JX_PREC_3XTF32 0
 #define JX_PREC_EXACT 1  /* sequential-k f32, no FMA: the reference's CPU loop order, bit-exact */
 /* JX_PREC_3XTF32 with the hi/lo split done inside the GEMM kernel from the
  * caller's f32 buffers: no split pass and no workspace.  Needs untransposed A
  * and B, 16-byte aligned, lda, ldb and batch strides multiples of 4 (and non-zero
- * batch strides when batch > 1); otherwise JX_EINVAL.  JX_PREC_3XTF32 already
- * picks this kernel where it is faster (products of at least one 128x256 tile
+ * batch strides when batch > 1); otherwise JX_EINVAL.  JX_PREC_3XTF32 picks
+ * this kernel where it is faster and the SM-pair kernel does not apply (products of at least one 128x256 tile
  * per SM with small M or N). */
 #define JX_PREC_3XTF32_FUSED 2
 /* JX_PREC_3XTF32 on SM pairs (tcgen05 cta_group::2, a 256x256 tile per pair

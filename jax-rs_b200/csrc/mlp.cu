@@ -23,11 +23,6 @@
 namespace jx {
 int col_sum(const float* dy, float* db, long long rows, int cols, cudaStream_t st);
 int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st);
-int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
-                       int batch, bool transposed, cudaStream_t st);
-int gemm_presplit(const float* Ah, const float* Al, const float* Bh, const float* Bl, float* C, int M, int N,
-                  int Kp, long long ldc, long long strideC, int batch, cudaStream_t st);
-long long gemm_kpad(long long K);
 }  // namespace jx
 
 namespace {
@@ -510,30 +505,21 @@ void adam_range(jx_mlp* n, long long off, long long count, cudaStream_t s) {
 }
 
 // Layer 1's weight gradient under data parallelism, in n->dw1_chunks row
-// chunks: the operands are split once, then each chunk's product is
-// all-reduced and its Adam update applied on the communication stream while
-// the next chunk's product runs.  This is the last gradient of the step, so
-// without the chunks its whole all-reduce and update would sit behind the
-// backward pass with nothing to overlap.
+// chunks: each chunk's product is all-reduced and its Adam update applied on
+// the communication stream while the next chunk's product runs.  This is the
+// last gradient of the step, so without the chunks its whole all-reduce and
+// update would sit behind the backward pass with nothing to overlap.  Rows
+// r0.. of dW1 = h0^T dz are the product of columns r0.. of h0 (A transposed,
+// lda = K) with dz.
 int dw1_chunked(jx_mlp* n, cudaStream_t st, int& evi) {
   const long long B = n->B, K = n->w[0], N = n->w[1];
   const int S = n->dw1_chunks;
-  const long long rows = K / S, Kp = jx::gemm_kpad(B);
+  const long long rows = K / S;
   float* gW = n->grads + n->woff[0];
-  void* ws = nullptr;
-  int rc = jx::scratch_get(sizeof(float) * (size_t)(2 * (K + N) * Kp), &ws, st);
-  if (rc) return rc;
-  float* Ah = static_cast<float*>(ws);
-  float* Al = Ah + K * Kp;
-  float* Bh = Al + K * Kp;
-  float* Bl = Bh + N * Kp;
-  // A = h0^T (element (feature r, sample k) = h0[k*K + r]); B = dz (element (n, k) = dz[k*N + n])
-  rc = jx::gemm_split_operand(n->h[0], Ah, Al, (int)K, (int)B, (int)Kp, K, 0, 1, true, st);
-  if (!rc) rc = jx::gemm_split_operand(n->dz, Bh, Bl, (int)N, (int)B, (int)Kp, N, 0, 1, true, st);
-  if (!rc) rc = jx::col_sum(n->dz, n->grads + n->boff[0], B, (int)N, st);
+  int rc = jx::col_sum(n->dz, n->grads + n->boff[0], B, (int)N, st);
   for (int c = 0; !rc && c < S; ++c) {
     const long long r0 = c * rows;
-    rc = jx::gemm_presplit(Ah + r0 * Kp, Al + r0 * Kp, Bh, Bl, gW + r0 * N, (int)rows, (int)N, (int)Kp, N, 0, 1, st);
+    rc = jx_gemm_f32(n->h[0] + r0, n->dz, gW + r0 * N, rows, N, B, 1, 0, K, N, N, 1, 0, 0, 0, n->prec, st);
     if (rc) break;
     cudaEvent_t e = n->ev[evi++];
     cudaError_t ce = cudaEventRecord(e, st);
@@ -547,8 +533,7 @@ int dw1_chunked(jx_mlp* n, cudaStream_t st, int& evi) {
     rc = jx::nccl_allreduce(n->comm, gW + r0 * N, count, n->cstream);
     if (!rc) adam_range(n, n->woff[0] + r0 * N, count, n->cstream);
   }
-  const int rc2 = jx::scratch_release(ws, st);
-  return rc ? rc : rc2;
+  return rc;
 }
 
 // One training step on stream st (forward, backward, optional all-reduce, Adam).

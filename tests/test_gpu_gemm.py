@@ -169,8 +169,9 @@ def test_8192_cubed_sampled_rows(jx, dev, oracle):
 
 
 def test_many_small_products_default_precision(jx, dev, oracle):
-    """160 products of 256^3 under JX_PREC_3XTF32: enough tiles per SM and small
-    M, N, so the dispatcher takes the fused-split kernel on its own."""
+    """160 products of 256^3 under JX_PREC_3XTF32: one 256 x 256 tile each,
+    160 in all, enough for every SM pair, so the dispatcher takes the SM-pair
+    kernel on its own (batch index as a TMA coordinate)."""
     bt, n = 160, 256
     rng = np.random.default_rng(17)
     a = rng.uniform(-1, 1, (bt, n, n)).astype(np.float32)
