@@ -190,6 +190,11 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        # a short timed region ends before the first 100 ms sample: wait (up
+        # to 1 s) for two samples so the line always carries a clock reading
+        t0 = time.time()
+        while len(self.lines) < 2 and time.time() - t0 < 1.0:
+            time.sleep(0.05)
         time.sleep(0.15)
         self.proc.terminate()
         try:
