@@ -1278,7 +1278,10 @@ def main():
         if wl == "sgemm":
             line = run_sgemm(args, dist, jx, torch)
             if not args.no_wide_mlp:
-                line["wide_mlp"] = wide_mlp_sub(args, dist, jx, torch)
+                try:
+                    line["wide_mlp"] = wide_mlp_sub(args, dist, jx, torch)
+                except Exception as e:  # keep the GEMM headline if the training run fails
+                    line["wide_mlp"] = {"error": f"{type(e).__name__}: {e}"[:400]}
         elif wl in ("chain", "chain_grad"):
             line = run_chain(args, dist, jx, torch)
         elif wl == "rng":

@@ -499,6 +499,13 @@ JX_API int jx_mlp_set_fused(jx_mlp *mlp, int enable);
  * Adam updates on the communication stream (with a communicator), else the
  * flat Adam update. */
 JX_API int jx_mlp_set_timing(jx_mlp *mlp, int enable);
+/* Data-parallel update form (no reference counterpart).  enable != 0 (the
+ * default): each gradient bucket whose size divides by the rank count is
+ * reduce-scattered, Adam updates this rank's 1/world of it, and the updated
+ * parameters are all-gathered (ZeRO-1-style; each rank keeps Adam moments for
+ * its own shards only).  enable = 0: all-reduce and Adam over every bucket on
+ * every rank.  Call before the first step. */
+JX_API int jx_mlp_set_dp_sharded(jx_mlp *mlp, int enable);
 JX_API int jx_mlp_step_times(jx_mlp *mlp, float *ms);
 /* Self-test of the bounded waits (no reference counterpart): a two-block
  * grid barrier waiting for one arrival more than the grid has.  Each block's

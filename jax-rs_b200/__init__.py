@@ -145,6 +145,7 @@ _SIGS = {
     "jx_mlp_train_step": [vp, vp, vp, vp, vp],
     "jx_mlp_set_fused": [vp, ci],
     "jx_mlp_set_timing": [vp, ci],
+    "jx_mlp_set_dp_sharded": [vp, ci],
     "jx_mlp_step_times": [vp, C.POINTER(cf)],
     "jx_selftest_barrier_timeout": [ci, C.POINTER(ci)],
     "jx_selftest_noalloc_flag": [C.c_uint],

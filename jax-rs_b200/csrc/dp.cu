@@ -29,6 +29,8 @@ struct NcclApi {
   ncclResult_t (*CommFinalize)(ncclComm_t);
   ncclResult_t (*CommDestroy)(ncclComm_t);
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*ReduceScatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   const char* (*GetErrorString)(ncclResult_t);
   bool ok;
 };
@@ -54,6 +56,8 @@ const NcclApi* nccl() {
     g_nccl.CommFinalize = reinterpret_cast<decltype(g_nccl.CommFinalize)>(sym("ncclCommFinalize"));
     g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
     g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(sym("ncclAllReduce"));
+    g_nccl.ReduceScatter = reinterpret_cast<decltype(g_nccl.ReduceScatter)>(sym("ncclReduceScatter"));
+    g_nccl.AllGather = reinterpret_cast<decltype(g_nccl.AllGather)>(sym("ncclAllGather"));
     g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
     g_nccl.ok = ok;
   });
@@ -72,6 +76,7 @@ int nccl_fail(ncclResult_t r, const char* what) {
 struct Comm {
   ncclComm_t comm;
   int timeout_ms;
+  int rank, nranks;
 };
 
 // Polls the communicator until its pending operation leaves ncclInProgress.
@@ -107,6 +112,38 @@ int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st) {
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
   return JX_OK;
 }
+
+// In place: rank r receives the sum of every rank's [r*shard, (r+1)*shard)
+// of buf at that same offset.
+int nccl_reduce_scatter(void* comm, float* buf, long long shard, cudaStream_t st) {
+  JX_NCCL_API(api);
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  JX_REQUIRE(c && c->comm, "reduce-scatter: communicator is NULL or was aborted");
+  ncclResult_t r = api->ReduceScatter(buf, buf + (long long)c->rank * shard, (size_t)shard, ncclFloat, ncclSum,
+                                      c->comm, st);
+  if (r == ncclInProgress) return wait_comm(c, c->timeout_ms, "ncclReduceScatter");
+  if (r != ncclSuccess) return nccl_fail(r, "ncclReduceScatter");
+  return JX_OK;
+}
+
+// In place: every rank's [r*shard, (r+1)*shard) of buf goes to all ranks.
+int nccl_all_gather(void* comm, float* buf, long long shard, cudaStream_t st) {
+  JX_NCCL_API(api);
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  JX_REQUIRE(c && c->comm, "all-gather: communicator is NULL or was aborted");
+  ncclResult_t r = api->AllGather(buf + (long long)c->rank * shard, buf, (size_t)shard, ncclFloat, c->comm, st);
+  if (r == ncclInProgress) return wait_comm(c, c->timeout_ms, "ncclAllGather");
+  if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+  return JX_OK;
+}
+
+int nccl_rank(void* comm, int* rank, int* nranks) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  JX_REQUIRE(c, "communicator is NULL");
+  *rank = c->rank;
+  *nranks = c->nranks;
+  return JX_OK;
+}
 }  // namespace jx
 
 extern "C" {
@@ -137,6 +174,8 @@ int jx_nccl_init(const void* id, int nranks, int rank, int timeout_ms, void** co
   JX_NCCL_API(api);
   Comm* c = new Comm();
   c->timeout_ms = timeout_ms;
+  c->rank = rank;
+  c->nranks = nranks;
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
   ncclUniqueId uid;

@@ -23,6 +23,9 @@
 namespace jx {
 int col_sum(const float* dy, float* db, long long rows, int cols, cudaStream_t st);
 int nccl_allreduce(void* comm, float* buf, long long count, cudaStream_t st);
+int nccl_reduce_scatter(void* comm, float* buf, long long shard, cudaStream_t st);
+int nccl_all_gather(void* comm, float* buf, long long shard, cudaStream_t st);
+int nccl_rank(void* comm, int* rank, int* nranks);
 }  // namespace jx
 
 namespace {
@@ -438,6 +441,8 @@ struct jx_mlp {
   cudaStream_t cstream = nullptr;
   std::vector<cudaEvent_t> ev;
   int dw1_chunks = 2;  // row chunks of layer 1's weight gradient under data parallelism
+  int dp_rank = 0, dp_world = 1;
+  bool dp_sharded = true;  // reduce-scatter + Adam on this rank's shard + all-gather
   // phase timing (jx_mlp_set_timing): events at step start, forward end,
   // backward end on the caller's stream, and step end
   bool timing = false;
@@ -504,6 +509,35 @@ void adam_range(jx_mlp* n, long long off, long long count, cudaStream_t s) {
                                                      1.0f - n->b2);
 }
 
+// The exchange of one gradient bucket [off, off + count) under data
+// parallelism, on the communication stream, in two halves: bucket_reduce as
+// soon as backward has produced the gradient, bucket_update once nothing in
+// the step reads the bucket's parameters any more.  Sharded (the default,
+// when count divides by the rank count): reduce-scatter the gradient, Adam on
+// this rank's 1/world of the bucket, all-gather the updated parameters; the
+// same communication volume as an all-reduce, and each rank's Adam pass
+// (28 bytes of HBM traffic per parameter) shrinks by the rank count.  Each
+// rank keeps Adam moments only for its own shards.  Otherwise: all-reduce and
+// Adam over the whole bucket on every rank.
+bool bucket_sharded(const jx_mlp* n, long long count) {
+  return n->dp_sharded && n->dp_world > 1 && count % n->dp_world == 0;
+}
+
+int bucket_reduce(jx_mlp* n, long long off, long long count) {
+  if (bucket_sharded(n, count)) return jx::nccl_reduce_scatter(n->comm, n->grads + off, count / n->dp_world, n->cstream);
+  return jx::nccl_allreduce(n->comm, n->grads + off, count, n->cstream);
+}
+
+int bucket_update(jx_mlp* n, long long off, long long count) {
+  if (bucket_sharded(n, count)) {
+    const long long shard = count / n->dp_world;
+    adam_range(n, off + n->dp_rank * shard, shard, n->cstream);
+    return jx::nccl_all_gather(n->comm, n->params + off, shard, n->cstream);
+  }
+  adam_range(n, off, count, n->cstream);
+  return JX_OK;
+}
+
 // Layer 1's weight gradient under data parallelism, in n->dw1_chunks row
 // chunks: each chunk's product is all-reduced and its Adam update applied on
 // the communication stream while the next chunk's product runs.  This is the
@@ -530,8 +564,8 @@ int dw1_chunked(jx_mlp* n, cudaStream_t st, int& evi) {
     }
     // the last chunk carries the bias gradient, which follows W1 in the bucket
     const long long count = rows * N + (c == S - 1 ? N : 0);
-    rc = jx::nccl_allreduce(n->comm, gW + r0 * N, count, n->cstream);
-    if (!rc) adam_range(n, n->woff[0] + r0 * N, count, n->cstream);
+    rc = bucket_reduce(n, n->woff[0] + r0 * N, count);
+    if (!rc) rc = bucket_update(n, n->woff[0] + r0 * N, count);
   }
   return rc;
 }
@@ -539,10 +573,10 @@ int dw1_chunked(jx_mlp* n, cudaStream_t st, int& evi) {
 // One training step on stream st (forward, backward, optional all-reduce, Adam).
 //
 // With a communicator attached, layer l's gradient bucket (W_l then b_l) is
-// all-reduced on the communication stream as soon as backward has produced
-// it, and that bucket's Adam update follows on the same stream once the
-// backward GEMM that reads W_l (dh = dz W_l^T) is done; both overlap the
-// backward of the layers below.  The caller's stream waits for the
+// reduced on the communication stream as soon as backward has produced it,
+// and that bucket's Adam update (with the all-gather of the sharded form)
+// follows on the same stream once the backward GEMM that reads W_l
+// (dh = dz W_l^T) is done; both overlap the backward of the layers below.  The caller's stream waits for the
 // communication stream before the step counter moves on.
 int run_step(jx_mlp* n, cudaStream_t st) {
   int rc;
@@ -583,7 +617,7 @@ int run_step(jx_mlp* n, cudaStream_t st) {
       if ((rc = jx::col_sum(n->dz, n->grads + n->boff[l - 1], B, (int)N, st))) return rc;
       if (n->comm) {
         if ((rc = hand_off())) return rc;
-        if ((rc = jx::nccl_allreduce(n->comm, gW, bucket, n->cstream))) return rc;
+        if ((rc = bucket_reduce(n, n->woff[l - 1], bucket))) return rc;
       }
     }
     if (l > 1) {
@@ -595,7 +629,7 @@ int run_step(jx_mlp* n, cudaStream_t st) {
     }
     if (n->comm && !chunked) {
       if ((rc = hand_off())) return rc;  // W_l is no longer read by this step
-      adam_range(n, n->woff[l - 1], bucket, n->cstream);
+      if ((rc = bucket_update(n, n->woff[l - 1], bucket))) return rc;
     }
   }
   if (n->timing) JX_CUDA(cudaEventRecord(n->tev[2], st));
@@ -816,7 +850,12 @@ int jx_mlp_attach_comm(jx_mlp* n, void* comm, int world, int64_t global_batch) {
   JX_TRACE("jx_mlp_attach_comm");
   JX_REQUIRE(n && comm, "jx_mlp_attach_comm: NULL argument");
   JX_REQUIRE(world >= 1 && global_batch == n->B * world, "jx_mlp_attach_comm: global batch must be batch * world");
+  int rank = 0, nranks = 0;
+  if (int rc = jx::nccl_rank(comm, &rank, &nranks)) return rc;
+  JX_REQUIRE(nranks == world, "jx_mlp_attach_comm: the communicator has %d ranks, world is %d", nranks, world);
   n->comm = comm;
+  n->dp_rank = rank;
+  n->dp_world = world;
   n->global_B = global_batch;
   if (!n->cstream) JX_CUDA(cudaStreamCreateWithFlags(&n->cstream, cudaStreamNonBlocking));
   if (n->ev.empty()) {
@@ -896,6 +935,14 @@ int jx_selftest_barrier_timeout(int timeout_ms, int* timed_out) {
   cudaFree(buf);
   if (e != cudaSuccess) return jx::check_cuda(e, "barrier self-test");
   *timed_out = h;
+  return JX_OK;
+}
+
+int jx_mlp_set_dp_sharded(jx_mlp* n, int enable) {
+  JX_TRACE("jx_mlp_set_dp_sharded");
+  JX_REQUIRE(n, "jx_mlp_set_dp_sharded: NULL");
+  JX_REQUIRE(n->steps == 0, "jx_mlp_set_dp_sharded: set before the first step (Adam moments live with their shard)");
+  n->dp_sharded = enable != 0;
   return JX_OK;
 }
 

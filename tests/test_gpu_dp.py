@@ -1,7 +1,9 @@
 """Data-parallel training through the native trainer and NCCL.
 
 * Two ranks, each with half of the batch, must train like one rank with the
-  whole batch (sums of per-rank gradients under the global loss normaliser).
+  whole batch (sums of per-rank gradients under the global loss normaliser),
+  in the default sharded update form (reduce-scatter, Adam on each rank's
+  shard, all-gather) and in the all-reduce form.
   The small exact-precision ReLU network: losses and parameters within 1e-5.
   The wide-MLP path at reduced width (four GELU layers, 3xTF32, He-normal; its
   layer-1 gradient all-reduced in row chunks and every bucket's Adam update on
@@ -31,6 +33,7 @@ def _free_port():
 
 SMALL = {"widths": [784, 256, 128, 10], "acts": ["relu", "relu"], "exact": True, "init": "xavier"}
 WIDE = {"widths": [1024, 512, 512, 512, 512, 100], "acts": ["gelu"] * 4, "exact": False, "init": "he"}
+WIDE_ALLREDUCE = dict(WIDE, sharded=False)
 
 
 def _data(steps, batch, features=784, classes=10):
@@ -83,6 +86,8 @@ def _dp_worker(rank, world, port, steps, batch, out_dir, cfg=SMALL):
     net.set_params(_init_params(net, cfg["init"]))
     net.set_adam()
     net.attach_comm(comm, world, batch)
+    if not cfg.get("sharded", True):
+        jx.call("jx_mlp_set_dp_sharded", net.handle, 0)
     xs, ys = _data(steps, batch, cfg["widths"][0], cfg["widths"][-1])
     s = torch.cuda.current_stream().cuda_stream
     losses = []
@@ -102,7 +107,8 @@ def _dp_worker(rank, world, port, steps, batch, out_dir, cfg=SMALL):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg,steps,batch", [(SMALL, 5, 128), (WIDE, 10, 256)], ids=["small_exact", "wide_gelu_3xtf32"])
+@pytest.mark.parametrize("cfg,steps,batch", [(SMALL, 5, 128), (WIDE, 10, 256), (WIDE_ALLREDUCE, 10, 256)],
+                         ids=["small_exact", "wide_gelu_3xtf32", "wide_allreduce_form"])
 def test_two_rank_dp_matches_single_rank(jx, dev, tmp_path, cfg, steps, batch):
     import torch
     import torch.multiprocessing as mp
