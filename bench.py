@@ -1240,7 +1240,7 @@ def run_mlp(args, dist, jx, torch, steps=None, warmup=None, e2e=True):
         fw, bw, tail = (dist.max(statistics.median(p[k] for p in ph)) for k in range(3))
         line["phases_ms"] = {"forward": round(fw, 3), "backward": round(bw, 3), "tail": round(tail, 3),
                              "tail_frac": round(tail / max(fw + bw + tail, 1e-9), 4),
-                             "note": "CUDA events in separate (untimed) steps; tail = exposed all-reduce + Adam"
+                             "note": "CUDA events in separate (untimed) steps; tail = exposed gradient exchange (reduce-scatter + all-gather, or all-reduce) + Adam"
                                      if comm is not None else "CUDA events in separate (untimed) steps; tail = Adam"}
     if comm is not None:
         torch.cuda.synchronize()
