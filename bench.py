@@ -89,7 +89,7 @@ def parse():
 # proportional to it.  batchnorm sums its three kernels (the roofline covers
 # the whole call).  None for any other size.
 TRAFFIC = {
-    "sgemm": None,                           # gemm_pair_kernel, 8192^3: not captured yet
+    "sgemm": 3.1289e9 + 0.2588e9,            # gemm_pair_kernel<0,1>, 8192^3
     "chain": 1.0738e9 + 1.0275e9,            # jx_tape_kernel, 2^28
     "rowsum": 1.0738e9 + 0.0039e9,           # reduce_rows_kernel<sum>
     "argmax": 1.0738e9 + 0.0033e9,           # argreduce_rows_kernel<max>
@@ -97,7 +97,7 @@ TRAFFIC = {
     "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
     "fft2d": 8 * (0.2685e9 + 0.2158e9),      # column pass fft1024_tma_kernel, batch 32 x 8
     "conv": 2 * (0.1082e9 + 0.0551e9 + 0.1079e9 + 0.0530e9 + 0.3201e9 + 0.0709e9),  # 3 conv_gemm_kernel, B 32 x 2
-    "bgemm": None,                           # gemm_pair_kernel, [64,2048,2048]^2: not captured yet
+    "bgemm": 3.4474e9 + 1.0573e9,            # gemm_pair_kernel<0,1>, [64,2048,2048]^2
     "pool": 0.8228e9 + 0.1918e9,             # pool2d_kernel<max,3,3>, [64,256,112,112]
     "batchnorm": (0.2055e9 + 0.0036e9) + 0.0005e9 + (0.2056e9 + 0.1571e9),  # stats + finalize + apply
     "conv1d": 0.2704e9 + 0.2296e9,           # conv1d_kernel<1,3>, [64,256,4096]
