@@ -62,6 +62,34 @@ def test_fwd_dx_dw_vs_oracle(jx, dev, oracle, case):
     assert normwise_rel(dw, dw_ref) <= 1e-5
 
 
+# Shapes the SM-pair path takes for the forward and the input gradient
+# (stride 1, 2*pad = K-1, H % 4 == 0, W % 8 == 0, W <= 64, source channels a
+# multiple of 32, at least one tile of 4 image rows per SM pair): a partial
+# second output-channel tile, 5x5 taps, 1x1 taps and the widest rows.
+PAIR_CASES = [
+    (20, 64, 16, 16, 96, 3, 3, 1, 1),
+    (8, 32, 40, 24, 288, 5, 5, 1, 2),
+    (10, 32, 32, 64, 64, 1, 1, 1, 0),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES)
+def test_pair_path_vs_oracle(jx, dev, oracle, case):
+    B, C, H, W, O, KH, KW, S, P = case
+    rng = np.random.default_rng(7 + sum(case))
+    x = rng.standard_normal((B, C, H, W)).astype(np.float32)
+    w = rng.standard_normal((O, C, KH, KW)).astype(np.float32)
+    y_ref = oracle.conv2d_fwd(x, w, S, P, nthreads=8)
+    y = _conv(jx, dev, "jx_conv2d_fwd_f32", x, w, y_ref.shape, case)
+    assert np.isfinite(y).all()
+    assert normwise_rel(y, y_ref) <= 1e-5
+    g = rng.standard_normal(y_ref.shape).astype(np.float32)
+    dx_ref = oracle.conv2d_bwd_data(g, w, x.shape, S, P, nthreads=8)
+    dx = _conv(jx, dev, "jx_conv2d_bwd_data_f32", g, w, x.shape, case)
+    assert np.isfinite(dx).all()
+    assert normwise_rel(dx, dx_ref) <= 1e-5
+
+
 def test_rejects_bad_shapes(jx, dev):
     with pytest.raises(jx.JaxRsError) as e:
         jx.call("jx_conv2d_fwd_f32", 1, 1, 1, 1, 3, 4, 4, 8, 7, 7, 1, 0, None)
