@@ -36,10 +36,6 @@ int gemm_presplit_err(const float* Ah, const float* Al, const float* Bh, const f
 int gemm_split_operand(const float* src, float* hi, float* lo, int rows, int K, int Kp, long long ld, long long sb,
                        int batch, bool transposed, cudaStream_t st);
 long long gemm_kpad(long long K);
-bool pair_conv_ok(long long B, long long M, long long Cs, long long H, long long W, long long KH, long long KW,
-                  long long pad);
-int launch_pair_conv(const float* A, const float* src, float* y, long long B, long long M, long long Cs, long long H,
-                     long long W, long long KH, long long KW, long long pad, cudaStream_t st);
 }  // namespace jx
 
 namespace {
@@ -612,75 +608,6 @@ long long images_per_pass(long long B, long long per_image_floats) {
   return nb < B ? nb : B;
 }
 
-// ---- SM-pair path (stride 1, "same" padding): NHWC source + pair kernel ----
-//
-// The pair kernel's convolution mode streams its B operand from an NHWC copy
-// of the source by TMA, one {32 channels, W, 2 rows} box per k-block, shifted
-// by the k-block's filter tap; the A operand is the filter reordered so that
-// its contraction index is (tap, channel).  Forward: source x, A[o][tap][c] =
-// w[o][c][tap].  Input gradient: source dY, A[c][tap'][o] = w[o][c] at the
-// flipped tap (KH-1-kh', KW-1-kw'), which for stride 1 and 2*pad = K-1 makes
-// dX[b,c,h,w] = sum over o, taps of A . dY shifted by the tap, the same form.
-
-// dst[b][p][c] = src[b][c][p] for p < P, c < C (32 x 32 tiles through shared memory).
-__global__ void nchw_to_nhwc(const float* __restrict__ src, float* __restrict__ dst, int C, int P) {
-  __shared__ float tile[32][33];
-  const long long b = blockIdx.z;
-  const float* s = src + b * C * (long long)P;
-  float* d = dst + b * C * (long long)P;
-  const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int c = c0 + j, p = p0 + threadIdx.x;
-    if (c < C && p < P) tile[j][threadIdx.x] = __ldcs(s + (long long)c * P + p);
-  }
-  __syncthreads();
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int p = p0 + j, c = c0 + threadIdx.x;
-    if (c < C && p < P) d[(long long)p * C + c] = tile[threadIdx.x][j];
-  }
-}
-
-// flip = 0: A[o][t][c] = w[o][c][t];  flip = 1: A[c][t][o] = w[o][c][taps-1-t]
-// (t = kh*KW + kw, taps = KH*KW; flipping both kh and kw reverses t).
-__global__ void filter_to_tap_major(const float* __restrict__ w, float* __restrict__ A, int O, int C, int taps,
-                                    int flip) {
-  const long long n = (long long)O * C * taps;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    // i indexes A: rows (o, or c when flipped), then t, then the inner channel
-    const int inner = flip ? O : C, rows_inner = taps * inner;
-    const long long r = i / rows_inner;
-    const int rem = (int)(i - r * rows_inner), t = rem / inner, k = rem - t * inner;
-    const long long o = flip ? k : r, c = flip ? r : k;
-    const int tw = flip ? taps - 1 - t : t;
-    A[i] = w[(o * C + c) * taps + tw];
-  }
-}
-
-int conv_pair(const float* src, const float* w, float* out, long long B, const Geo& g, bool dx, cudaStream_t st) {
-  const long long Cs = dx ? g.O : g.C, M = dx ? g.C : g.O, taps = (long long)g.KH * g.KW;
-  const long long P = (long long)g.H * g.W;
-  void* ws = nullptr;
-  int rc = jx::scratch_get(sizeof(float) * (size_t)(B * Cs * P + M * taps * Cs), &ws, st);
-  if (rc) return rc;
-  float* src_nhwc = static_cast<float*>(ws);
-  float* A = src_nhwc + B * Cs * P;
-  nchw_to_nhwc<<<dim3((unsigned)((P + 31) / 32), (unsigned)((Cs + 31) / 32), (unsigned)B), dim3(32, 8), 0, st>>>(
-      src, src_nhwc, (int)Cs, (int)P);
-  filter_to_tap_major<<<blocks_for((M * taps * Cs + 255) / 256, 8), 256, 0, st>>>(w, A, g.O, g.C, (int)taps,
-                                                                                  dx ? 1 : 0);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) rc = jx::check_cuda(e, "conv2d: NHWC copy / filter reorder");
-  if (!rc) rc = jx::launch_pair_conv(A, src_nhwc, out, B, M, Cs, g.H, g.W, g.KH, g.KW, g.P, st);
-  const int rc2 = jx::scratch_release(ws, st);
-  return rc ? rc : rc2;
-}
-
-bool pair_conv_fits(const Geo& g, long long B, bool dx, const float* out) {
-  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  return g.S == 1 && a16(out) &&
-         jx::pair_conv_ok(B, dx ? g.C : g.O, dx ? g.O : g.C, g.H, g.W, g.KH, g.KW, g.P);
-}
-
 // ---- implicit GEMM host side ------------------------------------------------
 
 // Shapes the implicit kernel covers: a gather table that fits shared memory,
@@ -889,7 +816,6 @@ int jx_conv2d_fwd_f32(const float* x, const float* w, float* y, int64_t B, int64
   JX_REQUIRE(x && w && y, "conv2d: NULL pointer");
   cudaStream_t st = jx::as_stream(stream);
   const long long K = g.K(), Kp = jx::gemm_kpad(K), NP = g.NP();
-  if (pair_conv_fits(g, B, false, y)) return conv_pair(x, w, y, B, g, false, st);
   if (implicit_fits(g, Kp, B * NP, C * H * W)) return conv_fwd_implicit(x, w, y, B, g, st);
   const long long nb = images_per_pass(B, 2 * NP * Kp);
   void* ws = nullptr;
@@ -922,7 +848,6 @@ int jx_conv2d_bwd_data_f32(const float* dy, const float* w, float* dx, int64_t B
   if (B == 0) return JX_OK;
   JX_REQUIRE(dy && w && dx, "conv2d: NULL pointer");
   cudaStream_t st = jx::as_stream(stream);
-  if (pair_conv_fits(g, B, true, dx)) return conv_pair(dy, w, dx, B, g, true, st);
   if (implicit_fits(g, jx::gemm_kpad(O * KH * KW), B * H * W, O * (long long)g.OH * g.OW))
     return conv_bwd_data_implicit(dy, w, dx, B, g, st);
   const long long K = g.K(), Op = jx::gemm_kpad(O), NP = g.NP();

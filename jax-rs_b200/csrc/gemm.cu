@@ -651,20 +651,6 @@ int make_map_3d_fn(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1
                    uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
   return make_map_3d(map, base, d0, d1, d2, s1, s2, b0, b1, sw);
 }
-// 4-D f32 map with 128-byte swizzle: dims {d0 (contiguous) .. d3}, byte
-// strides s1..s3, box {b0, b1, b2, 1} (the convolution's NHWC source).
-int make_map_4d_fn(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
-                   uint64_t s1, uint64_t s2, uint64_t s3, uint32_t b0, uint32_t b1, uint32_t b2) {
-  cuuint64_t dims[4] = {d0, d1, d2, d3};
-  cuuint64_t strides[3] = {s1, s2, s3};
-  cuuint32_t box[4] = {b0, b1, b2, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return jx::fail(JX_ECUDA, "cuTensorMapEncodeTiled (4-D) failed (%d)", (int)r);
-  return JX_OK;
-}
 bool pair_gemm_ok(const float* A, const float* B, long long M, long long N, long long lda, long long ldb,
                   long long batch, long long sA, long long sB);
 int launch_pair_gemm(const float* A, const float* B, float* C, long long M, long long N, long long K, bool transA,

@@ -108,31 +108,12 @@ __device__ __forceinline__ void load_op(uint8_t* dst, const CUtensorMap* tm, uin
   }
 }
 
-// Convolution mode (stride 1, "same" padding, NHWC source tensor): the B
-// operand of k-block kb is tap kb / (Cs/32), channels 32*(kb % (Cs/32)) ..+31
-// of the source shifted by the tap; CTA r of a pair loads image rows
-// t0 + 2r and t0 + 2r + 1 (a {32 channels, W, 2, 1} TMA box: the tap shift
-// moves only the W and H coordinates, the zero fill outside the image is the
-// padding), so a pair tile is 256 output channels x 4 image rows (N = 4W).
-struct PairConv {
-  int H, W;          // image height and width (output = input size)
-  int Cs;            // channels of the NHWC source (multiple of 32)
-  int KW, pad;       // filter width; padding, 2*pad = KH - 1 = KW - 1
-  int tiles_per_img; // H / 4
-};
-
 // A_MN: A is transposed (stored [K][M]); B_MN: B is not transposed (stored [K][N]).
-// CONV: the convolution mode above (A and B K-major); C is then the NCHW
-// output with M channels.
-template <bool A_MN, bool B_MN, bool CONV>
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(PR_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      float* __restrict__ C, int M, int N, int num_kb, long long ldc, long long strideC, int tiles_m,
-                     int tiles_n, int num_tiles, unsigned int* err, const PairConv cv) {
-  // columns of the pair tile, rows of B per CTA, 16-byte chunks of B per stage
-  const int n_pair = CONV ? 4 * cv.W : PR_TILE;
-  const int b_rows = n_pair / 2;
-  const int b_chunks = b_rows * (BK * 4 / 16);
+                     int tiles_n, int num_tiles, unsigned int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = jxd::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -214,22 +195,12 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
       for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
         const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
         const int ya = ti.m_blk * PR_TILE + (int)rank * PR_ROWS, yb = ti.n_blk * PR_TILE + (int)rank * PR_ROWS;
-        // conv: image and first image row of this CTA's half of the tile
-        const int img = CONV ? ti.n_blk / cv.tiles_per_img : 0;
-        const int row0 = CONV ? (ti.n_blk - img * cv.tiles_per_img) * 4 + 2 * (int)rank : 0;
-        const int cblocks = CONV ? cv.Cs / BK : 1;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
           uint8_t* st = smem + stage * PR_STAGE;
-          jxd::mbar_arrive_expect_tx(&raw_full[stage], PR_OP + b_rows * BK * 4);
+          jxd::mbar_arrive_expect_tx(&raw_full[stage], 2 * PR_OP);
           load_op<A_MN>(st, &tmA, &raw_full[stage], kb, ya, ti.b);
-          if constexpr (CONV) {
-            const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * BK;
-            const int kh = tap / cv.KW, kw = tap - kh * cv.KW;
-            jxd::tma_load_4d(st + 2 * PR_OP, &tmB, &raw_full[stage], c0, kw - cv.pad, row0 + kh - cv.pad, img);
-          } else {
-            load_op<B_MN>(st + 2 * PR_OP, &tmB, &raw_full[stage], kb, yb, ti.b);
-          }
+          load_op<B_MN>(st + 2 * PR_OP, &tmB, &raw_full[stage], kb, yb, ti.b);
           if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -240,8 +211,8 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
     }
     if (warp == 1 && rank == 0 && jxd::elect_one()) {
       // ---------------- pair MMA issuer (even CTA) ----------------
-      const uint32_t idesc =
-          jxd::idesc_tf32(PR_TILE, n_pair) | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
+      constexpr uint32_t idesc =
+          jxd::idesc_tf32(PR_TILE, PR_TILE) | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
       const uint32_t smem_base = jxd::smem_u32(smem);
       int stage = 0;
       uint32_t phase = 0, span_ctr = 0;
@@ -295,13 +266,11 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < BATCH; ++j) {
             const int f = sid + 32 * PR_SPLIT_WARPS * (j0 + j);
-            if (f < PR_OP / 16 + b_chunks)
-              x[j] = *reinterpret_cast<const float4*>(st + (f < PR_OP / 16 ? f * 16 : PR_OP + f * 16));
+            x[j] = *reinterpret_cast<const float4*>(st + (f < PR_OP / 16 ? f * 16 : PR_OP + f * 16));
           }
 #pragma unroll
           for (int j = 0; j < BATCH; ++j) {
             const int f = sid + 32 * PR_SPLIT_WARPS * (j0 + j);
-            if (f >= PR_OP / 16 + b_chunks) continue;  // rows of a short B tile (conv mode)
             float4 l;
             l.x = jxd::tf32_lo_of_trunc(x[j].x);
             l.y = jxd::tf32_lo_of_trunc(x[j].y);
@@ -332,12 +301,10 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
         if (!warp_wait(&sfull[p], ph)) { ok = false; break; }
         jxd::tc_fence_after();
-        const int ncols = n_pair / 2;  // columns of this warp's half of the tile
         const uint32_t t_addr =
-            tmem_base + ((uint32_t)(q * 32) << 16) + p * (uint32_t)PR_TILE + (uint32_t)(half * ncols);
+            tmem_base + ((uint32_t)(q * 32) << 16) + p * (uint32_t)PR_TILE + (uint32_t)(half * EPI_COLS);
 #pragma unroll
         for (int c = 0; c < EPI_COLS; c += 16) {
-          if (c >= ncols) break;
           uint32_t r[16];
           jxd::tmem_ld16(t_addr + c, r);
           jxd::tmem_ld_wait();
@@ -351,20 +318,6 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
       if (!ok) break;
       const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
       const int row = ti.m_blk * PR_TILE + (int)rank * PR_ROWS + q * 32 + lane;
-      if constexpr (CONV) {
-        // NCHW: output channel `row` of image img, pixels t0*W + half*2W ..+2W
-        if (row < M) {
-          const int ncols = n_pair / 2;
-          const int img = ti.n_blk / cv.tiles_per_img;
-          const long long pix0 = (long long)(ti.n_blk - img * cv.tiles_per_img) * 4 * cv.W + half * ncols;
-          float4* dst =
-              reinterpret_cast<float4*>(C + ((long long)img * M + row) * ((long long)cv.H * cv.W) + pix0);
-#pragma unroll
-          for (int v = 0; v < EPI_COLS / 4; ++v)
-            if (4 * v < ncols) dst[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-        }
-        continue;
-      }
       if (row < M) {
         float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
         const int col0 = ti.n_blk * PR_TILE + half * EPI_COLS;
@@ -393,11 +346,11 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
 }
 
 using PairKernel = void (*)(CUtensorMap, CUtensorMap, float*, int, int, int, long long, long long, int, int, int,
-                            unsigned int*, PairConv);
+                            unsigned int*);
 
 PairKernel pair_kernel(bool a_mn, bool b_mn) {
-  if (a_mn) return b_mn ? gemm_pair_kernel<true, true, false> : gemm_pair_kernel<true, false, false>;
-  return b_mn ? gemm_pair_kernel<false, true, false> : gemm_pair_kernel<false, false, false>;
+  if (a_mn) return b_mn ? gemm_pair_kernel<true, true> : gemm_pair_kernel<true, false>;
+  return b_mn ? gemm_pair_kernel<false, true> : gemm_pair_kernel<false, false>;
 }
 
 std::mutex g_pair_mu;
@@ -405,7 +358,7 @@ std::mutex g_pair_mu;
 // Per device and variant, once: the shared-memory limit, the register count
 // the kernel was built with, and how many pairs can be resident at once.
 int pair_prepare(PairKernel k, int variant, int* regs_out, int* max_pairs_out) {
-  static int regs[64][5], max_pairs[64][5];
+  static int regs[64][4], max_pairs[64][4];
   int dev = 0;
   JX_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_pair_mu);
@@ -440,8 +393,6 @@ namespace jx {
 int get_encode_fn();
 int make_map_3d_fn(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
                    uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw);
-int make_map_4d_fn(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
-                   uint64_t s1, uint64_t s2, uint64_t s3, uint32_t b0, uint32_t b1, uint32_t b2);
 
 // Products the pair kernel takes: 16-byte aligned operands whose leading
 // dimensions and batch strides are multiples of 4 floats (TMA strides), and
@@ -501,58 +452,7 @@ int launch_pair_gemm(const float* A, const float* B, float* C, long long M, long
   float* Cp = C;
   int Mi = (int)M, Ni = (int)N, tm = tiles_m, tn = tiles_n, nti = (int)nt;
   unsigned int* errw = device_error_word();
-  PairConv cv{};
-  JX_CUDA(cudaLaunchKernelEx(&cfg, k, mA, mB, Cp, Mi, Ni, num_kb, ldc, sC, tm, tn, nti, errw, cv));
-  return JX_OK;
-}
-
-// Convolution on the pair kernel (conv mode): A [M][taps*Cs] K-major filter,
-// src the NHWC source [B][H][W][Cs], y the NCHW output [B][M][H][W].
-bool pair_conv_ok(long long B, long long M, long long Cs, long long H, long long W, long long KH, long long KW,
-                  long long pad) {
-  return Cs % BK == 0 && H % 4 == 0 && W % 8 == 0 && W <= 64 && KH == KW && 2 * pad == KH - 1 && KH * KW <= 64 &&
-         B * (H / 4) * ((M + PR_TILE - 1) / PR_TILE) >= num_sms() / 2 && B * H * W * Cs < (1LL << 40);
-}
-
-int launch_pair_conv(const float* A, const float* src, float* y, long long B, long long M, long long Cs, long long H,
-                     long long W, long long KH, long long KW, long long pad, cudaStream_t st) {
-  int rc = get_encode_fn();
-  if (rc) return rc;
-  PairKernel k = gemm_pair_kernel<false, false, true>;
-  int regs = 0, max_pairs = 0;
-  if ((rc = pair_prepare(k, 4, &regs, &max_pairs))) return rc;
-  if (regs != PR_LAUNCH_REGS)
-    return fail(JX_EUNSUPPORTED, "gemm_pair_kernel (conv) built with %d registers per thread, expected %d", regs,
-                PR_LAUNCH_REGS);
-  if (max_pairs < 1) return fail(JX_EUNSUPPORTED, "gemm_pair_kernel: no SM pair can hold a cluster");
-  const long long K = KH * KW * Cs;
-  CUtensorMap mA, mB;
-  if ((rc = make_map_3d_fn(&mA, A, K, M, 1, K * 4, K * 4 * M, BK, PR_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-  if ((rc = make_map_4d_fn(&mB, src, Cs, W, H, B, Cs * 4, Cs * W * 4, Cs * W * H * 4, BK, (uint32_t)W, 2)))
-    return rc;
-  PairConv cv{(int)H, (int)W, (int)Cs, (int)KW, (int)pad, (int)(H / 4)};
-  const int tiles_m = (int)((M + PR_TILE - 1) / PR_TILE), tiles_n = (int)(B * (H / 4));
-  const long long nt = (long long)tiles_m * tiles_n;
-  if (nt > 0x7fffffffLL) return fail(JX_EINVAL, "conv2d: too many tiles");
-  const int pairs = (int)std::min<long long>(nt, max_pairs);
-  const int num_kb = (int)(K / BK);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * pairs));
-  cfg.blockDim = dim3(PR_THREADS);
-  cfg.dynamicSmemBytes = PR_SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = 2;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  float* Cp = y;
-  int Mi = (int)M, Ni = (int)(B * H * W), tm = tiles_m, tn = tiles_n, nti = (int)nt;
-  long long ldc = 0, sC = 0;
-  unsigned int* errw = device_error_word();
-  JX_CUDA(cudaLaunchKernelEx(&cfg, k, mA, mB, Cp, Mi, Ni, num_kb, ldc, sC, tm, tn, nti, errw, cv));
+  JX_CUDA(cudaLaunchKernelEx(&cfg, k, mA, mB, Cp, Mi, Ni, num_kb, ldc, sC, tm, tn, nti, errw));
   return JX_OK;
 }
 }  // namespace jx

@@ -62,10 +62,8 @@ def test_fwd_dx_dw_vs_oracle(jx, dev, oracle, case):
     assert normwise_rel(dw, dw_ref) <= 1e-5
 
 
-# Shapes the SM-pair path takes for the forward and the input gradient
-# (stride 1, 2*pad = K-1, H % 4 == 0, W % 8 == 0, W <= 64, source channels a
-# multiple of 32, at least one tile of 4 image rows per SM pair): a partial
-# second output-channel tile, 5x5 taps, 1x1 taps and the widest rows.
+# Larger "same" convolutions: a partial second 128-row output-channel tile
+# for the forward, 5x5 taps, 1x1 taps and 64-pixel rows.
 PAIR_CASES = [
     (20, 64, 16, 16, 96, 3, 3, 1, 1),
     (8, 32, 40, 24, 288, 5, 5, 1, 2),
@@ -74,7 +72,7 @@ PAIR_CASES = [
 
 
 @pytest.mark.parametrize("case", PAIR_CASES)
-def test_pair_path_vs_oracle(jx, dev, oracle, case):
+def test_same_padding_shapes_vs_oracle(jx, dev, oracle, case):
     B, C, H, W, O, KH, KW, S, P = case
     rng = np.random.default_rng(7 + sum(case))
     x = rng.standard_normal((B, C, H, W)).astype(np.float32)
