@@ -1053,9 +1053,9 @@ def pair_ok(M, N, K, transA, transB, batch=1, sms=148):
     """Whether jx_gemm_f32 (JX_PREC_3XTF32) takes the SM-pair kernel: leading
     dimensions (contiguous operands) multiples of 4 floats and at least one
     256x256 tile per SM pair."""
-    if transA or transB:  # transposed products take the split path
-        return False
-    return K % 4 == 0 and N % 4 == 0 and -(-M // 256) * -(-N // 256) * batch >= sms // 2
+    lda = M if transA else K
+    ldb = K if transB else N
+    return lda % 4 == 0 and ldb % 4 == 0 and -(-M // 256) * -(-N // 256) * batch >= sms // 2
 
 
 def gemm_kernels(M, N, K, transA, transB, exact, batch=1, sms=148):

@@ -94,11 +94,11 @@ JX_API int jx_host_unregister(void *ptr);
 
 /* ---- GEMM (gpu_matmul src/backend/ops.rs:460-467; Array::matmul
  *      src/ops/linalg.rs:154-237; einsum "bij,bjk->bik" src/ops/einsum.rs:488-523) */
-/* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32.
- * Untransposed products with at least one 256x256 tile per SM pair and
- * TMA-compatible operands (16-byte aligned, lda/ldb/batch strides multiples
- * of 4) run on the SM-pair kernel (see JX_PREC_3XTF32_PAIR); others split the
- * operands into library scratch first. */
+/* tcgen05 kind::tf32, A=Ah+Al, B=Bh+Bl, Ah.Bh+Ah.Bl+Al.Bh in TMEM f32.  Products
+ * with at least one 256x256 tile per SM pair and TMA-compatible operands
+ * (16-byte aligned, lda/ldb/batch strides multiples of 4) run on the SM-pair
+ * kernel (see JX_PREC_3XTF32_PAIR); others split the operands into library
+ * scratch first. */
 #define JX_PREC_3XTF32 0
 #define JX_PREC_EXACT 1  /* sequential-k f32, no FMA: the reference's CPU loop order, bit-exact */
 /* JX_PREC_3XTF32 with the hi/lo split done inside the GEMM kernel from the

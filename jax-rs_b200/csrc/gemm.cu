@@ -833,12 +833,10 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
     return launch_fused_split(A, B, C, M, N, K, lda, ldb, ldc, batch, strideA, strideB, strideC, st);
   }
   JX_REQUIRE(precision == JX_PREC_3XTF32, "matmul: unknown precision %d", precision);
-  // Untransposed, with enough 256x256 tiles for every SM pair: the pair
-  // kernel splits in shared memory and needs no split pass (8192^3: 4.37 ms
-  // against 4.70 ms for the split pass plus the main kernel).  With a
-  // transposed operand the pair kernel runs at 4.90-5.00 ms, behind the split
-  // pass plus the main kernel, so those take the split path.
-  if (!transA && !transB && jx::pair_gemm_ok(A, B, M, N, lda, ldb, batch, strideA, strideB))
+  // Enough 256x256 tiles for every SM pair: the pair kernel splits in shared
+  // memory and needs no split pass (8192^3: 4.37 ms against 4.70 ms for the
+  // split pass plus the main kernel; every transposition).
+  if (jx::pair_gemm_ok(A, B, M, N, lda, ldb, batch, strideA, strideB))
     return jx::launch_pair_gemm(A, B, C, M, N, K, transA != 0, transB != 0, lda, ldb, ldc, batch, strideA, strideB,
                                 strideC, st);
   // The split pass costs about 250 * (1/M + 1/N) of the main kernel's time
