@@ -835,7 +835,10 @@ int jx_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
   JX_REQUIRE(precision == JX_PREC_3XTF32, "matmul: unknown precision %d", precision);
   // Enough 256x256 tiles for every SM pair: the pair kernel splits in shared
   // memory and needs no split pass (8192^3: 4.37 ms against 4.70 ms for the
-  // split pass plus the main kernel; every transposition).
+  // split pass plus the main kernel).  Transposed products stay on it too:
+  // it runs them at 4.90-5.00 ms, and the transposing split passes of the
+  // wide MLP's tall backward operands cost more (taking the split path for
+  // them slowed its step from 149.7k to 136.0k samples/s).
   if (jx::pair_gemm_ok(A, B, M, N, lda, ldb, batch, strideA, strideB))
     return jx::launch_pair_gemm(A, B, C, M, N, K, transA != 0, transB != 0, lda, ldb, ldc, batch, strideA, strideB,
                                 strideC, st);
