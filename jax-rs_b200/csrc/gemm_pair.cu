@@ -74,6 +74,26 @@ constexpr size_t PR_SMEM = (size_t)PR_STAGES * PR_STAGE + 1024 /*align*/ + 256 /
 static_assert(128 * PR_LOW_REGS + 128 * PR_SPLIT_REGS + 256 * PR_HIGH_REGS <= PR_THREADS * PR_LAUNCH_REGS,
               "register split exceeds the launch allocation");
 
+// Tile t of a [batch][tiles_m][tiles_n] grid of pair tiles, grouped
+// PR_GROUP_M row blocks at a time so the pairs of one wave share A and B
+// tiles in L2.
+constexpr int PR_GROUP_M = 8;
+__device__ __forceinline__ TileInfo pair_tile_coords(int t, int tiles_m, int tiles_n) {
+  const int per_batch = tiles_m * tiles_n;
+  const int b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int in_group = PR_GROUP_M * tiles_n;
+  const int g = r / in_group;
+  const int first_m = g * PR_GROUP_M;
+  const int gsize = min(tiles_m - first_m, PR_GROUP_M);
+  const int local = r - g * in_group;
+  TileInfo ti;
+  ti.m_blk = first_m + local % gsize;
+  ti.n_blk = local / gsize;
+  ti.b = b;
+  return ti;
+}
+
 __device__ __forceinline__ bool wait_cl(uint64_t* bar, uint32_t parity, unsigned int* err) {
   if (jxd::mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = global_ns();
@@ -193,7 +213,7 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
-        const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+        const TileInfo ti = pair_tile_coords(t, tiles_m, tiles_n);
         const int ya = ti.m_blk * PR_TILE + (int)rank * PR_ROWS, yb = ti.n_blk * PR_TILE + (int)rank * PR_ROWS;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
@@ -316,7 +336,7 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         if (!group_arrive(&gempty[p], ph, sempty0 + p * 8, gt == 0)) { ok = false; break; }
       }
       if (!ok) break;
-      const TileInfo ti = tile_coords(t, tiles_m, tiles_n);
+      const TileInfo ti = pair_tile_coords(t, tiles_m, tiles_n);
       const int row = ti.m_blk * PR_TILE + (int)rank * PR_ROWS + q * 32 + lane;
       if (row < M) {
         float* crow = C + (long long)ti.b * strideC + (long long)row * ldc;
