@@ -185,3 +185,24 @@ def test_many_small_products_default_precision(jx, dev, oracle):
         assert normwise_rel(c[i], oracle.matmul(a[i], b[i], nthreads=8)) <= TOL
     assert normwise_rel(c.astype(np.float64).sum(axis=1), np.einsum("bij,bjk->bk", a.astype(np.float64),
                                                                     b.astype(np.float64))) <= TOL
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 520, 1000), (2304, 2304, 512)], ids=["split_path", "pair_kernel"])
+def test_non_finite_operands_mark_the_same_outputs(jx, dev, oracle, M, N, K):
+    """An infinite or NaN operand element: the 3xTF32 product is non-finite
+    exactly where the reference's loop (src/ops/linalg.rs:220-228) is, and
+    every other output keeps the normwise tolerance.  (Where the reference
+    gives +-inf the 3xTF32 value can be NaN: the infinite hi part meets the
+    other operand's lo part, which may be zero or of the other sign.)"""
+    rng = np.random.default_rng(M)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    a[7, 3] = np.inf
+    a[M - 2, K - 1] = np.nan
+    b[5, N // 2] = -np.inf
+    c = _gemm(jx, dev, a, b, jx.PREC_3XTF32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        ref = a.astype(np.float64) @ b.astype(np.float64)
+    bad = ~np.isfinite(ref)
+    assert np.array_equal(~np.isfinite(c), bad)
+    assert normwise_rel(c[~bad], ref[~bad]) <= TOL
