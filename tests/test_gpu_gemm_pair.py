@@ -92,3 +92,23 @@ def test_pair_precision_rejects_too_few_tiles(jx, dev):
         jx.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), 256, 256, 256, precision=jx.PREC_3XTF32_PAIR,
                 stream=dev.stream)
     assert e.value.status == jx.JX_EINVAL and "SM pair" in e.value.message
+
+
+def test_pair_padded_output_rows_and_batch_stride(jx, dev, oracle):
+    """C with ldc > N and a batch stride beyond M*ldc: the pair kernel writes
+    only the product's columns, the padding keeps its sentinel."""
+    bt, M, N, K = 3, 1024, 1536, 200
+    ldc, sC = N + 12, (1024 + 3) * (N + 12)
+    rng = np.random.default_rng(41)
+    a = rng.uniform(-1, 1, (bt, M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (bt, K, N)).astype(np.float32)
+    A, B = dev.put(a), dev.put(b)
+    Cbuf = dev.full((bt * sC,), -5.0)
+    jx.gemm(A.data_ptr(), B.data_ptr(), Cbuf.data_ptr(), M, N, K, ldc=ldc, batch=bt, strideA=M * K,
+            strideB=K * N, strideC=sC, precision=jx.PREC_3XTF32_PAIR, stream=dev.stream)
+    c = dev.get(Cbuf)
+    for i in range(bt):
+        blk = c[i * sC:i * sC + M * ldc].reshape(M, ldc)
+        assert normwise_rel(blk[:, :N], a[i].astype(np.float64) @ b[i].astype(np.float64)) <= TOL
+        assert (blk[:, N:] == -5.0).all()
+        assert (c[i * sC + M * ldc:(i + 1) * sC] == -5.0).all()
