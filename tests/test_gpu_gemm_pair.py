@@ -97,7 +97,7 @@ def test_pair_precision_rejects_too_few_tiles(jx, dev):
 def test_pair_padded_output_rows_and_batch_stride(jx, dev, oracle):
     """C with ldc > N and a batch stride beyond M*ldc: the pair kernel writes
     only the product's columns, the padding keeps its sentinel."""
-    bt, M, N, K = 3, 1024, 1536, 200
+    bt, M, N, K = 4, 1024, 1536, 200  # 4 x 4 x 6 = 96 pair tiles
     ldc, sC = N + 12, (1024 + 3) * (N + 12)
     rng = np.random.default_rng(41)
     a = rng.uniform(-1, 1, (bt, M, K)).astype(np.float32)
