@@ -379,6 +379,17 @@ JX_API int jx_conv2d_bwd_data_f32(const float *dy, const float *w, float *dx, in
 JX_API int jx_conv2d_bwd_filter_f32(const float *x, const float *dy, float *dw, int64_t B, int64_t C, int64_t H,
                              int64_t W, int64_t O, int64_t KH, int64_t KW, int64_t stride, int64_t pad,
                              jx_stream_t stream);
+/* Kernel of the implicit convolutions above (no reference counterpart; for
+ * tests and tuning), process-wide.  JX_CONV_AUTO: the SM-pair kernel
+ * (tcgen05 cta_group::2, 256x256 tiles) when the pass has at least one tile
+ * per SM pair, else the one-CTA kernel (128x256 tiles).  The two compute the
+ * same sums in the same order.  Shapes beyond the implicit kernels (more
+ * than 4096 gathered indices or 32 filter taps) take the explicit path
+ * whatever the setting.  Returns JX_EINVAL for another value. */
+#define JX_CONV_AUTO 0
+#define JX_CONV_ONE_CTA 1
+#define JX_CONV_PAIR 2
+JX_API int jx_conv_set_kernel(int which);
 
 /* ---- layers: conv1d, pooling, normalisation ------------------------------- */
 /* gpu_conv1d (src/backend/ops.rs:1014-1025; shader src/backend/shaders.rs:449-519),

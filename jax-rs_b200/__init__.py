@@ -21,6 +21,7 @@ JX_OK, JX_EINVAL, JX_ENOMEM, JX_ECUDA, JX_ENCCL, JX_ETIMEOUT, JX_EUNSUPPORTED, J
 STATUS_NAMES = {0: "JX_OK", 1: "JX_EINVAL", 2: "JX_ENOMEM", 3: "JX_ECUDA", 4: "JX_ENCCL", 5: "JX_ETIMEOUT",
                 6: "JX_EUNSUPPORTED", 7: "JX_EDEVICE", 8: "JX_EINTERNAL"}
 PREC_3XTF32, PREC_EXACT, PREC_3XTF32_FUSED, PREC_3XTF32_PAIR = 0, 1, 2, 3
+CONV_AUTO, CONV_ONE_CTA, CONV_PAIR = 0, 1, 2  # jx_conv_set_kernel
 POOL_MAX, POOL_AVG = 0, 1
 BIN = {"add": 0, "sub": 1, "mul": 2, "div": 3, "pow": 4, "min": 5, "max": 6}
 UN = {"neg": 0, "abs": 1, "sin": 2, "cos": 3, "tanh": 4, "exp": 5, "log": 6, "sqrt": 7, "recip": 8,
@@ -125,6 +126,7 @@ _SIGS = {
     "jx_max_rows_vjp_f32": [vp, vp, vp, i64, i64, vp],
     "jx_fft_c2c_f32": [vp, vp, i64, i64, ci, vp],
     "jx_fft2_c2c_f32": [vp, vp, i64, i64, i64, ci, vp],
+    "jx_conv_set_kernel": [ci],
     "jx_conv2d_fwd_f32": [vp, vp, vp] + [i64] * 9 + [vp],
     "jx_conv2d_bwd_data_f32": [vp, vp, vp] + [i64] * 9 + [vp],
     "jx_conv2d_bwd_filter_f32": [vp, vp, vp] + [i64] * 9 + [vp],

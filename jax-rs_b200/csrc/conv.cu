@@ -26,6 +26,8 @@
 // indices, more than 32 filter taps) take the explicit path:
 // fused im2col+split producers into scratch, the plain GEMM, col2im.
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "tc_gemm.cuh"
 
@@ -184,6 +186,11 @@ using jxg::SPAN_KB;
 using jxg::STAGE_BYTES;
 using jxg::STAGES;
 using jxg::TMEM_COLS;
+using jxg::PAIR_OP;
+using jxg::PAIR_ROWS;
+using jxg::PAIR_TILE;
+using jxg::TileInfo;
+using jxg::pair_tile_coords;
 
 // Warps: warpgroup 0 = TMA (warp 0), MMA issuer and TMEM owner (warp 1), two
 // idle warps; warpgroups 1 and 2 (warps 4..11) gather, drain and store.  The
@@ -225,6 +232,9 @@ struct ImplicitArgs {
   unsigned npo_m, ow_m;              // q / NPo and p / OW as multiply-high (Granlund-Montgomery)
   int npo_l, ow_l;
   long long ldc, strideC;            // row-major partial outputs per slice
+  int Ksp;                           // per-slice stride of the contraction (k-blocks * BK)
+  const uint2* pixtab;               // conv_pair_kernel, cols mode: per contraction position
+                                     // (offset of its base from src, tap mask), [slices][Ksp]
 };
 
 // Table of the gathered index: TAB_FWD (c,kh,kw) over x; TAB_DX (o,kh,kw)
@@ -276,6 +286,118 @@ __device__ __forceinline__ float gather_one(const float* base, int off, uint32_t
       : "+f"(v)
       : "l"(base + off), "r"(ok));
   return v;
+}
+
+// Rows mode (forward, input gradient): the base pointer and tap mask of B
+// row n, the flattened output pixel (forward) or input pixel (input
+// gradient) n = b * NPpix + p.  Rows past N keep mask 0 (zeros).
+__device__ __forceinline__ void row_position(const float* src, long long n, const ImplicitArgs& a, const float*& base,
+                                             uint32_t& mask) {
+  if (n >= a.N) return;
+  const long long b = n / a.NPpix;
+  const int p = (int)(n - b * a.NPpix);
+  const int ph = p / a.PW, pw = p - (p / a.PW) * a.PW;
+  int qh, qw, rh = 0, rw = 0;
+  if (a.dx_mode) {
+    const int th = ph + a.P, tw = pw + a.P;
+    qh = th / a.S;
+    rh = th - qh * a.S;
+    qw = tw / a.S;
+    rw = tw - qw * a.S;
+  } else {
+    qh = ph * a.S - a.P;
+    qw = pw * a.S - a.P;
+  }
+  mask = tap_mask(qh, qw, rh, rw, a, a.dx_mode != 0);
+  base = src + (b * a.img_stride + (long long)qh * a.LW + qw);
+}
+
+// Cols mode (weight gradient): the base pointer and tap mask of contraction
+// position jq of slice `slice`, the output pixel q = slice * Ks + jq of all
+// images; positions past the slice or past Q get mask 0.
+__device__ __forceinline__ void col_offset(int jq, int slice, const ImplicitArgs& a, long long& off, uint32_t& gmask) {
+  const long long q = (long long)slice * a.Ks + jq;
+  gmask = 0;
+  off = 0;
+  if (jq < a.Ks && q < a.Q) {
+    const int qi = (int)q;
+    // qi < 2^31: n / d = (umulhi(n, m) + n) >> l with the host's (m, l)
+    const int b = (int)((__umulhi((unsigned)qi, a.npo_m) + (unsigned)qi) >> a.npo_l);
+    const int p = qi - b * a.NPo;
+    const int oh = (int)((__umulhi((unsigned)p, a.ow_m) + (unsigned)p) >> a.ow_l), ow = p - oh * a.OW;
+    const int qh = oh * a.S - a.P, qw = ow * a.S - a.P;
+    gmask = tap_mask(qh, qw, 0, 0, a, false);
+    off = (long long)b * a.img_stride + (long long)qh * a.LW + qw;
+  }
+}
+__device__ __forceinline__ void col_position(const float* src, int jq, int slice, const ImplicitArgs& a,
+                                             const float*& gbase, uint32_t& gmask) {
+  long long off;
+  col_offset(jq, slice, a, off, gmask);
+  if (gmask) gbase = src + off;
+}
+
+// The cols-mode position table of conv_pair_kernel: entry s * Ksp + j =
+// (offset from src of position j of slice s, its tap mask), mask 0 past the
+// slice or past Q.  Offsets fit 32 bits (the host checks the whole tensor).
+__global__ void build_pixel_table(uint2* __restrict__ tq, long long n, const ImplicitArgs a) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int s = (int)(i / a.Ksp), j = (int)(i - (long long)s * a.Ksp);
+    long long off;
+    uint32_t m;
+    col_offset(j, s, a, off, m);
+    tq[i] = make_uint2((uint32_t)(int)off, m);
+  }
+}
+
+// Store one epilogue thread's EPI_COLS outputs of row m, columns n0.. of the
+// GEMM.  Rows mode: NCHW, out[b, m, p] for the flattened pixel n = b * NPpix
+// + p; cols mode: row-major partial output of slice b.
+template <bool COLS>
+__device__ __forceinline__ void store_tile(const float (&acc)[EPI_COLS], const ImplicitArgs& a, int m, long long n0,
+                                           int slice, float* __restrict__ out) {
+  if (m >= a.M) return;
+  if constexpr (!COLS) {
+    long long b = n0 / a.NPpix;
+    int p = (int)(n0 - b * a.NPpix);
+    float* ob = out + b * a.out_img_stride + (long long)m * a.NPpix;
+    const long long nlim = a.N - n0;
+    if ((a.NPpix & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+      for (int v4 = 0; v4 < EPI_COLS / 4; ++v4) {
+        if (4 * v4 < nlim)
+          *reinterpret_cast<float4*>(ob + p) = make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
+        p += 4;
+        if (p == a.NPpix) {
+          p = 0;
+          ob += a.out_img_stride;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j) {
+        if (j < nlim) ob[p] = acc[j];
+        if (++p == a.NPpix) {
+          p = 0;
+          ob += a.out_img_stride;
+        }
+      }
+    }
+  } else {
+    float* crow = out + (long long)slice * a.strideC + (long long)m * a.ldc;
+    const long long nlim = a.N - n0;
+    if ((a.ldc & 3) == 0 && (a.strideC & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+        nlim >= EPI_COLS) {
+      float4* dst = reinterpret_cast<float4*>(crow + n0);
+#pragma unroll
+      for (int v4 = 0; v4 < EPI_COLS / 4; ++v4)
+        dst[v4] = make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j)
+        if (j < nlim) crow[n0 + j] = acc[j];
+    }
+  }
 }
 
 // COLS = false: forward / input gradient (B rows = pixels, k = gathered index)
@@ -369,27 +491,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       // rows mode: this thread's B row is one pixel for the whole tile
       const float* base = src;
       uint32_t mask = 0;
-      if constexpr (!COLS) {
-        const long long n = (long long)ti.n_blk * BN + gw * 32 + lane;
-        if (n < a.N) {
-          const long long b = n / a.NPpix;
-          const int p = (int)(n - b * a.NPpix);
-          const int ph = p / a.PW, pw = p - (p / a.PW) * a.PW;
-          int qh, qw, rh = 0, rw = 0;
-          if (a.dx_mode) {
-            const int th = ph + a.P, tw = pw + a.P;
-            qh = th / a.S;
-            rh = th - qh * a.S;
-            qw = tw / a.S;
-            rw = tw - qw * a.S;
-          } else {
-            qh = ph * a.S - a.P;
-            qw = pw * a.S - a.P;
-          }
-          mask = tap_mask(qh, qw, rh, rw, a, a.dx_mode != 0);
-          base = src + (b * a.img_stride + (long long)qh * a.LW + qw);
-        }
-      }
+      if constexpr (!COLS) row_position(src, (long long)ti.n_blk * BN + gw * 32 + lane, a, base, mask);
       bool ok = true;
       int spans_done = 0;
       const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
@@ -397,22 +499,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       auto gather = [&](float (&v)[32], int kb) {
         const float* gbase = base;
         uint32_t gmask = mask;
-        if constexpr (COLS) {
-          // this lane's contraction position: output pixel q of slice ti.b
-          const int jq = kb * BK + lane;
-          const long long q = (long long)ti.b * a.Ks + jq;
-          gmask = 0;
-          if (jq < a.Ks && q < a.Q) {
-            const int qi = (int)q;
-            // qi < 2^31: n / d = (umulhi(n, m) + n) >> l with the host's (m, l)
-            const int b = (int)((__umulhi((unsigned)qi, a.npo_m) + (unsigned)qi) >> a.npo_l);
-            const int p = qi - b * a.NPo;
-            const int oh = (int)((__umulhi((unsigned)p, a.ow_m) + (unsigned)p) >> a.ow_l), ow = p - oh * a.OW;
-            const int qh = oh * a.S - a.P, qw = ow * a.S - a.P;
-            gmask = tap_mask(qh, qw, 0, 0, a, false);
-            gbase = src + ((long long)b * a.img_stride + (long long)qh * a.LW + qw);
-          }
-        }
+        if constexpr (COLS) col_position(src, kb * BK + lane, ti.b, a, gbase, gmask);
         const uint4* te = reinterpret_cast<const uint4*>(COLS ? tab + ti.n_blk * BN + gw * 32 : tab + kb * BK);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -490,53 +577,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       }
       if (!ok) break;
       // ---- store ----
-      const int m = ti.m_blk * BM + q4 * 32 + lane;
-      if (m < a.M) {
-        const long long n0 = (long long)ti.n_blk * BN + half * EPI_COLS;
-        if constexpr (!COLS) {
-          // NCHW: out[b, m, p] for the flattened pixel n = b * NPpix + p
-          long long b = n0 / a.NPpix;
-          int p = (int)(n0 - b * a.NPpix);
-          float* ob = out + b * a.out_img_stride + (long long)m * a.NPpix;
-          const long long nlim = a.N - n0;
-          if ((a.NPpix & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-#pragma unroll
-            for (int v4 = 0; v4 < EPI_COLS / 4; ++v4) {
-              if (4 * v4 < nlim)
-                *reinterpret_cast<float4*>(ob + p) =
-                    make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
-              p += 4;
-              if (p == a.NPpix) {
-                p = 0;
-                ob += a.out_img_stride;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < EPI_COLS; ++j) {
-              if (j < nlim) ob[p] = acc[j];
-              if (++p == a.NPpix) {
-                p = 0;
-                ob += a.out_img_stride;
-              }
-            }
-          }
-        } else {
-          float* crow = out + (long long)ti.b * a.strideC + (long long)m * a.ldc;
-          const long long nlim = a.N - n0;
-          if ((a.ldc & 3) == 0 && (a.strideC & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
-              nlim >= EPI_COLS) {
-            float4* dst = reinterpret_cast<float4*>(crow + n0);
-#pragma unroll
-            for (int v4 = 0; v4 < EPI_COLS / 4; ++v4)
-              dst[v4] = make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < EPI_COLS; ++j)
-              if (j < nlim) crow[n0 + j] = acc[j];
-          }
-        }
-      }
+      store_tile<COLS>(acc, a, ti.m_blk * BM + q4 * 32 + lane, (long long)ti.n_blk * BN + half * EPI_COLS, ti.b,
+                       out);
     }
   }
 
@@ -546,6 +588,310 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     jxd::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Implicit GEMM on SM pairs
+// ---------------------------------------------------------------------------
+// conv_pair_kernel: the same three convolutions on the pair MMA
+// (tcgen05.mma.cta_group::2, a 256 x 256 tile per cluster of two CTAs).
+// CTA r of the pair holds rows 128r.. of the tile's A operand (the filter's
+// or dY's hi and lo, by TMA) and gathers rows 128r.. of its B operand, so an
+// SM gathers 128 B rows per k-block instead of conv_gemm_kernel's 256 for
+// the same tensor-core work, and a stage takes 64 KB instead of 96, which
+// leaves room for three stages instead of two.
+//
+//   warp 0 (each CTA)    TMA: this CTA's A hi / lo slices
+//   warp 1 (even CTA)    TMEM (both CTAs) + the pair MMA issuer
+//   warp 2 (each CTA)    forwards gfull[s] completions to the even CTA's full[s]
+//   warp 3 (each CTA)    forwards gempty[p] completions to the even CTA's sempty[p]
+//   warps 4..11 (each)   gather B, drain the TMEM spans, store
+// The forwarders keep the gathering warps from ever waiting on their own
+// group: a warp arrives locally and moves on to its next k-block.
+//
+// Rows mode: B row = one pixel; the two warps of a TMEM lane quarter share
+// 32 pixels and take 16 of the k-block's 32 gathered indices each.  Cols
+// mode: B row = one gathered index; a thread takes 4 rows at 4 consecutive
+// output pixels of the k-block, whose base offsets and tap masks come from a
+// table built once per call (build_pixel_table), and writes one 16-byte
+// chunk per row.
+//
+// Handshakes (every wait bounded, about 4 s, then JX_DEVERR_TIMEOUT):
+//   gfull[s]  (each CTA)  TMA's expect_tx arrival + one per gathering warp
+//   full[s]   (even CTA)  one arrival per CTA, by its warp 2 once gfull[s]
+//                         completes (cluster-scope release)
+//   empty[s]  (each CTA)  the pair's MMAs on stage s retired (multicast commit)
+//   sfull[p]  (each CTA)  span buffer p holds a finished partial (multicast)
+//   gempty[p] (each CTA)  one arrival per draining warp; sempty[p] (even
+//                         CTA) one per CTA, by its warp 3
+constexpr int CP_STAGES = 3;
+// k-blocks whose gathers are in flight ahead of the one being written
+// (forward at [64,256,56,56]: 1.149 / 0.973 / 1.022 ms with 1 / 2 / 3 ahead;
+// from 3 ahead the gathering warps spill)
+constexpr int CP_AHEAD = 2;
+constexpr int CP_STAGE = 4 * PAIR_OP;  // [A hi][A lo][B hi][B lo], 16 KB each
+constexpr size_t CP_SMEM = (size_t)CP_STAGES * CP_STAGE + BAR_BYTES + TABLE_MAX * 8 + 1024 /*align*/;
+static_assert(CP_SMEM <= 232448, "conv_pair_kernel shared memory exceeds the per-block limit");
+static_assert(EPI_COLS == PAIR_TILE / 2, "two draining warps per TMEM lane quarter split the tile's columns");
+static_assert(BN == PAIR_TILE, "gather tables are padded to whole tiles of either kernel");
+
+template <bool COLS>
+__global__ void __launch_bounds__(CONV_THREADS, 1)
+    conv_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                     const float* __restrict__ src, const uint2* __restrict__ table, const ImplicitArgs a,
+                     float* __restrict__ out, unsigned int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = jxd::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CP_STAGES * CP_STAGE);
+  uint64_t* gfull = bars;                       // [CP_STAGES] local
+  uint64_t* full = bars + CP_STAGES;            // [CP_STAGES] (even CTA)
+  uint64_t* empty = bars + 2 * CP_STAGES;       // [CP_STAGES]
+  uint64_t* sfull = bars + 3 * CP_STAGES;       // [2]
+  uint64_t* sempty = bars + 3 * CP_STAGES + 2;  // [2] (even CTA)
+  uint64_t* gempty = bars + 3 * CP_STAGES + 4;  // [2] local
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * CP_STAGES + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint2* tab = reinterpret_cast<uint2*>(smem + CP_STAGES * CP_STAGE + BAR_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = jxd::cluster_ctarank();  // 0 or 1 within the pair
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_kb = a.num_kb;
+
+  for (int i = threadIdx.x; i < a.table_n; i += blockDim.x) tab[i] = table[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CP_STAGES; ++s) {
+      jxd::mbar_init(&gfull[s], 1 + EPI_WARPS);
+      jxd::mbar_init(&full[s], 2);
+      jxd::mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      jxd::mbar_init(&sfull[s], 1);
+      jxd::mbar_init(&sempty[s], 2);
+      jxd::mbar_init(&gempty[s], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    jxd::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    jxd::tma_prefetch_desc(&tmAh);
+    jxd::tma_prefetch_desc(&tmAl);
+  }
+  if (warp == 1) {
+    jxd::tmem_alloc_pair(tmem_slot, 2 * PAIR_TILE);
+    jxd::tmem_relinquish_pair();
+  }
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::cluster_sync_all();  // the peer's barriers are initialised before anyone signals them
+  jxd::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full0 = jxd::mapa_shared(&full[0], 0), sempty0 = jxd::mapa_shared(&sempty[0], 0);
+
+  if (warp < CONV_FIRST_EPI) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CONV_LOW_REGS));
+    if (warp == 0 && jxd::elect_one()) {
+      // ---------------- TMA: this CTA's A hi / lo slices ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < a.num_tiles && !*abort_flag; t += npairs) {
+        const TileInfo ti = pair_tile_coords(t, a.tiles_m, a.tiles_n);
+        const int ya = ti.m_blk * PAIR_TILE + (int)rank * PAIR_ROWS, za = a.a_bcast ? 0 : ti.b;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          uint8_t* st = smem + stage * CP_STAGE;
+          jxd::mbar_arrive_expect_tx(&gfull[stage], 2 * PAIR_OP);
+          jxd::tma_load_3d(st, &tmAh, &gfull[stage], kb * BK, ya, za);
+          jxd::tma_load_3d(st + PAIR_OP, &tmAl, &gfull[stage], kb * BK, ya, za);
+          if (++stage == CP_STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      for (int s = 0; s < CP_STAGES; ++s) {
+        if (!jxg::wait_bounded(&empty[stage], phase ^ 1u, err)) break;
+        if (++stage == CP_STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    if (warp == 1 && rank == 0 && jxd::elect_one())
+      // ---------------- pair MMA issuer (even CTA) ----------------
+      jxg::pair_mma_issuer<false, false, CP_STAGES, CP_STAGE>(jxd::smem_u32(smem), full, empty, sfull, sempty,
+                                                              tmem_base, pair, a.num_tiles, npairs, num_kb, abort_flag,
+                                                              err);
+    if (warp == 2 && jxd::elect_one()) {
+      // ---------------- forward "stage written" to the even CTA ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < a.num_tiles; t += npairs)
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (*abort_flag || !jxg::wait_bounded(&gfull[stage], phase, err)) { *abort_flag = 1; ok = false; break; }
+          jxd::mbar_arrive_cluster(full0 + stage * 8);
+          if (++stage == CP_STAGES) { stage = 0; phase ^= 1u; }
+        }
+    }
+    if (warp == 3 && jxd::elect_one()) {
+      // ---------------- forward "span drained" to the even CTA ----------------
+      const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
+      uint32_t span_ctr = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < a.num_tiles; t += npairs)
+        for (int sp = 0; sp < nspan; ++sp, ++span_ctr) {
+          const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+          if (*abort_flag || !jxg::wait_bounded(&gempty[p], ph, err)) { *abort_flag = 1; ok = false; break; }
+          jxd::mbar_arrive_cluster(sempty0 + p * 8);
+        }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CONV_HIGH_REGS));
+    // ---------------- gather B, drain spans, store (warps 4..11) ----------------
+    const int gw = warp - CONV_FIRST_EPI;  // 0..7
+    const int q4 = warp & 3, half = gw >> 2;
+    const int rg = gw * 4 + (lane >> 3), pg = lane & 7;  // cols mode: row group, position group
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t span_ctr = 0;
+    bool ok = true;
+    for (int t = pair; ok && t < a.num_tiles; t += npairs) {
+      const TileInfo ti = pair_tile_coords(t, a.tiles_m, a.tiles_n);
+      float acc[EPI_COLS];
+#pragma unroll
+      for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+      // rows mode: this thread's B row is one pixel for the whole tile
+      const float* base = src;
+      uint32_t mask = 0;
+      if constexpr (!COLS)
+        row_position(src, (long long)ti.n_blk * PAIR_TILE + (int)rank * PAIR_ROWS + q4 * 32 + lane, a, base, mask);
+      int spans_done = 0;
+      const int nspan = (num_kb + SPAN_KB - 1) / SPAN_KB;
+      // gather(v, kb): issue k-block kb's 16 loads of this thread (no wait on the stage).
+      auto gather = [&](float (&v)[16], int kb) {
+        if constexpr (!COLS) {
+          const uint4* te = reinterpret_cast<const uint4*>(tab + kb * BK + half * 16);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 e = te[i];
+            v[2 * i] = gather_one(base, (int)e.x, e.y & mask);
+            v[2 * i + 1] = gather_one(base, (int)e.z, e.w & mask);
+          }
+        } else {
+          // rows 4 rg .. 4 rg + 3 at the k-block's positions 4 pg .. 4 pg + 3:
+          // two 16-byte loads of the position table, two of the row table
+          const uint4* pq = reinterpret_cast<const uint4*>(a.pixtab + (long long)ti.b * a.Ksp + kb * BK + 4 * pg);
+          const uint4 p01 = __ldg(pq), p23 = __ldg(pq + 1);
+          const uint4* te = reinterpret_cast<const uint4*>(tab + ti.n_blk * PAIR_TILE + (int)rank * PAIR_ROWS + 4 * rg);
+          const uint4 r01 = te[0], r23 = te[1];
+          const int po[4] = {(int)p01.x, (int)p01.z, (int)p23.x, (int)p23.z};
+          const uint32_t pm[4] = {p01.y, p01.w, p23.y, p23.w};
+          const uint32_t ro[4] = {r01.x, r01.z, r23.x, r23.z};
+          const uint32_t rm[4] = {r01.y, r01.w, r23.y, r23.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[4 * i + j] = gather_one(src + po[j], (int)ro[i], rm[i] & pm[j]);
+        }
+      };
+      // drain(): add span partial span_ctr into acc and hand its buffer back.
+      auto drain = [&]() -> bool {
+        const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+        if (!jxg::warp_wait_bounded(&sfull[p], ph, abort_flag, err)) return false;
+        jxd::tc_fence_after();
+        const uint32_t t_addr =
+            tmem_base + ((uint32_t)(q4 * 32) << 16) + p * (uint32_t)PAIR_TILE + (uint32_t)(half * EPI_COLS);
+#pragma unroll
+        for (int c = 0; c < EPI_COLS; c += 16) {
+          uint32_t r[16];
+          jxd::tmem_ld16(t_addr + c, r);
+          jxd::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c + j] = __fadd_rn(acc[c + j], __uint_as_float(r[j]));
+        }
+        jxd::tc_fence_before();
+        ++span_ctr;
+        ++spans_done;
+        __syncwarp();
+        if (lane == 0) jxd::mbar_arrive(&gempty[p]);  // warp 3 forwards the group's completion
+        return true;
+      };
+      // publish(v, kb): wait for the stage, write v as tf32 hi/lo, hand the
+      // stage to the pair (once TMA's A slices have landed too), and drain a
+      // span partial when one is due.
+      auto publish = [&](float (&v)[16], int kb) -> bool {
+        if (!jxg::warp_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, err)) return false;
+        uint8_t* bh = smem + stage * CP_STAGE + 2 * PAIR_OP;
+        if constexpr (!COLS) {
+          // row q4*32+lane, 16-byte chunks 4*half..4*half+3 of its 128-byte row, 128-byte swizzle
+          const int row = q4 * 32 + lane;
+          uint8_t* rp = bh + row * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float4 h, l;
+            jxd::split_tf32(v[4 * c], h.x, l.x);
+            jxd::split_tf32(v[4 * c + 1], h.y, l.y);
+            jxd::split_tf32(v[4 * c + 2], h.z, l.z);
+            jxd::split_tf32(v[4 * c + 3], h.w, l.w);
+            const int off = ((4 * half + c) ^ (row & 7)) << 4;
+            *reinterpret_cast<float4*>(rp + off) = h;
+            *reinterpret_cast<float4*>(rp + PAIR_OP + off) = l;
+          }
+        } else {
+          // rows 4 rg + i: positions 4 pg .. 4 pg + 3 are 16-byte chunk pg of the row
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int row = 4 * rg + i;
+            float4 h, l;
+            jxd::split_tf32(v[4 * i], h.x, l.x);
+            jxd::split_tf32(v[4 * i + 1], h.y, l.y);
+            jxd::split_tf32(v[4 * i + 2], h.z, l.z);
+            jxd::split_tf32(v[4 * i + 3], h.w, l.w);
+            const int off = row * 128 + ((pg ^ (row & 7)) << 4);
+            *reinterpret_cast<float4*>(bh + off) = h;
+            *reinterpret_cast<float4*>(bh + PAIR_OP + off) = l;
+          }
+        }
+        jxd::fence_proxy_async_smem();  // make the generic-proxy writes visible to the tensor cores
+        __syncwarp();
+        if (lane == 0) jxd::mbar_arrive(&gfull[stage]);  // warp 2 forwards the stage's completion
+        if (++stage == CP_STAGES) { stage = 0; phase ^= 1u; }
+        // Once span i is fully written, drain span i-1 (its MMAs have been
+        // issued before any of span i's could be).
+        if ((kb % SPAN_KB == SPAN_KB - 1 || kb == num_kb - 1) && kb >= SPAN_KB)
+          if (!drain()) return false;
+        return true;
+      };
+      // Software pipeline over CP_AHEAD + 1 register buffers: the loads of
+      // k-blocks kb+1 .. kb+CP_AHEAD are in flight while k-block kb waits
+      // for its stage and is written (half-rows make a buffer 16 values, so
+      // four of them cost what conv_gemm_kernel's two full rows do).
+      float v[CP_AHEAD + 1][16];
+#pragma unroll
+      for (int j = 0; j < CP_AHEAD; ++j)
+        if (j < num_kb) gather(v[j], j);
+      for (int kb0 = 0; ok && kb0 < num_kb; kb0 += CP_AHEAD + 1) {
+#pragma unroll
+        for (int j = 0; j <= CP_AHEAD; ++j) {
+          const int kb = kb0 + j;
+          if (kb >= num_kb) break;
+          if (kb + CP_AHEAD < num_kb) gather(v[(j + CP_AHEAD) % (CP_AHEAD + 1)], kb + CP_AHEAD);
+          if (!publish(v[j], kb)) { ok = false; break; }
+        }
+      }
+      while (ok && spans_done < nspan)
+        if (!drain()) ok = false;
+      if (!ok) break;
+      store_tile<COLS>(acc, a, ti.m_blk * PAIR_TILE + (int)rank * PAIR_ROWS + q4 * 32 + lane,
+                       (long long)ti.n_blk * PAIR_TILE + half * EPI_COLS, ti.b, out);
+    }
+  }
+
+  jxd::tc_fence_before();
+  __syncthreads();
+  jxd::cluster_sync_all();  // neither CTA leaves while its peer may still signal it
+  jxd::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    jxd::tmem_dealloc_pair(tmem_base, 2 * PAIR_TILE);
   }
 }
 
@@ -647,6 +993,102 @@ int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, cons
   return JX_OK;
 }
 
+// ---- SM-pair launcher --------------------------------------------------------
+
+std::atomic<int> g_conv_kernel{JX_CONV_AUTO};
+std::mutex g_conv_pair_mu;
+
+// Whether a pass with `pair_tiles` 256 x 256 tiles runs on conv_pair_kernel.
+bool conv_use_pair(long long pair_tiles) {
+  const int k = g_conv_kernel.load();
+  if (k == JX_CONV_ONE_CTA) return false;
+  if (k == JX_CONV_PAIR) return true;
+  return pair_tiles >= jx::num_sms() / 2;
+}
+
+// Per device and mode, once: the shared-memory limit, the register count the
+// kernel was built with, and how many pairs can be resident at once.
+template <bool COLS>
+int conv_pair_prepare(int* regs_out, int* max_pairs_out) {
+  static int regs[64], max_pairs[64];
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_conv_pair_mu);
+  if (!regs[dev & 63]) {
+    auto k = conv_pair_kernel<COLS>;
+    cudaFuncAttributes fa;
+    JX_CUDA(cudaFuncGetAttributes(&fa, k));
+    JX_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CP_SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)jx::num_sms());
+    cfg.blockDim = dim3(CONV_THREADS);
+    cfg.dynamicSmemBytes = CP_SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    JX_CUDA(cudaOccupancyMaxActiveClusters(&clusters, (void*)k, &cfg));
+    max_pairs[dev & 63] = clusters;
+    regs[dev & 63] = fa.numRegs;
+  }
+  *regs_out = regs[dev & 63];
+  *max_pairs_out = max_pairs[dev & 63];
+  return JX_OK;
+}
+
+// a.tiles_m / tiles_n / num_tiles count 256 x 256 pair tiles.
+template <bool COLS>
+int launch_conv_pair(const float* Ah, const float* Al, int a_batch, int Kp, const float* src, const uint2* tab,
+                     const ImplicitArgs& a, float* out, cudaStream_t st) {
+  CUtensorMap mAh, mAl;
+  int rc = jx::gemm_make_kmajor_map(&mAh, Ah, Kp, a.M, a_batch, PAIR_ROWS);
+  if (!rc) rc = jx::gemm_make_kmajor_map(&mAl, Al, Kp, a.M, a_batch, PAIR_ROWS);
+  if (rc) return rc;
+  int regs = 0, max_pairs = 0;
+  if ((rc = conv_pair_prepare<COLS>(&regs, &max_pairs))) return rc;
+  // The register split inside the kernel assumes exactly CONV_LAUNCH_REGS per
+  // thread at launch; with any other allocation setmaxnreg.inc could wait for
+  // registers that never come, so refuse to launch.
+  if (regs != CONV_LAUNCH_REGS)
+    return jx::fail(JX_EUNSUPPORTED, "conv_pair_kernel built with %d registers per thread, expected %d", regs,
+                    CONV_LAUNCH_REGS);
+  if (max_pairs < 1) return jx::fail(JX_EUNSUPPORTED, "conv_pair_kernel: no SM pair can hold a cluster");
+  if (a.num_tiles == 0) return JX_OK;
+  const int pairs = std::min(a.num_tiles, max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(CONV_THREADS);
+  cfg.dynamicSmemBytes = CP_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  unsigned int* errw = jx::device_error_word();
+  JX_CUDA(cudaLaunchKernelEx(&cfg, conv_pair_kernel<COLS>, mAh, mAl, src, tab, a, out, errw));
+  return JX_OK;
+}
+
+// Tile counts of a pass with M GEMM rows, N columns and `slices` batch
+// entries, for the kernel it runs on, then the launch.
+template <bool COLS>
+int launch_implicit(bool pair, const float* Ah, const float* Al, int a_batch, int Kp, const float* src,
+                    const uint2* tab, ImplicitArgs a, int slices, float* out, cudaStream_t st) {
+  const int tm = pair ? PAIR_TILE : BM, tn = pair ? PAIR_TILE : BN;
+  a.tiles_m = (a.M + tm - 1) / tm;
+  a.tiles_n = (a.N + tn - 1) / tn;
+  a.num_tiles = a.tiles_m * a.tiles_n * slices;
+  return pair ? launch_conv_pair<COLS>(Ah, Al, a_batch, Kp, src, tab, a, out, st)
+              : launch_conv_gemm<COLS>(Ah, Al, a_batch, Kp, src, tab, a, out, st);
+}
+
 int table_build(uint2* tab, int n, int count, int mode, const Geo& g, cudaStream_t st) {
   build_gather_table<<<(n + 255) / 256, 256, 0, st>>>(tab, n, count, mode, g);
   JX_LAUNCH_CHECK("build_gather_table");
@@ -668,9 +1110,6 @@ int conv_fwd_implicit(const float* x, const float* w, float* y, long long B, con
     a.M = g.O;
     a.N = (int)(B * NP);
     a.num_kb = (int)(Kp / BK);
-    a.tiles_m = (g.O + BM - 1) / BM;
-    a.tiles_n = (a.N + BN - 1) / BN;
-    a.num_tiles = a.tiles_m * a.tiles_n;
     a.a_bcast = 1;
     a.table_n = (int)Kp;
     a.LH = g.H;
@@ -684,7 +1123,8 @@ int conv_fwd_implicit(const float* x, const float* w, float* y, long long B, con
     a.NPpix = (int)NP;
     a.dx_mode = 0;
     a.out_img_stride = (long long)g.O * NP;
-    rc = launch_conv_gemm<false>(Wh, Wl, 1, (int)Kp, x, tab, a, y, st);
+    const bool pair = conv_use_pair((long long)((a.M + PAIR_TILE - 1) / PAIR_TILE) * ((a.N + PAIR_TILE - 1) / PAIR_TILE));
+    rc = launch_implicit<false>(pair, Wh, Wl, 1, (int)Kp, x, tab, a, 1, y, st);
   }
   const int rc2 = jx::scratch_release(ws, st);
   return rc ? rc : rc2;
@@ -707,9 +1147,6 @@ int conv_bwd_data_implicit(const float* dy, const float* w, float* dx, long long
     a.M = g.C;
     a.N = (int)(B * g.H * g.W);
     a.num_kb = (int)(Kdp / BK);
-    a.tiles_m = (g.C + BM - 1) / BM;
-    a.tiles_n = (a.N + BN - 1) / BN;
-    a.num_tiles = a.tiles_m * a.tiles_n;
     a.a_bcast = 1;
     a.table_n = (int)Kdp;
     a.LH = g.OH;
@@ -723,16 +1160,18 @@ int conv_bwd_data_implicit(const float* dy, const float* w, float* dx, long long
     a.NPpix = g.H * g.W;
     a.dx_mode = 1;
     a.out_img_stride = (long long)g.C * g.H * g.W;
-    rc = launch_conv_gemm<false>(Ah, Al, 1, (int)Kdp, dy, tab, a, dx, st);
+    const bool pair = conv_use_pair((long long)((a.M + PAIR_TILE - 1) / PAIR_TILE) * ((a.N + PAIR_TILE - 1) / PAIR_TILE));
+    rc = launch_implicit<false>(pair, Ah, Al, 1, (int)Kdp, dy, tab, a, 1, dx, st);
   }
   const int rc2 = jx::scratch_release(ws, st);
   return rc ? rc : rc2;
 }
 
 // Slices of the weight-gradient contraction: the count in [1, 64] (each slice
-// at least 1024 long) whose tile count fills the SMs' last wave best.
-long long dw_slices(long long tiles, long long Q) {
-  const long long sms = jx::num_sms();
+// at least 1024 long) whose tile count fills the last wave of `units`
+// resident tiles (SMs, or SM pairs) best.
+long long dw_slices(long long tiles, long long Q, long long units) {
+  const long long sms = units;
   long long best = 1;
   double best_eff = -1.0;
   for (long long S = 1; S <= 64; ++S) {
@@ -750,18 +1189,25 @@ long long dw_slices(long long tiles, long long Q) {
 
 int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long long B, const Geo& g, cudaStream_t st) {
   const long long K = g.K(), NP = g.NP(), Q = B * NP;
+  // SM pairs when their tiles, sliced to fill the pairs, reach one per pair
+  const long long pair_tiles = (long long)((g.O + PAIR_TILE - 1) / PAIR_TILE) * ((K + PAIR_TILE - 1) / PAIR_TILE);
+  const long long pair_slices = dw_slices(pair_tiles, Q, jx::num_sms() / 2);
+  // the pair kernel's position table holds 32-bit offsets into the whole x
+  const bool pair = B * g.C * g.H * g.W < (1LL << 31) && conv_use_pair(pair_tiles * pair_slices);
   const int tiles_m = (g.O + BM - 1) / BM, tiles_n = (int)((K + BN - 1) / BN);
-  const long long S = dw_slices((long long)tiles_m * tiles_n, Q);
+  const long long S = pair ? pair_slices : dw_slices((long long)tiles_m * tiles_n, Q, jx::num_sms());
   const long long Ks = (Q + S - 1) / S, Ksp = jx::gemm_kpad(Ks);
-  const long long tab_n = (long long)tiles_n * BN;
+  const long long tab_n = (long long)tiles_n * BN;  // BN = PAIR_TILE: whole tiles of either kernel
   void* ws = nullptr;
-  const size_t floats = (size_t)(2 * S * g.O * Ksp + 2 * tab_n + (S > 1 ? S * g.O * K : 0));
+  const long long pix_n = pair ? S * Ksp : 0;  // position table entries
+  const size_t floats = (size_t)(2 * S * g.O * Ksp + 2 * tab_n + 2 * pix_n + (S > 1 ? S * g.O * K : 0));
   int rc = jx::scratch_get(sizeof(float) * floats, &ws, st);
   if (rc) return rc;
   float* Ah = reinterpret_cast<float*>(ws);
   float* Al = Ah + S * g.O * Ksp;
   uint2* tab = reinterpret_cast<uint2*>(Al + S * g.O * Ksp);
-  float* part = S > 1 ? reinterpret_cast<float*>(tab + tab_n) : dw;
+  uint2* pixtab = tab + tab_n;  // 16-byte aligned: Ksp and tab_n are multiples of 32
+  float* part = S > 1 ? reinterpret_cast<float*>(pixtab + pix_n) : dw;
   dy_rows_split<<<blocks_for(S * g.O, 16), 256, 0, st>>>(dy, Ah, Al, Q, Ks, (int)Ksp, (int)S, g);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) rc = jx::check_cuda(e, "dy_rows_split");
@@ -771,9 +1217,6 @@ int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long lo
     a.M = g.O;
     a.N = (int)K;
     a.num_kb = (int)(Ksp / BK);
-    a.tiles_m = tiles_m;
-    a.tiles_n = tiles_n;
-    a.num_tiles = (int)(tiles_m * tiles_n * S);
     a.a_bcast = 0;
     a.table_n = (int)tab_n;
     a.LH = g.H;
@@ -791,7 +1234,14 @@ int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long lo
     magic_div((unsigned)a.OW, a.ow_m, a.ow_l);
     a.ldc = K;
     a.strideC = (long long)g.O * K;
-    rc = launch_conv_gemm<true>(Ah, Al, (int)S, (int)Ksp, x, tab, a, part, st);
+    a.Ksp = (int)Ksp;
+    a.pixtab = pixtab;
+    if (pair) {
+      build_pixel_table<<<blocks_for((pix_n + 255) / 256, 8), 256, 0, st>>>(pixtab, pix_n, a);
+      const cudaError_t e2 = cudaGetLastError();
+      if (e2 != cudaSuccess) rc = jx::check_cuda(e2, "build_pixel_table");
+    }
+    if (!rc) rc = launch_implicit<true>(pair, Ah, Al, (int)S, (int)Ksp, x, tab, a, (int)S, part, st);
   }
   if (!rc && S > 1) {
     slice_sum<<<blocks_for((g.O * K + 255) / 256, 8), 256, 0, st>>>(part, dw, g.O * K, (int)S);
@@ -805,6 +1255,14 @@ int conv_bwd_filter_implicit(const float* x, const float* dy, float* dw, long lo
 }  // namespace
 
 extern "C" {
+
+int jx_conv_set_kernel(int which) {
+  JX_TRACE("jx_conv_set_kernel");
+  JX_REQUIRE(which == JX_CONV_AUTO || which == JX_CONV_ONE_CTA || which == JX_CONV_PAIR,
+             "jx_conv_set_kernel: unknown kernel %d", which);
+  g_conv_kernel.store(which);
+  return JX_OK;
+}
 
 int jx_conv2d_fwd_f32(const float* x, const float* w, float* y, int64_t B, int64_t C, int64_t H, int64_t W, int64_t O,
                       int64_t KH, int64_t KW, int64_t stride, int64_t pad, jx_stream_t stream) {

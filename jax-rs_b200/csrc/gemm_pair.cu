@@ -55,10 +55,10 @@ namespace {
 
 using namespace jxg;
 
-constexpr int PR_ROWS = 128;                                // rows of A (and columns of B) per CTA
-constexpr int PR_TILE = 256;                                // output tile edge per pair
+constexpr int PR_ROWS = PAIR_ROWS;                          // rows of A (and columns of B) per CTA
+constexpr int PR_TILE = PAIR_TILE;                          // output tile edge per pair
 constexpr int PR_STAGES = 3;
-constexpr int PR_OP = PR_ROWS * BK * 4;                     // 16 KB: one operand's raw (or lo) tile per CTA
+constexpr int PR_OP = PAIR_OP;                              // 16 KB: one operand's raw (or lo) tile per CTA
 constexpr int PR_STAGE = 4 * PR_OP;                         // [A raw][A lo][B raw][B lo]
 constexpr int PR_THREADS = 512;
 constexpr int PR_FIRST_SPLIT = 4;                           // warps 4..7: the split warpgroup
@@ -68,51 +68,11 @@ constexpr int PR_LAUNCH_REGS = 128;
 constexpr int PR_LOW_REGS = 40;                             // TMA / MMA warpgroup
 constexpr int PR_SPLIT_REGS = 72;
 constexpr int PR_HIGH_REGS = 200;
-constexpr int PR_BOX = 32 * BK * 4;                         // one 32 x 32 MN-major box: 4 KB
+constexpr int PR_BOX = PAIR_BOX;                             // one 32 x 32 MN-major box: 4 KB
 constexpr uint32_t PR_TMEM_COLS = 2 * PR_TILE;              // two span buffers of 256 columns
 constexpr size_t PR_SMEM = (size_t)PR_STAGES * PR_STAGE + 1024 /*align*/ + 256 /*barriers*/;
 static_assert(128 * PR_LOW_REGS + 128 * PR_SPLIT_REGS + 256 * PR_HIGH_REGS <= PR_THREADS * PR_LAUNCH_REGS,
               "register split exceeds the launch allocation");
-
-// Tile t of a [batch][tiles_m][tiles_n] grid of pair tiles, grouped
-// PR_GROUP_M row blocks at a time so the pairs of one wave share A and B
-// tiles in L2.
-constexpr int PR_GROUP_M = 8;
-__device__ __forceinline__ TileInfo pair_tile_coords(int t, int tiles_m, int tiles_n) {
-  const int per_batch = tiles_m * tiles_n;
-  const int b = t / per_batch;
-  const int r = t - b * per_batch;
-  const int in_group = PR_GROUP_M * tiles_n;
-  const int g = r / in_group;
-  const int first_m = g * PR_GROUP_M;
-  const int gsize = min(tiles_m - first_m, PR_GROUP_M);
-  const int local = r - g * in_group;
-  TileInfo ti;
-  ti.m_blk = first_m + local % gsize;
-  ti.n_blk = local / gsize;
-  ti.b = b;
-  return ti;
-}
-
-__device__ __forceinline__ bool wait_cl(uint64_t* bar, uint32_t parity, unsigned int* err) {
-  if (jxd::mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (true) {
-    for (int i = 0; i < 256; ++i)
-      if (jxd::mbar_try_wait_cluster(bar, parity)) return true;
-    if (global_ns() - t0 > 4000000000ull) {
-      atomicOr(err, JX_DEVERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-// Shared-memory descriptor of k-step k (8 of the stage's 32 k) of a 128-row operand tile.
-template <bool MN>
-__device__ __forceinline__ uint64_t op_desc(uint32_t base, int k) {
-  if constexpr (MN) return jxd::smem_desc_mn_sw128_32b(base + k * 1024, PR_BOX);
-  else return jxd::smem_desc_k_sw128(base + k * 32);
-}
 
 // TMA of one CTA's 128-row slice of an operand for k-block kb: `row0` is the
 // slice's first row (M for A, N for B).  K-major: one 32 x 128 box;
@@ -183,27 +143,11 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t full0 = jxd::mapa_shared(&full[0], 0), sempty0 = jxd::mapa_shared(&sempty[0], 0);
 
-  // A bounded wait whose outcome is the same in every lane of the warp (the
-  // warp is converged again on return, as tcgen05.ld needs).
   auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
-    const bool got = !*abort_flag && wait_bounded(bar, parity, err);
-    if (__all_sync(0xffffffffu, got)) return true;
-    *abort_flag = 1;
-    return false;
+    return warp_wait_bounded(bar, parity, abort_flag, err);
   };
-  // Every warp of a group arrives on the local barrier `gbar`; the group's
-  // first thread (`first`) waits for all of them (bounded), then alone
-  // signals the even CTA's barrier at `cluster_bar`.  Warp-uniform outcome.
   auto group_arrive = [&](uint64_t* gbar, uint32_t parity, uint32_t cluster_bar, bool first) -> bool {
-    __syncwarp();
-    if (lane == 0) jxd::mbar_arrive(gbar);
-    int ok = 1;
-    if (first) {
-      ok = wait_bounded(gbar, parity, err) ? 1 : 0;
-      if (ok) jxd::mbar_arrive_cluster(cluster_bar);
-      else *abort_flag = 1;
-    }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+    return group_arrive_cluster(gbar, parity, cluster_bar, first, lane, abort_flag, err);
   };
 
   if (warp < PR_FIRST_SPLIT) {
@@ -229,41 +173,10 @@ __global__ void __launch_bounds__(PR_THREADS, 1)
         if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
       }
     }
-    if (warp == 1 && rank == 0 && jxd::elect_one()) {
+    if (warp == 1 && rank == 0 && jxd::elect_one())
       // ---------------- pair MMA issuer (even CTA) ----------------
-      constexpr uint32_t idesc =
-          jxd::idesc_tf32(PR_TILE, PR_TILE) | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
-      const uint32_t smem_base = jxd::smem_u32(smem);
-      int stage = 0;
-      uint32_t phase = 0, span_ctr = 0;
-      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
-        for (int kb0 = 0; kb0 < num_kb && !*abort_flag; kb0 += SPAN_KB) {
-          const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
-          if (!wait_cl(&sempty[p], ph ^ 1u, err)) { *abort_flag = 1; break; }
-          jxd::tc_fence_after();
-          const uint32_t d_tmem = tmem_base + p * (uint32_t)PR_TILE;
-          const int kb_end = min(kb0 + SPAN_KB, num_kb);
-          for (int kb = kb0; kb < kb_end; ++kb) {
-            if (!wait_cl(&full[stage], phase, err)) { *abort_flag = 1; break; }
-            jxd::tc_fence_after();
-            const uint32_t sa = smem_base + stage * PR_STAGE;
-            const uint32_t sb = sa + 2 * PR_OP;
-#pragma unroll
-            for (int k = 0; k < BK / 8; ++k) {
-              const uint64_t ah = op_desc<A_MN>(sa, k), al = op_desc<A_MN>(sa + PR_OP, k);
-              const uint64_t bh = op_desc<B_MN>(sb, k), bl = op_desc<B_MN>(sb + PR_OP, k);
-              jxd::mma_tf32_pair(d_tmem, al, bh, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-              jxd::mma_tf32_pair(d_tmem, ah, bl, idesc, 1u);
-              jxd::mma_tf32_pair(d_tmem, ah, bh, idesc, 1u);
-            }
-            jxd::mma_commit_pair(&empty[stage], 0x3);  // frees stage s in both CTAs
-            if (++stage == PR_STAGES) { stage = 0; phase ^= 1u; }
-          }
-          jxd::mma_commit_pair(&sfull[p], 0x3);  // span partial ready in both CTAs' TMEM
-          ++span_ctr;
-        }
-      }
-    }
+      pair_mma_issuer<A_MN, B_MN, PR_STAGES, PR_STAGE>(jxd::smem_u32(smem), full, empty, sfull, sempty, tmem_base,
+                                                       pair, num_tiles, npairs, num_kb, abort_flag, err);
   } else if (warp < PR_FIRST_EPI) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PR_SPLIT_REGS));
     // ---------------- split (warps 4..7): lo next to every raw value ----------------

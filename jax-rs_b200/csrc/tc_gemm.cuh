@@ -194,6 +194,129 @@ __device__ __forceinline__ bool drain_span(float (&acc)[EPI_COLS], uint32_t tmem
   return true;
 }
 
+// ---- SM pairs (cta_group::2) -------------------------------------------------
+// A cluster of two CTAs owns a PAIR_TILE x PAIR_TILE output tile; CTA r holds
+// rows PAIR_ROWS*r.. of the A tile and of the B tile (K-major: the N rows of
+// B^T) in the same stage layout [A hi][A lo][B hi][B lo], PAIR_OP bytes each,
+// and its TMEM receives its PAIR_ROWS rows of the product.
+constexpr int PAIR_TILE = 256;
+constexpr int PAIR_ROWS = 128;
+constexpr int PAIR_OP = PAIR_ROWS * BK * 4;  // 16 KB
+constexpr int PAIR_BOX = 32 * BK * 4;        // one 32 x 32 MN-major box: 4 KB
+
+// Tile t of a [batch][tiles_m][tiles_n] grid of pair tiles, grouped
+// PAIR_GROUP_M row blocks at a time so the pairs of one wave share A and B
+// tiles in L2.
+constexpr int PAIR_GROUP_M = 8;
+__device__ __forceinline__ TileInfo pair_tile_coords(int t, int tiles_m, int tiles_n) {
+  const int per_batch = tiles_m * tiles_n;
+  const int b = t / per_batch;
+  const int r = t - b * per_batch;
+  const int in_group = PAIR_GROUP_M * tiles_n;
+  const int g = r / in_group;
+  const int first_m = g * PAIR_GROUP_M;
+  const int gsize = min(tiles_m - first_m, PAIR_GROUP_M);
+  const int local = r - g * in_group;
+  TileInfo ti;
+  ti.m_blk = first_m + local % gsize;
+  ti.n_blk = local / gsize;
+  ti.b = b;
+  return ti;
+}
+
+// wait_bounded with cluster-scope acquire: for barriers that receive the
+// other CTA's arrivals.
+__device__ __forceinline__ bool wait_bounded_cluster(uint64_t* bar, uint32_t parity, unsigned int* err) {
+  if (jxd::mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    for (int i = 0; i < 256; ++i)
+      if (jxd::mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_ns() - t0 > 4000000000ull) {
+      atomicOr(err, JX_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// A bounded wait whose outcome is the same in every lane of the warp (the
+// warp is converged again on return, as tcgen05.ld needs).
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned int* err) {
+  const bool got = !*abort_flag && wait_bounded(bar, parity, err);
+  if (__all_sync(0xffffffffu, got)) return true;
+  *abort_flag = 1;
+  return false;
+}
+
+// Every warp of a group arrives on the local barrier `gbar`; the group's
+// first thread (`first`) waits for its phase to complete (bounded), then
+// alone arrives, with release at cluster scope, on the even CTA's barrier at
+// shared::cluster address `cluster_bar`: one cluster-scope release per group
+// instead of one per warp.  Warp-uniform outcome.
+__device__ __forceinline__ bool group_arrive_cluster(uint64_t* gbar, uint32_t parity, uint32_t cluster_bar, bool first,
+                                                     int lane, volatile int* abort_flag, unsigned int* err) {
+  __syncwarp();
+  if (lane == 0) jxd::mbar_arrive(gbar);
+  int ok = 1;
+  if (first) {
+    ok = wait_bounded(gbar, parity, err) ? 1 : 0;
+    if (ok) jxd::mbar_arrive_cluster(cluster_bar);
+    else *abort_flag = 1;
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Shared-memory descriptor of k-step k (8 of the stage's 32 k) of a 128-row operand tile.
+template <bool MN>
+__device__ __forceinline__ uint64_t pair_op_desc(uint32_t base, int k) {
+  if constexpr (MN) return jxd::smem_desc_mn_sw128_32b(base + k * 1024, PAIR_BOX);
+  else return jxd::smem_desc_k_sw128(base + k * 32);
+}
+
+// The single-thread pair MMA issuer (even CTA): for every tile of this pair,
+// Al.Bh + Ah.Bl + Ah.Bh per k-step into one of two TMEM span buffers of
+// PAIR_TILE columns.  full[s] and sempty[p] live in the even CTA and collect
+// one arrival per CTA; empty[s] and sfull[p] are committed to both CTAs.
+// A_MN / B_MN: the operand tiles are MN-major (SWIZZLE_128B_ATOM_32B boxes).
+template <bool A_MN, bool B_MN, int NSTAGE, int STAGE_BYTES_>
+__device__ __forceinline__ void pair_mma_issuer(uint32_t smem_base, uint64_t* full, uint64_t* empty, uint64_t* sfull,
+                                                uint64_t* sempty, uint32_t tmem_base, int first_tile, int num_tiles,
+                                                int tile_step, int num_kb, volatile int* abort_flag,
+                                                unsigned int* err) {
+  constexpr uint32_t idesc =
+      jxd::idesc_tf32(PAIR_TILE, PAIR_TILE) | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
+  int stage = 0;
+  uint32_t phase = 0, span_ctr = 0;
+  for (int t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
+    for (int kb0 = 0; kb0 < num_kb && !*abort_flag; kb0 += SPAN_KB) {
+      const uint32_t p = span_ctr & 1u, ph = (span_ctr >> 1) & 1u;
+      if (!wait_bounded_cluster(&sempty[p], ph ^ 1u, err)) { *abort_flag = 1; break; }
+      jxd::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + p * (uint32_t)PAIR_TILE;
+      const int kb_end = min(kb0 + SPAN_KB, num_kb);
+      for (int kb = kb0; kb < kb_end; ++kb) {
+        if (!wait_bounded_cluster(&full[stage], phase, err)) { *abort_flag = 1; break; }
+        jxd::tc_fence_after();
+        const uint32_t sa = smem_base + stage * STAGE_BYTES_;
+        const uint32_t sb = sa + 2 * PAIR_OP;
+#pragma unroll
+        for (int k = 0; k < BK / 8; ++k) {
+          const uint64_t ah = pair_op_desc<A_MN>(sa, k), al = pair_op_desc<A_MN>(sa + PAIR_OP, k);
+          const uint64_t bh = pair_op_desc<B_MN>(sb, k), bl = pair_op_desc<B_MN>(sb + PAIR_OP, k);
+          jxd::mma_tf32_pair(d_tmem, al, bh, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          jxd::mma_tf32_pair(d_tmem, ah, bl, idesc, 1u);
+          jxd::mma_tf32_pair(d_tmem, ah, bh, idesc, 1u);
+        }
+        jxd::mma_commit_pair(&empty[stage], 0x3);  // frees stage s in both CTAs
+        if (++stage == NSTAGE) { stage = 0; phase ^= 1u; }
+      }
+      jxd::mma_commit_pair(&sfull[p], 0x3);  // span partial ready in both CTAs' TMEM
+      ++span_ctr;
+    }
+  }
+}
+
 }  // namespace jxg
 
 namespace jx {

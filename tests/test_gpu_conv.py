@@ -9,6 +9,16 @@ from conftest import normwise_rel
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["one_cta", "pair"])
+def kernel(jx, request):
+    """Runs the test on each implicit kernel (one-CTA 128x256 tiles, SM-pair
+    256x256 tiles); the automatic choice takes the pair kernel only once a
+    pass has a tile per SM pair, which these shapes mostly do not."""
+    jx.call("jx_conv_set_kernel", jx.CONV_ONE_CTA if request.param == "one_cta" else jx.CONV_PAIR)
+    yield request.param
+    jx.call("jx_conv_set_kernel", jx.CONV_AUTO)
+
+
 def _conv(jx, dev, name, a, b, out_shape, geo):
     A, Bt = dev.put(a), dev.put(b)
     Y = dev.full(out_shape, np.nan)
@@ -45,7 +55,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", CASES)
-def test_fwd_dx_dw_vs_oracle(jx, dev, oracle, case):
+def test_fwd_dx_dw_vs_oracle(jx, dev, oracle, kernel, case):
     B, C, H, W, O, KH, KW, S, P = case
     rng = np.random.default_rng(sum(case))
     x = rng.standard_normal((B, C, H, W)).astype(np.float32)
@@ -72,7 +82,7 @@ PAIR_CASES = [
 
 
 @pytest.mark.parametrize("case", PAIR_CASES)
-def test_same_padding_shapes_vs_oracle(jx, dev, oracle, case):
+def test_same_padding_shapes_vs_oracle(jx, dev, oracle, kernel, case):
     B, C, H, W, O, KH, KW, S, P = case
     rng = np.random.default_rng(7 + sum(case))
     x = rng.standard_normal((B, C, H, W)).astype(np.float32)
@@ -86,6 +96,16 @@ def test_same_padding_shapes_vs_oracle(jx, dev, oracle, case):
     dx = _conv(jx, dev, "jx_conv2d_bwd_data_f32", g, w, x.shape, case)
     assert np.isfinite(dx).all()
     assert normwise_rel(dx, dx_ref) <= 1e-5
+    dw_ref = oracle.conv2d_bwd_filter(x, g, w.shape, S, P, nthreads=8)
+    dw = _conv(jx, dev, "jx_conv2d_bwd_filter_f32", x, g, w.shape, case)
+    assert np.isfinite(dw).all()
+    assert normwise_rel(dw, dw_ref) <= 1e-5
+
+
+def test_set_kernel_rejects_unknown(jx):
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.call("jx_conv_set_kernel", 7)
+    assert e.value.status == jx.JX_EINVAL
 
 
 def test_rejects_bad_shapes(jx, dev):
@@ -94,6 +114,35 @@ def test_rejects_bad_shapes(jx, dev):
     assert "Kernel height too large" in e.value.message
     with pytest.raises(jx.JaxRsError):
         jx.call("jx_conv2d_fwd_f32", 1, 1, 1, 1, 3, 4, 4, 8, 3, 3, 0, 0, None)
+
+
+def test_pair_and_one_cta_kernels_agree(jx, dev):
+    """Both implicit kernels split the operands the same way and promote the
+    same 128-long partial sums, on a shape large enough for the automatic
+    choice to take the pair kernel (batch 16 of 256 x 28 x 28, 3x3)."""
+    import torch
+    B, C, H, W, O, K = 16, 256, 28, 28, 256, 3
+    geo = (B, C, H, W, O, K, K, 1, 1)
+    g_ = torch.Generator(device="cuda")
+    g_.manual_seed(9)
+    X = torch.randn((B, C, H, W), device="cuda", generator=g_)
+    Wt = torch.randn((O, C, K, K), device="cuda", generator=g_)
+    G = torch.randn((B, O, H, W), device="cuda", generator=g_)
+    outs = {}
+    try:
+        for which in (jx.CONV_ONE_CTA, jx.CONV_PAIR):
+            jx.call("jx_conv_set_kernel", which)
+            Y, DX, DW = torch.empty_like(G), torch.empty_like(X), torch.empty_like(Wt)
+            jx.call("jx_conv2d_fwd_f32", X.data_ptr(), Wt.data_ptr(), Y.data_ptr(), *geo, dev.stream)
+            jx.call("jx_conv2d_bwd_data_f32", G.data_ptr(), Wt.data_ptr(), DX.data_ptr(), *geo, dev.stream)
+            jx.call("jx_conv2d_bwd_filter_f32", X.data_ptr(), G.data_ptr(), DW.data_ptr(), *geo, dev.stream)
+            dev.sync()
+            outs[which] = [t.cpu().numpy() for t in (Y, DX, DW)]
+    finally:
+        jx.call("jx_conv_set_kernel", jx.CONV_AUTO)
+    for a, b in zip(outs[jx.CONV_ONE_CTA], outs[jx.CONV_PAIR]):
+        assert np.isfinite(b).all()
+        assert normwise_rel(b, a) <= 1e-6
 
 
 def test_full_config_sampled_image_and_adjoint_identity(jx, dev, oracle):
