@@ -109,27 +109,39 @@ __global__ void im2col_cols_split(const float* __restrict__ x, float* __restrict
 }
 
 // Weight-gradient A operand: for slice s, row o holds dY[b, o, p] at q = b*P + p.
+// A thread writes 4 consecutive positions (16-byte hi and lo stores; Ksp is
+// a multiple of 32) and divides once per 4: Q < 2^31, so 32-bit division.
 __global__ void dy_rows_split(const float* __restrict__ dy, float* __restrict__ hi, float* __restrict__ lo,
                               long long Q, long long Ks, int Ksp, int S_slices, const Geo g) {
-  const int np = g.NP();
+  const unsigned np = (unsigned)g.NP();
   const long long rows = (long long)S_slices * g.O;
   for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
     const int s = (int)(r / g.O);
     const int o = (int)(r - (long long)s * g.O);
-    float* hr = hi + r * Ksp;
-    float* lr = lo + r * Ksp;
-    for (int j = threadIdx.x; j < Ksp; j += blockDim.x) {
-      const long long q = (long long)s * Ks + j;
-      float v = 0.0f;
-      if (j < Ks && q < Q) {
-        const long long b = q / np;
-        const int p = (int)(q - b * np);
-        v = __ldg(dy + (b * g.O + o) * (long long)np + p);
+    float4* hr = reinterpret_cast<float4*>(hi + r * Ksp);
+    float4* lr = reinterpret_cast<float4*>(lo + r * Ksp);
+    const long long qs = (long long)s * Ks;
+    for (int j4 = threadIdx.x; j4 < Ksp / 4; j4 += blockDim.x) {
+      const int j0 = 4 * j4;
+      const unsigned q0 = (unsigned)(qs + j0);
+      unsigned b = q0 / np, p = q0 - b * np;
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const long long q = qs + j0 + e;
+        v[e] = (j0 + e < Ks && q < Q) ? __ldg(dy + ((long long)b * g.O + o) * (long long)np + p) : 0.0f;
+        if (++p == np) {
+          p = 0;
+          ++b;
+        }
       }
-      float h, l;
-      jxd::split_tf32(v, h, l);
-      hr[j] = h;
-      lr[j] = l;
+      float4 h, l;
+      jxd::split_tf32(v[0], h.x, l.x);
+      jxd::split_tf32(v[1], h.y, l.y);
+      jxd::split_tf32(v[2], h.z, l.z);
+      jxd::split_tf32(v[3], h.w, l.w);
+      hr[j4] = h;
+      lr[j4] = l;
     }
   }
 }
@@ -1348,6 +1360,7 @@ int jx_conv2d_bwd_filter_f32(const float* x, const float* dy, float* dw, int64_t
     return JX_OK;
   }
   JX_REQUIRE(x && dy, "conv2d: NULL pointer");
+  JX_REQUIRE(B * NP < (1LL << 31), "conv2d: weight gradient over 2^31 or more output pixels");
   if (implicit_fits(g, (K + 255) / 256 * 256, std::max(K, B * NP), C * H * W))
     return conv_bwd_filter_implicit(x, dy, dw, B, g, st);
   const long long Q = B * NP;  // contraction length: every image's every output pixel
