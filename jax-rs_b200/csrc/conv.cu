@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 constexpr int CP_STAGES = 3;
 // k-blocks whose gathers are in flight ahead of the one being written
 // (forward at [64,256,56,56]: 1.149 / 0.973 / 1.022 ms with 1 / 2 / 3 ahead;
-// from 3 ahead the gathering warps spill)
+// with 2 ahead the gathering warps spill a few dozen bytes, with 3 more)
 constexpr int CP_AHEAD = 2;
 constexpr int CP_STAGE = 4 * PAIR_OP;  // [A hi][A lo][B hi][B lo], 16 KB each
 constexpr size_t CP_SMEM = (size_t)CP_STAGES * CP_STAGE + BAR_BYTES + TABLE_MAX * 8 + 1024 /*align*/;
