@@ -165,6 +165,25 @@ def test_layer_argument_checks(jx):
     jx.call("jx_pool2d_f32", None, None, 0, 3, 4, 4, 2, 2, 2, 2, 0, 0, jx.POOL_AVG, None)
 
 
+def test_conv2d_argument_checks(jx):
+    """conv2d rejects bad geometry with the reference's assert messages
+    (src/nn.rs:2062-2067), and the kernel choice and the weight gradient's
+    size limit are checked, all before any device work."""
+    with pytest.raises(jx.JaxRsError, match="Kernel height too large"):
+        jx.call("jx_conv2d_fwd_f32", 1, 1, 1, 1, 3, 4, 4, 8, 7, 7, 1, 0, None)
+    with pytest.raises(jx.JaxRsError, match="Stride must be positive"):
+        jx.call("jx_conv2d_bwd_data_f32", 1, 1, 1, 1, 3, 4, 4, 8, 3, 3, 0, 0, None)
+    with pytest.raises(jx.JaxRsError, match="2\\^31"):
+        jx.call("jx_conv2d_bwd_filter_f32", 1, 1, 1, 1 << 20, 1, 64, 64, 1, 1, 1, 1, 0, None)
+    with pytest.raises(jx.JaxRsError) as e:
+        jx.call("jx_conv_set_kernel", 3)
+    assert e.value.status == jx.JX_EINVAL
+    for which in (jx.CONV_ONE_CTA, jx.CONV_PAIR, jx.CONV_AUTO):
+        jx.call("jx_conv_set_kernel", which)
+    # empty batches are no-ops
+    jx.call("jx_conv2d_fwd_f32", None, None, None, 0, 3, 8, 8, 4, 3, 3, 1, 1, None)
+
+
 def test_rust_ffi_block_matches_header():
     """INTEGRATION.md's Rust extern block is the generator's output for the
     current header, and it declares every JX_API function exactly once."""
