@@ -270,7 +270,8 @@ __global__ void fft_tiny_kernel(const float2* __restrict__ in, float2* __restric
   cf2 u[R > 1 ? R : 1];
   for (int i = 0; i < R; ++i) {
     const float2 x = in[base + i * es];
-    u[i] = {x.x, x.y};
+    u[i].x = x.x;
+    u[i].y = x.y;
   }
   if constexpr (R > 1) dft_r<R, INV>(u);
   for (int i = 0; i < R; ++i) out[ob + i * es] = make_float2(u[i].x * scale, u[i].y * scale);
