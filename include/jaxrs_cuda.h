@@ -381,8 +381,8 @@ JX_API int jx_conv2d_bwd_filter_f32(const float *x, const float *dy, float *dw, 
                              jx_stream_t stream);
 /* Kernel of the implicit convolutions above (no reference counterpart; for
  * tests and tuning), process-wide.  JX_CONV_AUTO: the SM-pair kernel
- * (tcgen05 cta_group::2, 256x256 tiles) when the pass has at least one tile
- * per SM pair, else the one-CTA kernel (128x256 tiles).  The two compute the
+ * (tcgen05 cta_group::2, 256x256 tiles) when the pass's tiles fill at least
+ * 90% of the SM pairs, else the one-CTA kernel (128x256 tiles).  The two compute the
  * same sums in the same order.  Shapes beyond the implicit kernels (more
  * than 4096 gathered indices or 32 filter taps) take the explicit path
  * whatever the setting.  Returns JX_EINVAL for another value. */

@@ -1010,12 +1010,15 @@ int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, cons
 std::atomic<int> g_conv_kernel{JX_CONV_AUTO};
 std::mutex g_conv_pair_mu;
 
-// Whether a pass with `pair_tiles` 256 x 256 tiles runs on conv_pair_kernel.
+// Whether a pass with `pair_tiles` 256 x 256 tiles runs on conv_pair_kernel:
+// by default once they fill at least 90% of the SM pairs (below that the
+// one-CTA kernel's 128 x 256 tiles spread over more SMs; at 72 tiles on 74
+// pairs, the weight gradient of 8 images sliced 8 ways, both fill 97%).
 bool conv_use_pair(long long pair_tiles) {
   const int k = g_conv_kernel.load();
   if (k == JX_CONV_ONE_CTA) return false;
   if (k == JX_CONV_PAIR) return true;
-  return pair_tiles >= jx::num_sms() / 2;
+  return 10 * pair_tiles >= 9 * (long long)(jx::num_sms() / 2);
 }
 
 // Per device and mode, once: the shared-memory limit, the register count the

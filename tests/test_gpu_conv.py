@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 def kernel(jx, request):
     """Runs the test on each implicit kernel (one-CTA 128x256 tiles, SM-pair
     256x256 tiles); the automatic choice takes the pair kernel only once a
-    pass has a tile per SM pair, which these shapes mostly do not."""
+    pass's tiles fill 90% of the SM pairs, which these shapes mostly do not."""
     jx.call("jx_conv_set_kernel", jx.CONV_ONE_CTA if request.param == "one_cta" else jx.CONV_PAIR)
     yield request.param
     jx.call("jx_conv_set_kernel", jx.CONV_AUTO)
