@@ -975,6 +975,29 @@ bool implicit_fits(const Geo& g, long long table_entries, long long n_cols, long
   return table_entries <= TABLE_MAX && g.KH * g.KW <= 32 && n_cols < (1LL << 31) && img_elems < (1LL << 31);
 }
 
+std::atomic<int> g_conv_kernel{JX_CONV_AUTO};  // jx_conv_set_kernel
+std::mutex g_conv_mu;                            // per-device kernel preparation
+
+// Per device and mode, once: conv_gemm_kernel's shared-memory limit and the
+// register count it was built with.  Two host threads making their first
+// call on a device serialise on the mutex.
+template <bool COLS>
+int conv_gemm_prepare(int* regs_out) {
+  static int regs[64];
+  int dev = 0;
+  JX_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_conv_mu);
+  if (!regs[dev & 63]) {
+    cudaFuncAttributes fa;
+    JX_CUDA(cudaFuncGetAttributes(&fa, conv_gemm_kernel<COLS>));
+    JX_CUDA(cudaFuncSetAttribute(conv_gemm_kernel<COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)IMPLICIT_SMEM));
+    regs[dev & 63] = fa.numRegs;
+  }
+  *regs_out = regs[dev & 63];
+  return JX_OK;
+}
+
 template <bool COLS>
 int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, const float* src, const uint2* tab,
                      const ImplicitArgs& a, float* out, cudaStream_t st) {
@@ -982,21 +1005,13 @@ int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, cons
   int rc = jx::gemm_make_kmajor_map(&mAh, Ah, Kp, a.M, a_batch, BM);
   if (!rc) rc = jx::gemm_make_kmajor_map(&mAl, Al, Kp, a.M, a_batch, BM);
   if (rc) return rc;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  JX_CUDA(cudaGetDevice(&dev));
-  if (!attr_set[dev & 63]) {
-    JX_CUDA(cudaFuncSetAttribute(conv_gemm_kernel<COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)IMPLICIT_SMEM));
-    attr_set[dev & 63] = true;
-  }
+  int regs = 0;
+  if ((rc = conv_gemm_prepare<COLS>(&regs))) return rc;
   // The register split inside the kernel assumes exactly CONV_LAUNCH_REGS per
   // thread at launch; with any other allocation setmaxnreg.inc could wait for
   // registers that never come, so refuse to launch.
-  cudaFuncAttributes fa;
-  JX_CUDA(cudaFuncGetAttributes(&fa, conv_gemm_kernel<COLS>));
-  if (fa.numRegs != CONV_LAUNCH_REGS)
-    return jx::fail(JX_EUNSUPPORTED, "conv_gemm_kernel built with %d registers per thread, expected %d", fa.numRegs,
+  if (regs != CONV_LAUNCH_REGS)
+    return jx::fail(JX_EUNSUPPORTED, "conv_gemm_kernel built with %d registers per thread, expected %d", regs,
                     CONV_LAUNCH_REGS);
   const int grid = std::min(a.num_tiles, jx::num_sms());
   conv_gemm_kernel<COLS><<<grid, CONV_THREADS, IMPLICIT_SMEM, st>>>(mAh, mAl, src, tab, a, out,
@@ -1007,8 +1022,6 @@ int launch_conv_gemm(const float* Ah, const float* Al, int a_batch, int Kp, cons
 
 // ---- SM-pair launcher --------------------------------------------------------
 
-std::atomic<int> g_conv_kernel{JX_CONV_AUTO};
-std::mutex g_conv_pair_mu;
 
 // Whether a pass with `pair_tiles` 256 x 256 tiles runs on conv_pair_kernel:
 // by default once they fill at least 90% of the SM pairs (below that the
@@ -1028,7 +1041,7 @@ int conv_pair_prepare(int* regs_out, int* max_pairs_out) {
   static int regs[64], max_pairs[64];
   int dev = 0;
   JX_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lk(g_conv_pair_mu);
+  std::lock_guard<std::mutex> lk(g_conv_mu);
   if (!regs[dev & 63]) {
     auto k = conv_pair_kernel<COLS>;
     cudaFuncAttributes fa;
