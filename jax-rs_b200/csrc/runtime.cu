@@ -49,7 +49,7 @@ cudaStream_t as_stream(jx_stream_t s) { return reinterpret_cast<cudaStream_t>(s)
 
 static const int kMaxDev = 64;
 static std::mutex g_mu;
-static int g_sms[kMaxDev];
+static std::atomic<int> g_sms[kMaxDev];  // SM count per device, 0 until first asked
 static unsigned int* g_err_word[kMaxDev];
 
 static int cur_dev() {
@@ -61,12 +61,13 @@ static int cur_dev() {
 int num_sms() {
   int d = cur_dev();
   if (d < 0 || d >= kMaxDev) return 148;
-  if (g_sms[d] == 0) {
-    int n = 0;
+  int n = g_sms[d].load(std::memory_order_relaxed);
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-    g_sms[d] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    g_sms[d].store(n, std::memory_order_relaxed);  // every thread that races here stores the same value
   }
-  return g_sms[d];
+  return n;
 }
 
 // Allocation-failure injection (jx_selftest_fail_alloc): the next N device
