@@ -1195,20 +1195,24 @@ int conv_bwd_data_implicit(const float* dy, const float* w, float* dx, long long
   return rc ? rc : rc2;
 }
 
-// Slices of the weight-gradient contraction: the count in [1, 64] (each slice
-// at least 1024 long) whose tile count fills the last wave of `units`
-// resident tiles (SMs, or SM pairs) best.
+// Slices of the weight-gradient contraction: the count in [1, 64] (each
+// slice at least 1024 long) that minimises the estimated time
+// waves x (k-blocks per tile + DW_TILE_COST), where `units` tiles run at once
+// (SMs, or SM pairs) and DW_TILE_COST is a tile's fixed cost (pipeline fill,
+// last span drain, partial store) in k-block times.  At [64,256,56,56] x
+// [256,256,3,3] on SM pairs this takes 8 slices (72 tiles, one wave of 784
+// k-blocks) over the 41 that fill the waves best (369 tiles, 5 waves of 153):
+// whole conv step 237.2 against 234.1 TFLOP/s; 16 slices gave 235.8.
+constexpr long long DW_TILE_COST = 13;
 long long dw_slices(long long tiles, long long Q, long long units) {
-  const long long sms = units;
-  long long best = 1;
-  double best_eff = -1.0;
+  long long best = 1, best_cost = -1;
   for (long long S = 1; S <= 64; ++S) {
     if (S > 1 && Q / S < 1024) break;
-    const long long total = tiles * S;
-    const long long waves = (total + sms - 1) / sms;
-    const double eff = (double)total / (double)(waves * sms);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
+    const long long waves = (tiles * S + units - 1) / units;
+    const long long kb = ((Q + S - 1) / S + BK - 1) / BK;
+    const long long cost = waves * (kb + DW_TILE_COST);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
       best = S;
     }
   }
