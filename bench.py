@@ -96,7 +96,7 @@ TRAFFIC = {
     "fullsum": 1.0738e9 + 0.0049e9,          # reduce_all_pass1<sum>
     "fft1d": 4 * (0.5369e9 + 0.4847e9),      # fft_kernel<12>, batch 16384 x 4
     "fft2d": 8 * (0.2685e9 + 0.2158e9),      # column pass fft1024_tma_kernel, batch 32 x 8
-    "conv": 4 * (0.0564e9 + 0.0084e9 + 0.0563e9 + 0.0070e9 + 0.1571e9 + 0.0620e9),  # 3 conv_pair_kernel, B 16 x 4
+    "conv": 4 * (0.0563e9 + 0.0067e9 + 0.0563e9 + 0.0032e9 + 0.1549e9 + 0.0006e9),  # 3 conv_pair_kernel, B 16 x 4
     "bgemm": 3.4474e9 + 1.0573e9,            # gemm_pair_kernel<0,1>, [64,2048,2048]^2
     "pool": 0.8228e9 + 0.1918e9,             # pool2d_kernel<max,3,3>, [64,256,112,112]
     "batchnorm": (0.2055e9 + 0.0036e9) + 0.0005e9 + (0.2056e9 + 0.1571e9),  # stats + finalize + apply
