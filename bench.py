@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--global-batch", type=int, default=65536, help="wide MLP global batch")
     p.add_argument("--fft-batch", type=int, default=0, help="override the FFT batch (smaller cases for profiling)")
     p.add_argument("--conv-batch", type=int, default=0, help="override the conv batch (smaller cases for profiling)")
+    p.add_argument("--conv-kernel", default="auto", choices=["auto", "one_cta", "pair"],
+                   help="implicit conv kernel (jx_conv_set_kernel); auto picks the SM-pair kernel at the default size")
     p.add_argument("--size", type=int, default=8192, help="GEMM M=N=K per rank (with --strong: of the whole product)")
     p.add_argument("--gemm-prec", default="3xtf32", choices=["3xtf32", "pair"],
                    help="sgemm/bgemm: JX_PREC_3XTF32 (the dispatcher's choice) or JX_PREC_3XTF32_PAIR (SM-pair "
@@ -768,6 +770,7 @@ def run_conv_bgemm(args, dist, jx, torch):
     g = torch.Generator(device=dev)
     g.manual_seed(3 + dist.rank)
     if args.workload == "conv":
+        jx.call("jx_conv_set_kernel", {"auto": jx.CONV_AUTO, "one_cta": jx.CONV_ONE_CTA, "pair": jx.CONV_PAIR}[args.conv_kernel])
         Bg = args.conv_batch or 64  # global batch, split over the ranks
         B, C, H, W, O, K = shard(Bg, dist, "conv batch"), 256, 56, 56, 256, 3
         geo = (B, C, H, W, O, K, K, 1, 1)
@@ -830,8 +833,9 @@ def run_conv_bgemm(args, dist, jx, torch):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": wl, "parallelism": f"global batch split over {dist.world} rank(s), no collective"},
             "roofline": {"bound": "tensor",
-                         "kernel": ("conv_pair_kernel x3 (implicit GEMM on SM pairs; whole step incl. filter/dY "
-                                    "splits)"
+                         "kernel": (("conv_gemm_kernel x3 (implicit GEMM, one CTA" if args.conv_kernel == "one_cta"
+                                     else "conv_pair_kernel x3 (implicit GEMM on SM pairs")
+                                    + "; whole step incl. filter/dY splits)"
                                     if args.workload == "conv" else
                                     ("gemm_pair_kernel" if pair_ok(2048, 2048, 2048, False, False, nb)
                                      else "gemm_fused_split_kernel") + " (whole batched call)"),
